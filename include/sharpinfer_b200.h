@@ -1,0 +1,167 @@
+/*
+ * sharpinfer_b200 -- C ABI of the B200 (sm_100a) K-quant inference library.
+ *
+ * This is the native side of SharpInfer's compute-backend boundary.  The
+ * reference binds a library named `sharpinfer_cuda` from C# with P/Invoke
+ * (src/SharpInfer.Gpu/CudaBackend.cs:139-164,
+ * src/SharpInfer.Core/Layers/FlashAttention.cs:378-385,
+ * src/SharpInfer.Core/Tensors/HardwareBackends.cs:436-443) and calls it
+ * through IComputeBackend (src/SharpInfer.Core/Tensors/TensorOps.cs:241-250).
+ * The f32 entry points of that interface are kept below under their
+ * original names; the quantised, device-resident entry points (si_*) are the
+ * hot path: weights stay in HBM as GGUF K-quant blocks and are dequantised
+ * inside the matvec/GEMM kernels.
+ *
+ * Conventions
+ *  - Every si_* call returns an si_status (0 = SI_OK).  On failure the
+ *    message is available from si_last_error() on the same thread.
+ *  - Pointers named *_dev are device pointers of the context's GPU; pointers
+ *    named *_host are host pointers, read or written before the call returns.
+ *  - A context owns one CUDA stream.  Device-pointer calls are asynchronous
+ *    on that stream; host-pointer calls synchronise before returning.  Calls
+ *    on one context are not thread-safe; use one context per thread.
+ *  - There is no CPU fallback: without a usable GPU, calls fail with
+ *    SI_ERR_CUDA.
+ */
+#ifndef SHARPINFER_B200_H
+#define SHARPINFER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define SI_EXPORT __declspec(dllexport)
+#else
+#define SI_EXPORT __attribute__((visibility("default")))
+#endif
+
+/* Status codes. */
+typedef enum {
+  SI_OK = 0,
+  SI_ERR_INVALID = 1,     /* bad argument (null pointer, shape, type) */
+  SI_ERR_CUDA = 2,        /* CUDA runtime error or no usable device */
+  SI_ERR_OOM = 3,         /* device allocation failed */
+  SI_ERR_UNSUPPORTED = 4, /* valid request this build does not implement */
+  SI_ERR_NCCL = 5,        /* collective failure */
+  SI_ERR_TIMEOUT = 6      /* a bounded device or host wait gave up */
+} si_status;
+
+/* GGML quantisation type ids, the values of SharpInfer's QuantType enum
+ * (src/SharpInfer.Core/Tensors/Quantization.cs:6-22). */
+typedef enum {
+  SI_F32 = 0,
+  SI_F16 = 1,
+  SI_Q8_0 = 8,
+  SI_Q4_K = 12,
+  SI_Q6_K = 14
+} si_qtype;
+
+/* Synthetic-data recipes for si_synth_* (benchmarks and tests). */
+typedef enum {
+  SI_SYNTH_PLAIN = 0, /* Q4_K: d,dmin=f16(|N|*sigma), 6-bit sc/m uniform 0..63 */
+  SI_SYNTH_MODEL = 1  /* Q4_K: zero-mean weights, sc 1..8, m=round(7.5 sc), dmin=d */
+} si_synth_recipe;
+
+typedef struct si_ctx si_ctx;
+typedef struct si_weight si_weight;
+
+/* ---------------------------------------------------------------- lifecycle */
+
+/* Library ABI version (major*10000 + minor*100 + patch). */
+SI_EXPORT int si_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+SI_EXPORT const char* si_last_error(void);
+
+/* Bind a context to `device` and create its stream.  Replaces cuda_init
+ * (src/SharpInfer.Gpu/Kernels/kernels.cu:30-37), which returned a null
+ * handle on failure; here the reason is kept in si_last_error(). */
+SI_EXPORT int si_init(int device, si_ctx** out);
+
+/* Release the context's stream and scratch memory (cuda_cleanup, kernels.cu:39-43). */
+SI_EXPORT int si_shutdown(si_ctx* ctx);
+
+/* Device name into buf (NUL-terminated, truncated to len). */
+SI_EXPORT int si_device_name(si_ctx* ctx, char* buf, int len);
+
+/* The context's cudaStream_t, for callers that enqueue their own work. */
+SI_EXPORT int si_stream(si_ctx* ctx, void** stream_out);
+
+/* Wait for all work queued on the context's stream. */
+SI_EXPORT int si_synchronize(si_ctx* ctx);
+
+/* ------------------------------------------------------------------ weights */
+
+/* Copy a row-major [rows][cols] tensor of raw GGUF blocks (cols/256 Q4_K or
+ * Q6_K blocks, or cols/32 Q8_0 blocks per row) from host memory into a
+ * device-resident weight.  The caller keeps ownership of `blocks_host`.
+ * The bytes are what SharpInfer's loader hands to Dequantize.DequantizeTensor
+ * (Quantization.cs:415-469); they are re-ordered on the device into the
+ * kernel layout (same byte count) and never expanded to f32.  cols must be a
+ * multiple of the block size. */
+SI_EXPORT int si_weight_upload(si_ctx* ctx, int qtype, const void* blocks_host, int64_t rows,
+                               int64_t cols, si_weight** out);
+
+/* Generate a seeded synthetic weight directly on the device (benchmarks,
+ * tests).  Bytes equal si_synth_blocks_host() for the same arguments. */
+SI_EXPORT int si_weight_synth(si_ctx* ctx, int qtype, int64_t rows, int64_t cols, uint64_t seed,
+                              uint64_t tag, int recipe, float sigma, si_weight** out);
+
+SI_EXPORT int si_weight_free(si_weight* w);
+
+/* Shape, type and device bytes of a weight (any out pointer may be NULL). */
+SI_EXPORT int si_weight_info(const si_weight* w, int* qtype, int64_t* rows, int64_t* cols,
+                             int64_t* device_bytes);
+
+/* ---------------------------------------------------------------- host data */
+
+/* Host-side generator of the same seeded blocks as si_weight_synth: fills
+ * rows*cols/blocksize GGUF blocks into out_host (row-major). */
+SI_EXPORT int si_synth_blocks_host(int qtype, int64_t rows, int64_t cols, uint64_t seed,
+                                   uint64_t tag, int recipe, float sigma, void* out_host);
+
+/* n f32 values mean + sigma*N(0,1) (seeded), host. */
+SI_EXPORT int si_synth_f32_host(int64_t n, uint64_t seed, uint64_t tag, float mean, float sigma,
+                                float* out_host);
+
+/* n f16 values f16(sigma*N(0,1)) (seeded), host. */
+SI_EXPORT int si_synth_f16_host(int64_t n, uint64_t seed, uint64_t tag, float sigma,
+                                uint16_t* out_host);
+
+/* -------------------------------------------------------------------- ops */
+
+/* Dequantise a weight to f32 [rows][cols] in device memory, bit-exact with
+ * Dequantize.DequantQ4_K / DequantQ6_K / DequantQ8_0
+ * (Quantization.cs:273-314, 362-391, 106-114). */
+SI_EXPORT int si_dequant(si_ctx* ctx, const si_weight* w, float* out_dev);
+
+/* y[b][r] = sum_c W[r][c] * x[b][c] for b < batch (1..16), x [batch][cols]
+ * f32, y [batch][rows] f32, both device pointers.  The quantised
+ * counterpart of IComputeBackend.MatVecMul (TensorOps.cs:243, :63-72):
+ * W is read once per call as K-quant blocks. */
+SI_EXPORT int si_qmatvec(si_ctx* ctx, const si_weight* w, const float* x_dev, float* y_dev,
+                         int batch);
+
+/* Two-phase form of si_qmatvec for several weights that share an input:
+ * si_act_prepare converts x [batch][cols] (device) once into the context's
+ * activation staging (f16 hi/lo fragments, per-vector scale, Q4_K sub-block
+ * sums); si_qmatvec_prepared then multiplies any weight with that many
+ * columns.  accumulate != 0 adds into y instead of storing (residual add). */
+SI_EXPORT int si_act_prepare(si_ctx* ctx, const float* x_dev, int64_t cols, int batch);
+SI_EXPORT int si_qmatvec_prepared(si_ctx* ctx, const si_weight* w, float* y_dev, int batch,
+                                  int accumulate);
+
+/* Same with host buffers (copied in, computed, copied out, synchronised),
+ * the calling convention of cuda_mat_vec_mul (kernels.cu:67-87). */
+SI_EXPORT int si_qmatvec_host(si_ctx* ctx, const si_weight* w, const float* x_host,
+                              float* y_host, int batch);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SHARPINFER_B200_H */

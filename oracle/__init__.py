@@ -1,0 +1,175 @@
+"""ctypes wrapper of the CPU oracle (oracle.cpp) -- TEST INFRASTRUCTURE ONLY.
+
+Imported by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg,
+and only as the checker or the timed CPU baseline; the sharpinfer_b200 package
+never imports it.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "_build", "liboracle.so")
+
+_c_p = ctypes.c_void_p
+_i32, _i64, _f32, _u16 = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_uint16
+_SIGS = {
+    "or_half_to_float": (_f32, [_u16]),
+    "or_block_size": (_i32, [_i32]),
+    "or_block_bytes": (_i32, [_i32]),
+    "or_dequant_tensor": (_i32, [_i32, _c_p, _i64, _c_p]),
+    "or_dot": (_f32, [_c_p, _c_p, _i32]),
+    "or_matvec_f32": (None, [_c_p, _c_p, _c_p, _i64, _i32, _i32]),
+    "or_qmatvec": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p, _i32, _i32]),
+    "or_matmul": (None, [_c_p, _c_p, _c_p, _i32, _i32, _i32]),
+    "or_softmax": (None, [_c_p, _i32]),
+    "or_rmsnorm": (None, [_c_p, _c_p, _c_p, _i32, _f32]),
+    "or_add_inplace": (None, [_c_p, _c_p, _i32]),
+    "or_mul_inplace": (None, [_c_p, _c_p, _i32]),
+    "or_silu": (None, [_c_p, _i32]),
+    "or_add_scaled": (None, [_c_p, _c_p, _f32, _i32]),
+    "or_argmax": (_i32, [_c_p, _i64]),
+    "or_rope_apply": (None, [_c_p, _c_p, _i32, _i32, _i32, _i32, _f32]),
+    "or_rope_table": (None, [_c_p, _i32, _i32, _f32]),
+    "or_attention_decode": (None, [_c_p, _c_p, _c_p, _i32, _i32, _i32, _i32, _c_p, _i32]),
+    "or_flash_attention": (None, [_c_p, _c_p, _c_p, _c_p, _i32, _i32, _i32, _f32, _i32, _i32]),
+    "or_model_create": (_c_p, [_i32] * 8 + [_f32, _f32, _i32, _i32]),
+    "or_model_free": (None, [_c_p]),
+    "or_model_set": (None, [_c_p, _i32, _i32, _i32, _c_p]),
+    "or_model_kv_fill": (None, [_c_p, _i32, _i32, _c_p, _c_p, _i32]),
+    "or_model_forward": (_i32, [_c_p, _i32, _i32, _i32, _i32, _c_p]),
+    "or_round_f16": (_f32, [_f32]),
+    "or_num_threads": (_i32, []),
+}
+
+_lib = None
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def load():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(os.path.join(HERE, "oracle.cpp")):
+            build()
+        lib = ctypes.CDLL(LIB)
+        for n, (r, a) in _SIGS.items():
+            f = getattr(lib, n)
+            f.restype, f.argtypes = r, a
+        _lib = lib
+    return _lib
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def nthreads():
+    return os.cpu_count() or 1
+
+
+def dequant(qtype, blocks, n):
+    out = np.empty(n, dtype=np.float32)
+    rc = load().or_dequant_tensor(qtype, _p(np.ascontiguousarray(blocks, np.uint8)), n, _p(out))
+    if rc:
+        raise ValueError("oracle: unsupported type %d" % qtype)
+    return out
+
+
+def dot(a, b):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    return load().or_dot(_p(a), _p(b), a.size)
+
+
+def qmatvec(qtype, blocks, rows, cols, x, threads=None):
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, cols)
+    y = np.empty((x.shape[0], rows), np.float32)
+    rc = load().or_qmatvec(qtype, _p(np.ascontiguousarray(blocks, np.uint8)), rows, cols, _p(x), _p(y),
+                           x.shape[0], threads or nthreads())
+    if rc:
+        raise ValueError("oracle qmatvec failed")
+    return y
+
+
+def matvec_f32(W, x, threads=None):
+    W = np.ascontiguousarray(W, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty(W.shape[0], np.float32)
+    load().or_matvec_f32(_p(W), _p(x), _p(y), W.shape[0], W.shape[1], threads or nthreads())
+    return y
+
+
+def rmsnorm(x, w, eps):
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    load().or_rmsnorm(_p(out), _p(x), _p(np.ascontiguousarray(w, np.float32)), x.size, eps)
+    return out
+
+
+def softmax(x):
+    x = np.array(x, np.float32)
+    load().or_softmax(_p(x), x.size)
+    return x
+
+
+def silu(x):
+    x = np.array(x, np.float32)
+    load().or_silu(_p(x), x.size)
+    return x
+
+
+def argmax(x):
+    x = np.ascontiguousarray(x, np.float32)
+    return load().or_argmax(_p(x), x.size)
+
+
+def rope_apply(q, k, pos, hd, theta):
+    q = np.array(q, np.float32)
+    k = np.array(k, np.float32)
+    load().or_rope_apply(_p(q), _p(k), pos, hd, q.size // hd, k.size // hd, theta)
+    return q, k
+
+
+def rope_table(npos, hd, theta):
+    t = np.empty(npos * hd, np.float32)
+    load().or_rope_table(_p(t), npos, hd, theta)
+    return t
+
+
+def attention_decode(q, K, V, nh, nkv, hd, threads=None):
+    q = np.ascontiguousarray(q, np.float32)
+    K = np.ascontiguousarray(K, np.float32)
+    V = np.ascontiguousarray(V, np.float32)
+    kv_len = K.size // (nkv * hd)
+    out = np.empty(nh * hd, np.float32)
+    load().or_attention_decode(_p(q), _p(K), _p(V), kv_len, nh, nkv, hd, _p(out), threads or nthreads())
+    return out
+
+
+def flash_attention(Q, K, V, scale, causal, start_pos=0):
+    Q = np.ascontiguousarray(Q, np.float32)
+    K = np.ascontiguousarray(K, np.float32)
+    V = np.ascontiguousarray(V, np.float32)
+    seq, hd = Q.shape
+    out = np.empty_like(Q)
+    load().or_flash_attention(_p(Q), _p(K), _p(V), _p(out), seq, K.shape[0], hd, scale, int(causal), start_pos)
+    return out
+
+
+def matmul(a, b):
+    a = np.ascontiguousarray(a, np.float32)
+    b = np.ascontiguousarray(b, np.float32)
+    M, K = a.shape
+    N = b.shape[1]
+    c = np.empty((M, N), np.float32)
+    load().or_matmul(_p(a), _p(b), _p(c), M, K, N)
+    return c
+
+
+def round_f16(x):
+    return load().or_round_f16(x)

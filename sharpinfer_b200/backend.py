@@ -1,0 +1,169 @@
+"""Host-side mirror of SharpInfer's compute-backend interface over the C ABI.
+
+SharpInfer injects an IComputeBackend (src/SharpInfer.Core/Tensors/
+TensorOps.cs:241-250) whose MatVecMul takes dequantised f32 spans.  The B200
+path keeps the weights quantised and device-resident, so its entry points take
+a QuantWeight handle instead of an f32 matrix.  Device tensors are torch CUDA
+tensors (plumbing for memory and streams); all arithmetic runs in
+libsharpinfer_b200.so.
+"""
+import ctypes
+
+import numpy as np
+
+from . import native as N
+
+
+def _torch():
+    import torch
+    return torch
+
+
+class QuantWeight:
+    """A device-resident GGUF-quantised [rows][cols] weight (si_weight*)."""
+
+    def __init__(self, ctx, handle, qtype, rows, cols):
+        self.ctx, self.handle, self.qtype, self.rows, self.cols = ctx, handle, qtype, rows, cols
+
+    @property
+    def device_bytes(self):
+        b = ctypes.c_int64()
+        N.call("si_weight_info", self.handle, None, None, None, ctypes.byref(b))
+        return b.value
+
+    @property
+    def gguf_bytes(self):
+        return self.rows * (self.cols // N.BLOCK_ELEMS[self.qtype]) * N.BLOCK_BYTES[self.qtype]
+
+    def free(self):
+        if self.handle:
+            N.call("si_weight_free", self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class B200Context:
+    """One GPU and one CUDA stream (si_ctx*)."""
+
+    def __init__(self, device=0):
+        N.load()
+        h = ctypes.c_void_p()
+        N.call("si_init", int(device), ctypes.byref(h))
+        self.handle = h
+        self.device = device
+        s = ctypes.c_void_p()
+        N.call("si_stream", self.handle, ctypes.byref(s))
+        self.stream_ptr = s.value
+        self._torch_stream = None
+
+    @property
+    def name(self):
+        buf = ctypes.create_string_buffer(256)
+        N.call("si_device_name", self.handle, buf, 256)
+        return buf.value.decode()
+
+    @property
+    def torch_stream(self):
+        """The context's stream as a torch stream (for allocations and events)."""
+        if self._torch_stream is None:
+            torch = _torch()
+            self._torch_stream = torch.cuda.ExternalStream(self.stream_ptr, device=self.device)
+        return self._torch_stream
+
+    def synchronize(self):
+        N.call("si_synchronize", self.handle)
+
+    def close(self):
+        if self.handle:
+            N.call("si_shutdown", self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- weights -----------------------------------------------------------------
+    def upload(self, qtype, blocks, rows, cols):
+        blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        want = rows * (cols // N.BLOCK_ELEMS[qtype]) * N.BLOCK_BYTES[qtype]
+        if blocks.nbytes != want:
+            raise ValueError("expected %d bytes of blocks, got %d" % (want, blocks.nbytes))
+        h = ctypes.c_void_p()
+        N.call("si_weight_upload", self.handle, qtype, N.ptr(blocks), rows, cols, ctypes.byref(h))
+        return QuantWeight(self, h, qtype, rows, cols)
+
+    def synth_weight(self, qtype, rows, cols, seed, tag, recipe=N.SYNTH_PLAIN, sigma=0.01):
+        h = ctypes.c_void_p()
+        N.call("si_weight_synth", self.handle, qtype, rows, cols, seed, tag, recipe, sigma,
+               ctypes.byref(h))
+        return QuantWeight(self, h, qtype, rows, cols)
+
+    # ---- ops (device tensors, asynchronous on the context stream) ----------------
+    def dequant(self, w, out=None):
+        torch = _torch()
+        with torch.cuda.stream(self.torch_stream):
+            if out is None:
+                out = torch.empty((w.rows, w.cols), dtype=torch.float32, device="cuda:%d" % self.device)
+            N.call("si_dequant", self.handle, w.handle, N.ptr(out))
+        return out
+
+    def qmatvec(self, w, x, out=None):
+        """y[b] = W x[b]; x is a [batch, cols] (or [cols]) f32 CUDA tensor."""
+        torch = _torch()
+        x2 = x.reshape(-1, w.cols)
+        batch = x2.shape[0]
+        with torch.cuda.stream(self.torch_stream):
+            if out is None:
+                out = torch.empty((batch, w.rows), dtype=torch.float32, device=x.device)
+            N.call("si_qmatvec", self.handle, w.handle, N.ptr(x2), N.ptr(out), batch)
+        return out
+
+    def act_prepare(self, x):
+        """Prepare x [batch, cols] once for several qmatvec_prepared calls."""
+        torch = _torch()
+        x2 = x.reshape(x.shape[0] if x.dim() > 1 else 1, -1)
+        with torch.cuda.stream(self.torch_stream):
+            N.call("si_act_prepare", self.handle, N.ptr(x2), x2.shape[1], x2.shape[0])
+        return x2.shape[0]
+
+    def qmatvec_prepared(self, w, batch, out=None, accumulate=False):
+        torch = _torch()
+        with torch.cuda.stream(self.torch_stream):
+            if out is None:
+                out = torch.empty((batch, w.rows), dtype=torch.float32, device="cuda:%d" % self.device)
+            N.call("si_qmatvec_prepared", self.handle, w.handle, N.ptr(out), batch, int(accumulate))
+        return out
+
+    def qmatvec_host(self, w, x):
+        """Same with host numpy arrays; synchronous (the cuda_mat_vec_mul convention)."""
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, w.cols)
+        y = np.empty((x.shape[0], w.rows), dtype=np.float32)
+        N.call("si_qmatvec_host", self.handle, w.handle, N.ptr(x), N.ptr(y), x.shape[0])
+        return y
+
+
+# ---- seeded synthetic host data (same bytes as the device generator) -------------
+def synth_blocks_host(qtype, rows, cols, seed, tag, recipe=N.SYNTH_PLAIN, sigma=0.01):
+    nb = rows * (cols // N.BLOCK_ELEMS.get(qtype, 256))
+    out = np.empty(max(nb * N.BLOCK_BYTES.get(qtype, 1), 1), dtype=np.uint8)
+    N.call("si_synth_blocks_host", qtype, rows, cols, seed, tag, recipe, sigma, N.ptr(out))
+    return out
+
+
+def synth_f32_host(n, seed, tag, mean=0.0, sigma=1.0):
+    out = np.empty(n, dtype=np.float32)
+    N.call("si_synth_f32_host", n, seed, tag, mean, sigma, N.ptr(out))
+    return out
+
+
+def synth_f16_host(n, seed, tag, sigma=1.0):
+    out = np.empty(n, dtype=np.uint16)
+    N.call("si_synth_f16_host", n, seed, tag, sigma, N.ptr(out))
+    return out

@@ -1,0 +1,105 @@
+"""ctypes binding of libsharpinfer_b200.so (the C ABI in include/sharpinfer_b200.h).
+
+The library is loaded from the package directory; there is no fallback: if it
+is missing or a call fails, an exception is raised.
+"""
+import ctypes
+import os
+import re
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libsharpinfer_b200.so")
+HEADER = os.path.join(os.path.dirname(_HERE), "include", "sharpinfer_b200.h")
+
+SI_OK = 0
+SI_F32, SI_F16, SI_Q8_0, SI_Q4_K, SI_Q6_K = 0, 1, 8, 12, 14
+SYNTH_PLAIN, SYNTH_MODEL = 0, 1
+BLOCK_ELEMS = {SI_Q4_K: 256, SI_Q6_K: 256, SI_Q8_0: 32}
+BLOCK_BYTES = {SI_Q4_K: 144, SI_Q6_K: 210, SI_Q8_0: 34}
+
+_c_p = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+_u64 = ctypes.c_uint64
+_f32 = ctypes.c_float
+
+
+class SIError(RuntimeError):
+    """A sharpinfer_b200 call returned a non-zero si_status."""
+
+    def __init__(self, status, msg):
+        super().__init__("si_status %d: %s" % (status, msg))
+        self.status = status
+
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "si_version": (_i32, []),
+    "si_last_error": (ctypes.c_char_p, []),
+    "si_init": (_i32, [_i32, ctypes.POINTER(_c_p)]),
+    "si_shutdown": (_i32, [_c_p]),
+    "si_device_name": (_i32, [_c_p, ctypes.c_char_p, _i32]),
+    "si_stream": (_i32, [_c_p, ctypes.POINTER(_c_p)]),
+    "si_synchronize": (_i32, [_c_p]),
+    "si_weight_upload": (_i32, [_c_p, _i32, _c_p, _i64, _i64, ctypes.POINTER(_c_p)]),
+    "si_weight_synth": (_i32, [_c_p, _i32, _i64, _i64, _u64, _u64, _i32, _f32, ctypes.POINTER(_c_p)]),
+    "si_weight_free": (_i32, [_c_p]),
+    "si_weight_info": (_i32, [_c_p, ctypes.POINTER(_i32), ctypes.POINTER(_i64), ctypes.POINTER(_i64),
+                              ctypes.POINTER(_i64)]),
+    "si_synth_blocks_host": (_i32, [_i32, _i64, _i64, _u64, _u64, _i32, _f32, _c_p]),
+    "si_synth_f32_host": (_i32, [_i64, _u64, _u64, _f32, _f32, _c_p]),
+    "si_synth_f16_host": (_i32, [_i64, _u64, _u64, _f32, _c_p]),
+    "si_dequant": (_i32, [_c_p, _c_p, _c_p]),
+    "si_qmatvec": (_i32, [_c_p, _c_p, _c_p, _c_p, _i32]),
+    "si_act_prepare": (_i32, [_c_p, _c_p, _i64, _i32]),
+    "si_qmatvec_prepared": (_i32, [_c_p, _c_p, _c_p, _i32, _i32]),
+    "si_qmatvec_host": (_i32, [_c_p, _c_p, _c_p, _c_p, _i32]),
+}
+
+_lib = None
+
+
+def load():
+    """Load the native library (once) and declare the signatures."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            "libsharpinfer_b200.so not built (%s); run `python sharpinfer_b200/build.py`" % LIB_PATH)
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def declared_symbols(header=HEADER):
+    """Names of the functions the public header declares with SI_EXPORT."""
+    text = open(header).read()
+    return re.findall(r"SI_EXPORT\s+[\w\s\*]+?\b(\w+)\s*\(", text)
+
+
+def check(status):
+    if status != SI_OK:
+        raise SIError(status, load().si_last_error().decode(errors="replace"))
+    return status
+
+
+def call(name, *args):
+    return check(getattr(load(), name)(*args))
+
+
+def ptr(x):
+    """Raw pointer of a torch tensor, numpy array, int address or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        return x.ctypes.data
+    raise TypeError("cannot take the address of %r" % type(x))
