@@ -168,6 +168,7 @@ def run_ours(args, world, rank, local):
         yd = torch.empty((1, HIDDEN), device=dev)
     torch.cuda.synchronize()
     stream = ctx.torch_stream
+    torch.cuda.set_stream(stream)  # all torch work on the context stream: no cross-stream waits
     nk = 3 * (args.steps)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * nk)]
 

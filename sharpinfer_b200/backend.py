@@ -78,6 +78,19 @@ class B200Context:
     def synchronize(self):
         N.call("si_synchronize", self.handle)
 
+    def _enter(self):
+        """Order the context stream after work queued on torch's current stream."""
+        torch = _torch()
+        cur = torch.cuda.current_stream(self.device)
+        if cur.cuda_stream != self.stream_ptr:
+            self.torch_stream.wait_stream(cur)
+        return cur
+
+    def _leave(self, cur):
+        """Order torch's current stream after the work just queued on the context stream."""
+        if cur.cuda_stream != self.stream_ptr:
+            cur.wait_stream(self.torch_stream)
+
     def close(self):
         if self.handle:
             N.call("si_shutdown", self.handle)
@@ -108,10 +121,12 @@ class B200Context:
     # ---- ops (device tensors, asynchronous on the context stream) ----------------
     def dequant(self, w, out=None):
         torch = _torch()
+        cur = self._enter()
         with torch.cuda.stream(self.torch_stream):
             if out is None:
                 out = torch.empty((w.rows, w.cols), dtype=torch.float32, device="cuda:%d" % self.device)
             N.call("si_dequant", self.handle, w.handle, N.ptr(out))
+        self._leave(cur)
         return out
 
     def qmatvec(self, w, x, out=None):
@@ -119,26 +134,32 @@ class B200Context:
         torch = _torch()
         x2 = x.reshape(-1, w.cols)
         batch = x2.shape[0]
+        cur = self._enter()
         with torch.cuda.stream(self.torch_stream):
             if out is None:
                 out = torch.empty((batch, w.rows), dtype=torch.float32, device=x.device)
             N.call("si_qmatvec", self.handle, w.handle, N.ptr(x2), N.ptr(out), batch)
+        self._leave(cur)
         return out
 
     def act_prepare(self, x):
         """Prepare x [batch, cols] once for several qmatvec_prepared calls."""
         torch = _torch()
         x2 = x.reshape(x.shape[0] if x.dim() > 1 else 1, -1)
+        cur = self._enter()
         with torch.cuda.stream(self.torch_stream):
             N.call("si_act_prepare", self.handle, N.ptr(x2), x2.shape[1], x2.shape[0])
+        self._leave(cur)
         return x2.shape[0]
 
     def qmatvec_prepared(self, w, batch, out=None, accumulate=False):
         torch = _torch()
+        cur = self._enter()
         with torch.cuda.stream(self.torch_stream):
             if out is None:
                 out = torch.empty((batch, w.rows), dtype=torch.float32, device="cuda:%d" % self.device)
             N.call("si_qmatvec_prepared", self.handle, w.handle, N.ptr(out), batch, int(accumulate))
+        self._leave(cur)
         return out
 
     def qmatvec_host(self, w, x):
