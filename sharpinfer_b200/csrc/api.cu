@@ -95,6 +95,33 @@ static int weight_alloc(si_ctx* c, int qt, int64_t rows, int64_t cols, si_weight
   return SI_OK;
 }
 
+// Read and clear the device error word after the stream has been synchronised.
+int check_device_errors(si_ctx* c) {
+  int v = 0;
+  SI_CUDA(cudaMemcpy(&v, c->dev_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) {
+    // a kernel gave up part-way: clear the error word and the shared-tile counters
+    SI_CUDA(cudaMemset(c->dev_err, 0, sizeof(int)));
+    if (c->qmv_count.ptr) SI_CUDA(cudaMemset(c->qmv_count.ptr, 0, c->qmv_count.bytes));
+    SI_FAIL(SI_ERR_TIMEOUT, "a device-side bounded wait gave up (error bits 0x%x)", v);
+  }
+  return SI_OK;
+}
+
+// Grow the streaming-matvec scratch for weight w (counters start at zero).
+int ensure_qmv_scratch(si_ctx* c, const si_weight* w) {
+  size_t sb;
+  int64_t cn;
+  const int64_t nunit = w->qtype == SI_Q8_0 ? (w->nblk + 7) / 8 : w->nblk;
+  qmv_scratch_need(w->tiles, nunit, c->sm_count, &sb, &cn);
+  if (c->qmv_split.bytes < sb) SI_TRY(ensure(c->qmv_split, sb));
+  if (c->qmv_count.bytes < (size_t)cn * 4) {
+    SI_TRY(ensure(c->qmv_count, (size_t)cn * 4));
+    SI_CUDA(cudaMemset(c->qmv_count.ptr, 0, c->qmv_count.bytes));
+  }
+  return SI_OK;
+}
+
 // Row chunk (multiple of 16 rows) whose GGUF bytes fit the staging budget.
 static int64_t chunk_rows(int qt, int64_t cols) {
   const int64_t budget = 64ll << 20;
@@ -137,6 +164,14 @@ SI_EXPORT int si_init(int device, si_ctx** out) {
     delete c;
     SI_FAIL(SI_ERR_CUDA, "cudaStreamCreate failed: %s", cudaGetErrorString(e));
   }
+  e = cudaMalloc(&c->dev_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(c->dev_err, 0, sizeof(int));
+
+  if (e != cudaSuccess) {
+    cudaStreamDestroy(c->stream);
+    delete c;
+    SI_FAIL(SI_ERR_CUDA, "context allocation failed: %s", cudaGetErrorString(e));
+  }
   *out = c;
   return SI_OK;
 }
@@ -146,10 +181,12 @@ SI_EXPORT int si_shutdown(si_ctx* c) {
   if (!c) return SI_OK;
   cudaSetDevice(c->device);
   cudaStreamSynchronize(c->stream);
-  for (si_devbuf* b : {&c->xfrag, &c->xsfrag, &c->xscale, &c->stage[0], &c->stage[1],
-                       &c->stage[2], &c->stage[3]})
+  for (si_devbuf* b : {&c->xprep, &c->stage[0], &c->stage[1], &c->stage[2], &c->stage[3]})
     if (b->ptr) cudaFree(b->ptr);
   if (c->pinned) cudaFreeHost(c->pinned);
+  if (c->dev_err) cudaFree(c->dev_err);
+  if (c->qmv_split.ptr) cudaFree(c->qmv_split.ptr);
+  if (c->qmv_count.ptr) cudaFree(c->qmv_count.ptr);
   cudaStreamDestroy(c->stream);
   delete c;
   return SI_OK;
@@ -177,7 +214,7 @@ SI_EXPORT int si_synchronize(si_ctx* c) {
   if (!c) SI_FAIL(SI_ERR_INVALID, "si_synchronize: ctx is NULL");
   SI_TRY(bind_device(c));
   SI_CUDA(cudaStreamSynchronize(c->stream));
-  return SI_OK;
+  return check_device_errors(c);
 }
 
 SI_EXPORT int si_weight_upload(si_ctx* c, int qt, const void* blocks, int64_t rows, int64_t cols,
@@ -339,11 +376,9 @@ SI_EXPORT int si_act_prepare(si_ctx* c, const float* x, int64_t cols, int batch)
     SI_FAIL(SI_ERR_INVALID, "si_act_prepare: cols=%lld must be a multiple of 32 in [32, %d]", (long long)cols, SI_MAX_K);
   SI_TRY(bind_device(c));
   const int K = (int)cols;
-  SI_TRY(ensure(c->xfrag, xfrag_bytes(K, batch)));
-  SI_TRY(ensure(c->xsfrag, xsfrag_bytes(K, batch)));
-  SI_TRY(ensure(c->xscale, xscale_bytes(batch)));
-  SI_TRY(launch_prep(c->stream, x, nullptr, nullptr, 0.f, SI_PREP_PLAIN, K, batch, nullptr,
-                     (uint4*)c->xfrag.ptr, (uint32_t*)c->xsfrag.ptr, (float*)c->xscale.ptr, false));
+  SI_TRY(ensure(c->xprep, xprep_bytes(K, batch)));
+  SI_TRY(launch_prep(c->stream, x, K, nullptr, nullptr, 0.f, SI_PREP_PLAIN, K, batch, nullptr,
+                     (uint8_t*)c->xprep.ptr, false));
   c->prep_cols = K;
   c->prep_batch = batch;
   return SI_OK;
@@ -357,8 +392,9 @@ SI_EXPORT int si_qmatvec_prepared(si_ctx* c, const si_weight* w, float* y, int b
     SI_FAIL(SI_ERR_INVALID, "si_qmatvec_prepared: prepared activations are %dx%d, weight needs %dx%lld",
             c->prep_batch, c->prep_cols, batch, (long long)w->cols);
   SI_TRY(bind_device(c));
-  return launch_qmv(c->stream, w, (const uint4*)c->xfrag.ptr, (const uint32_t*)c->xsfrag.ptr,
-                    (const float*)c->xscale.ptr, batch, y, accumulate ? SI_EPI_ADD : SI_EPI_STORE, true);
+  SI_TRY(ensure_qmv_scratch(c, w));
+  return launch_qmv(c->stream, w, (const uint8_t*)c->xprep.ptr, batch, y,
+                    accumulate ? SI_EPI_ADD : SI_EPI_STORE, c->qmv(), true);
 }
 
 SI_EXPORT int si_qmatvec(si_ctx* c, const si_weight* w, const float* x, float* y, int batch) {
@@ -384,6 +420,7 @@ SI_EXPORT int si_qmatvec_host(si_ctx* c, const si_weight* w, const float* x, flo
   uint8_t* yh = (uint8_t*)c->pinned + xb;
   SI_CUDA(cudaMemcpyAsync(yh, c->stage[2].ptr, yb, cudaMemcpyDeviceToHost, c->stream));
   SI_CUDA(cudaStreamSynchronize(c->stream));
+  SI_TRY(check_device_errors(c));
   memcpy(y, yh, yb);
   return SI_OK;
 }

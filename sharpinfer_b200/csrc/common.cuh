@@ -43,6 +43,39 @@ void clear_error();
 // Context / weights
 // ---------------------------------------------------------------------------
 
+namespace si {
+// Device scratch of the streaming matvec: partial sums of row tiles split
+// between warps ([tiles][slots][64] f32) and per-tile arrival counters
+// ([tiles] int, zero between launches).
+struct QmvBuffers {
+  float* split;
+  size_t split_bytes;
+  int* count;
+  int64_t count_n;
+  int* err;
+  int sms;
+};
+// CTAs (of nw warps) of the streaming matvec for `units` 16x256 units.
+inline int64_t qmv_warp_grid(int64_t units, int nw, int sms) {
+  int64_t g = units / nw;
+  return g < 1 ? 1 : (g > sms ? sms : g);
+}
+// Scratch a streaming matvec over `tiles` row tiles of `nunit` units needs:
+// split floats and counter ints (an upper bound over the ring layouts).
+inline void qmv_scratch_need(int64_t tiles, int64_t nunit, int sms, size_t* split_bytes,
+                             int64_t* counts) {
+  int64_t worst = 0;
+  for (int nw : {8, 16}) {
+    const int64_t units = tiles * nunit, grid = qmv_warp_grid(units, nw, sms);
+    const int64_t minr = units / (grid * nw);
+    const int64_t maxc = minr > 0 ? (nunit - 1 + minr - 1) / minr + 1 : nunit + 1;
+    if (maxc > worst) worst = maxc;
+  }
+  *split_bytes = (size_t)tiles * worst * 64 * 4;
+  *counts = tiles;
+}
+}  // namespace si
+
 // Grow-only device buffer owned by a context.
 struct si_devbuf {
   void* ptr = nullptr;
@@ -56,8 +89,15 @@ struct si_ctx {
   cudaStream_t stream = nullptr;
   // Activation staging for the stand-alone quantised matvec: fragment-ordered
   // f16 hi/lo activations, Q4_K sub-block sums and per-vector scales.
-  si_devbuf xfrag, xsfrag, xscale;
+  si_devbuf xprep;
   int prep_cols = 0, prep_batch = 0;  // shape of the prepared activations
+  int* dev_err = nullptr;             // device error word (SI_DEVERR_* bits)
+  si_devbuf qmv_split;                // streaming-matvec split-tile partial sums
+  si_devbuf qmv_count;                // and their counters (zero between launches)
+  si::QmvBuffers qmv() const {
+    return si::QmvBuffers{(float*)qmv_split.ptr, qmv_split.bytes, (int*)qmv_count.ptr,
+                          (int64_t)(qmv_count.bytes / 4), dev_err, sm_count};
+  }
   // Host-pointer entry points: device staging and pinned host staging.
   si_devbuf stage[4];
   void* pinned = nullptr;
@@ -79,6 +119,8 @@ namespace si {
 int ensure(si_devbuf& b, size_t bytes);
 int ensure_pinned(si_ctx* c, size_t bytes);
 int bind_device(si_ctx* c);
+int check_device_errors(si_ctx* c);
+int ensure_qmv_scratch(si_ctx* c, const si_weight* w);
 
 // Bytes of one 16-row x one quant block tile in the device layout.
 inline int64_t tile_block_bytes(int qt) {
@@ -109,16 +151,21 @@ enum { SI_EPI_STORE = 0, SI_EPI_ADD = 1 };
 constexpr int SI_MAX_K = 49152;  // activation length limit of the prep kernel (smem)
 constexpr int SI_MAX_BATCH = 16;
 
-// Sizes of the prepared-activation buffers for K columns and batch B.
-inline size_t xfrag_bytes(int K, int B) { return (size_t)((B + 3) / 4) * (K / 32) * 32 * 16; }
-inline size_t xsfrag_bytes(int K, int B) { return (size_t)((B + 3) / 4) * (K / 256 + 1) * 32 * 4; }
-inline size_t xscale_bytes(int B) { return (size_t)((B + 3) / 4) * 4 * 4; }
+// Prepared activations ("xprep") for K columns and batch B.  Batch b is MMA
+// group mg = b/4; a group with Bm batches uses LW = 8*Bm fragment lanes.
+// Per group and per 256-column unit (132*LW + 16 bytes): [8 x 32-column
+// groups][LW lanes] x 16 B of f16 hi/lo B fragments, LW x 4 B of Q4_K
+// sub-block sums, then the 4 inverse activation scales (f32) of the group.
+inline int xprep_units(int K) { return (K + 255) / 256; }
+inline size_t xprep_bytes(int K, int B) {
+  const int nmg = (B + 3) / 4;
+  return (size_t)xprep_units(K) * (132 * 8 * B + 16 * nmg);
+}
 
-int launch_prep(cudaStream_t s, const float* x, const float* x2, const float* norm_w,
-                float eps, int mode, int K, int B, float* xout, uint4* xfrag, uint32_t* xsfrag,
-                float* xscale, bool pdl);
-int launch_qmv(cudaStream_t s, const si_weight* w, const uint4* xfrag, const uint32_t* xsfrag,
-               const float* xscale, int B, float* y, int epi, bool pdl);
+int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const float* norm_w,
+                float eps, int mode, int K, int B, float* xout, uint8_t* xprep, bool pdl);
+int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
+               const QmvBuffers& qb, bool pdl);
 int launch_synth_blocks(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma,
                         int64_t blk0, int64_t nblocks, uint8_t* dst);
 
@@ -160,11 +207,11 @@ __device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
   return r;
 }
 
-// D = A(16x16 f16, row) * B(16x8 f16, col) + C (f32).
+// D = A(16x16 f16, row) * B(16x8 f16, col) + C (f32).  No side effects beyond
+// its registers, so the compiler may schedule it freely.
 __device__ __forceinline__ void mma16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2,
                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -191,6 +238,75 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+
+// ---- shared-memory barriers and bulk (TMA engine) copies --------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for phase `parity` of a barrier; gives up after ~200 ms (returns false).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 24); i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && globaltimer_ns() - t0 > 200000000ull) return false;
+  }
+  return false;
+}
+// Bulk global -> shared copy (16-byte aligned addresses, size a multiple of 16)
+// completing `bytes` transactions on the barrier.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
+                                         uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+  return r;
+}
+__device__ __forceinline__ uint2 lds_v2(uint32_t a) {
+  uint2 r;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
+  return r;
+}
+__device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
+  uint32_t r;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(a));
+  return r;
+}
+
+// Device error bits written by kernels whose bounded waits give up.
+enum { SI_DEVERR_WAIT_TIMEOUT = 1 };
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

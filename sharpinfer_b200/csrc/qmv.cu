@@ -7,23 +7,31 @@
 // The kernel is bound by HBM: every weight byte is read once.  To keep the
 // instruction rate below the byte rate, the multiply-adds run on the tensor
 // cores (mma.m16n8k16, f16 inputs, f32 accumulation):
-//  * quant codes are small integers and exact in f16; for Q4_K the 6-bit
-//    sub-block scale is folded in exactly with one f16 FMA per pair
-//    ((1024+q)*sc - 1024*sc = q*sc, exact because q*sc <= 945);
+//  * quant codes are small integers and exact in f16; for Q4_K a nibble
+//    masked in place is the f16 subnormal q * 2^-24 (or 16q * 2^-24), and
+//    one f16 multiply by the 6-bit sub-block scale gives q*sc*2^-24 exactly
+//    (q*sc <= 945 fits the subnormal grid);
 //  * activations are split into f16 hi + lo parts (x*2^e = hi + lo, ~22
-//    significant bits) that occupy two MMA columns, so the product keeps
-//    f32-level accuracy; batch b uses columns 2(b%4), 2(b%4)+1 of MMA group
-//    b/4;
+//    significant bits, e chosen per 256-column unit) that occupy two MMA
+//    columns, so the product keeps f32-level accuracy; batch b uses columns
+//    2(b%4), 2(b%4)+1 of MMA group b/4;
 //  * the Q4_K mins term dmin * sum_s m_s * X_s (X_s = sum of x over the 32
 //    elements of sub-block s) is one more MMA per block.
-// A row tile of 16 rows is one CTA of 8 warps; the warps split the K blocks
-// and are reduced through shared memory.
+// A row tile of 16 rows is one CTA of 8 warps; the warps split the K range
+// in units of 256 columns and are reduced through shared memory at the end.
+//
+// Batch <= 4: each warp streams its units through its own shared-memory ring
+// (cp.async.bulk on the TMA engine, one mbarrier per stage): the 16-row
+// weight tile-block and the unit's prepared activations arrive together, so
+// no load sits on the critical path of the MMAs.  Batch 5..16 reads the
+// weights and activations straight from global memory.
 #include "common.cuh"
 
 namespace si {
 namespace {
 
 constexpr int QMV_WARPS = 8;
+constexpr int XUNIT_LANES_FULL = 32;
 
 __device__ __forceinline__ float h2f_lo(uint32_t w) {
   return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFF)));
@@ -43,123 +51,99 @@ __device__ __forceinline__ uint32_t pack2(__half a, __half b) {
   return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
 }
 
-__device__ __forceinline__ float block_reduce_sum(float v, float* red) {
-  v = warp_sum(v);
-  int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float r = 0.f;
-  for (int i = 0; i < nw; i++) r += red[i];
-  return r;
-}
-
-__device__ __forceinline__ float block_reduce_max(float v, float* red) {
-  v = warp_max(v);
-  int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  float r = 0.f;
-  for (int i = 0; i < nw; i++) r = fmaxf(r, red[i]);
-  return r;
+// Byte offset of MMA group mg, unit u in the prepared-activation buffer.
+// A unit of a group with LW lanes is 132*LW + 16 bytes: fragments, Q4_K
+// sub-block sums, then the 4 inverse activation scales of the group.
+__device__ __forceinline__ int xunit_bytes(int LW) { return 132 * LW + 16; }
+__device__ __forceinline__ int64_t xprep_off(int mg, int nunit, int u, int LW) {
+  return (int64_t)mg * nunit * xunit_bytes(XUNIT_LANES_FULL) + (int64_t)u * xunit_bytes(LW);
 }
 
 // ---------------------------------------------------------------------------
-// Activation preparation.  One CTA per (padded) batch row.
+// Activation preparation.  One CTA per (256-column unit u, batch row b).
 //   mode 0: v = x
-//   mode 1: v = RmsNorm(x) * w   (TensorOps.cs:135-145)
+//   mode 1: v = RmsNorm(x) * w   (TensorOps.cs:135-145); every CTA of a row
+//           computes the row's sum of squares in the same order
 //   mode 2: v = SiLU(x) * x2     (TensorOps.cs:191-195 then :169-185)
-// Outputs (lane (g, t) of MMA group mg owns column g = batch 4mg + g/2,
-// part g&1 = hi/lo):
-//   xfrag [nmg][K/32][32] uint4 = {b01, b23} of k-tiles 2j and 2j+1,
-//   xsfrag [nmg][K/256][32] u32 = (X_{2t}, X_{2t+1}) * 2^-5 of the block,
-//   xscale[b] = 2^-e where v * 2^e is what the fragments hold.
+// x row b starts at x + b*ldx (x2 likewise).  The unit's values are scaled by
+// 2^e (max |v * 2^e| in [2^13, 2^14)), split into f16 hi/lo fragments for
+// the lanes 8(b%4) .. 8(b%4)+7 of MMA group b/4, and 2^-e is stored with them.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(512) k_prep(const float* __restrict__ x,
+__global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int ldx,
                                               const float* __restrict__ x2,
                                               const float* __restrict__ nw, float eps, int mode,
                                               int K, int B, float* __restrict__ xout,
-                                              uint4* __restrict__ xfrag,
-                                              uint32_t* __restrict__ xsfrag,
-                                              float* __restrict__ xscale) {
-  extern __shared__ float sv[];  // K values
-  __shared__ float red[32];
-  const int b = blockIdx.x, mg = b >> 2, cb = b & 3;
-  const bool live = b < B;
+                                              uint8_t* __restrict__ xprep) {
+  __shared__ float sv[256];
+  __shared__ float red[8];
+  const int u = blockIdx.x, b = blockIdx.y, mg = b >> 2, cb = b & 3;
+  const int Bm = min(4, B - 4 * mg), LW = 8 * Bm;
+  const int nunit = gridDim.x;
+  const int tid = threadIdx.x, k = 256 * u + tid;
   pdl_wait();
-  float amax = 0.f;
-  if (live) {
-    const float* xb = x + (int64_t)b * K;
-    float scale = 1.f;
-    if (mode == 1) {
-      float ss = 0.f;
-      for (int k = threadIdx.x; k < K; k += blockDim.x) ss = __fadd_rn(ss, __fmul_rn(xb[k], xb[k]));
-      ss = block_reduce_sum(ss, red);
-      scale = 1.0f / sqrtf(ss / (float)K + eps);
-    }
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-      float v;
-      if (mode == 1) {
-        v = __fmul_rn(__fmul_rn(xb[k], scale), nw[k]);
-      } else if (mode == 2) {
-        float gte = xb[k];
-        float sl = __fdiv_rn(gte, __fadd_rn(1.0f, expf(-gte)));
-        v = __fmul_rn(sl, x2[(int64_t)b * K + k]);
-      } else {
-        v = xb[k];
-      }
-      sv[k] = v;
-      if (xout) xout[(int64_t)b * K + k] = v;
-      amax = fmaxf(amax, fabsf(v));
-    }
-    amax = block_reduce_max(amax, red);
+  const float* xb = x + (int64_t)b * ldx;
+  float scale = 1.f;
+  if (mode == 1) {
+    float ss = 0.f;
+    for (int i = tid; i < K; i += 256) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < 8; i++) t += red[i];
+    scale = 1.0f / sqrtf(t / (float)K + eps);
   }
+  float v = 0.f;
+  if (k < K) {
+    if (mode == 1) {
+      v = __fmul_rn(__fmul_rn(xb[k], scale), nw[k]);
+    } else if (mode == 2) {
+      const float gte = xb[k];
+      const float sl = __fdiv_rn(gte, __fadd_rn(1.0f, expf(-gte)));
+      v = __fmul_rn(sl, x2[(int64_t)b * ldx + k]);
+    } else {
+      v = xb[k];
+    }
+    if (xout) xout[(int64_t)b * K + k] = v;
+  }
+  sv[tid] = v;
+  float amax = warp_max(fabsf(v));
   __syncthreads();
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  __syncthreads();
+  amax = 0.f;
+  for (int i = 0; i < 8; i++) amax = fmaxf(amax, red[i]);
   int e = 0;
-  if (live && amax > 0.f && amax <= 3.0e38f) {
+  if (amax > 0.f && amax <= 3.0e38f) {
     int E;
     frexpf(amax, &E);  // amax < 2^E
     e = 14 - E;
     e = e < -100 ? -100 : (e > 100 ? 100 : e);
   }
   const float s = ldexpf(1.0f, e);
-  if (threadIdx.x == 0) xscale[b] = live ? ldexpf(1.0f, -e) : 0.f;
-  const int K32 = K >> 5;
-  for (int it = threadIdx.x; it < K32 * 8; it += blockDim.x) {
-    int j = it >> 3, part = (it >> 2) & 1, t = it & 3;
-    int lane = 8 * cb + 4 * part + t;
-    uint4 r = make_uint4(0, 0, 0, 0);
-    if (live) {
-      uint32_t w[4];
+  uint8_t* unit = xprep + xprep_off(mg, nunit, u, LW);
+  if (tid < 64) {  // fragments: 8 groups x (hi, lo) x 4 lanes
+    const int jj = tid >> 3, part = (tid >> 2) & 1, t = tid & 3;
+    const int L = 8 * cb + 4 * part + t;
+    uint32_t w[4];
 #pragma unroll
-      for (int h = 0; h < 2; h++) {
-        int base = 32 * j + 16 * h + 2 * t;
-        float v0 = sv[base] * s, v1 = sv[base + 1] * s, v2 = sv[base + 8] * s,
-              v3 = sv[base + 9] * s;
-        w[2 * h] = pack2(split_part(v0, part), split_part(v1, part));
-        w[2 * h + 1] = pack2(split_part(v2, part), split_part(v3, part));
-      }
-      r = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int h = 0; h < 2; h++) {
+      const int base = 32 * jj + 16 * h + 2 * t;
+      const float v0 = sv[base] * s, v1 = sv[base + 1] * s, v2 = sv[base + 8] * s, v3 = sv[base + 9] * s;
+      w[2 * h] = pack2(split_part(v0, part), split_part(v1, part));
+      w[2 * h + 1] = pack2(split_part(v2, part), split_part(v3, part));
     }
-    xfrag[((int64_t)mg * K32 + j) * 32 + lane] = r;
-  }
-  if (xsfrag && (K & 255) == 0) {
-    const int K256 = K >> 8;
-    const float s5 = s * 0.03125f;  // X * 2^-5 keeps the 32-term sums inside f16 range
-    for (int it = threadIdx.x; it < K256 * 8; it += blockDim.x) {
-      int bb = it >> 3, part = (it >> 2) & 1, t = it & 3;
-      int lane = 8 * cb + 4 * part + t;
-      uint32_t r = 0;
-      if (live) {
-        float X0 = 0.f, X1 = 0.f;
-        const float* p0 = sv + 256 * bb + 32 * (2 * t);
-        for (int k = 0; k < 32; k++) X0 += p0[k];
-        for (int k = 0; k < 32; k++) X1 += p0[32 + k];
-        r = pack2(split_part(X0 * s5, part), split_part(X1 * s5, part));
-      }
-      xsfrag[((int64_t)mg * K256 + bb) * 32 + lane] = r;
-    }
+    *(uint4*)(unit + (jj * LW + L) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else if (tid < 72) {  // Q4_K sub-block sums (X_{2t}, X_{2t+1}) * 2^-5
+    const int part = (tid >> 2) & 1, t = tid & 3;
+    const int L = 8 * cb + 4 * part + t;
+    float X0 = 0.f, X1 = 0.f;
+    for (int i = 0; i < 32; i++) X0 += sv[64 * t + i];
+    for (int i = 0; i < 32; i++) X1 += sv[64 * t + 32 + i];
+    const float s5 = s * 0.03125f;
+    *(uint32_t*)(unit + 8 * LW * 16 + L * 4) = pack2(split_part(X0 * s5, part), split_part(X1 * s5, part));
+  } else if (tid == 72) {
+    *(float*)(unit + 132 * LW + 4 * cb) = ldexpf(1.0f, -e);
   }
   __syncthreads();
   pdl_launch();
@@ -170,19 +154,18 @@ __global__ void __launch_bounds__(512) k_prep(const float* __restrict__ x,
 // tg/tg8: rows g and g+8 of the tile, batch 4mg + t.
 // ---------------------------------------------------------------------------
 template <int NMG, int EPI>
-__device__ __forceinline__ void qmv_epilogue(const float (&tg)[NMG], const float (&tg8)[NMG],
-                                             const float* __restrict__ xscale, int B, int64_t rows,
-                                             float* __restrict__ y) {
+__device__ __forceinline__ void qmv_epilogue(const float (&tg)[NMG], const float (&tg8)[NMG], int B,
+                                             int64_t rows, float* __restrict__ y, int tile) {
   __shared__ float red[QMV_WARPS][NMG][2][32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  __syncthreads();  // the previous tile's reduction has been read
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
   for (int mg = 0; mg < NMG; mg++) {
     red[warp][mg][0][lane] = tg[mg];
     red[warp][mg][1][lane] = tg8[mg];
   }
   __syncthreads();
-  // 2 * NMG * 32 outputs, one per thread.
-  const int o = threadIdx.x;
+  const int o = threadIdx.x;  // 2 * NMG * 32 outputs, one per thread
   if (o < 2 * NMG * 32) {
     const int mg = o >> 6, half = (o >> 5) & 1, ln = o & 31;
     float v = 0.f;
@@ -190,31 +173,52 @@ __device__ __forceinline__ void qmv_epilogue(const float (&tg)[NMG], const float
     for (int w = 0; w < QMV_WARPS; w++) v += red[w][mg][half][ln];
     const int gg = ln >> 2, tt = ln & 3;
     const int bt = 4 * mg + tt;
-    const int64_t row = (int64_t)blockIdx.x * 16 + gg + 8 * half;
+    const int64_t row = (int64_t)tile * 16 + gg + 8 * half;
     if (bt < B && row < rows) {
-      v *= xscale[bt];
       float* dst = y + (int64_t)bt * rows + row;
       if (EPI == SI_EPI_ADD) *dst += v;
       else *dst = v;
     }
   }
-  (void)g;
-  (void)t;
 }
 
 // ---------------------------------------------------------------------------
-// Q4_K
+// Per-unit compute, shared by the streaming (shared memory) and the global
+// memory kernels.  `Ld` reads the unit's weight bytes (w*) and this lane's
+// activation data: fragments of 32-column group j (frag), the Q4_K sub-block
+// sum word (xsum) and the inverse activation scale of its batch (inv).  Lanes
+// without a batch column read zeros.
 // ---------------------------------------------------------------------------
-struct Q4kRegs {
-  uint4 h0, h1, q[4];
+struct SmemLd {
+  const uint8_t* w;
+  const uint8_t* xf;  // lane's fragment base (or the zero region)
+  const uint8_t* xs;  // lane's sub-block sum word (or zero)
+  const uint8_t* xi;  // lane's inverse scale (or zero)
+  int fstride;        // bytes between 32-column groups
+  __device__ __forceinline__ uint4 w16(int off) const { return *(const uint4*)(w + off); }
+  __device__ __forceinline__ uint2 w8(int off) const { return *(const uint2*)(w + off); }
+  __device__ __forceinline__ uint32_t w4(int off) const { return *(const uint32_t*)(w + off); }
+  __device__ __forceinline__ uint4 frag(int j) const { return *(const uint4*)(xf + j * fstride); }
+  __device__ __forceinline__ uint32_t xsum() const { return *(const uint32_t*)xs; }
+  __device__ __forceinline__ float inv() const { return *(const float*)xi; }
 };
 
-__device__ __forceinline__ void q4k_load(Q4kRegs& r, const uint8_t* tb, int g, int lane) {
-  r.h0 = ldg_nc_v4(tb + 16 * g);
-  r.h1 = ldg_nc_v4(tb + 16 * (g + 8));
-#pragma unroll
-  for (int c = 0; c < 4; c++) r.q[c] = ldg_nc_v4(tb + 256 + c * 512 + lane * 16);
-}
+struct GlobLd {
+  const uint8_t* w;
+  const uint8_t* xf;
+  const uint8_t* xs;
+  const uint8_t* xi;
+  int fstride;
+  bool on, oni;
+  __device__ __forceinline__ uint4 w16(int off) const { return __ldg((const uint4*)(w + off)); }
+  __device__ __forceinline__ uint2 w8(int off) const { return __ldg((const uint2*)(w + off)); }
+  __device__ __forceinline__ uint32_t w4(int off) const { return __ldg((const unsigned*)(w + off)); }
+  __device__ __forceinline__ uint4 frag(int j) const {
+    return on ? __ldg((const uint4*)(xf + j * fstride)) : make_uint4(0, 0, 0, 0);
+  }
+  __device__ __forceinline__ uint32_t xsum() const { return on ? __ldg((const unsigned*)xs) : 0u; }
+  __device__ __forceinline__ float inv() const { return oni ? __ldg((const float*)xi) : 0.f; }
+};
 
 __device__ __forceinline__ uint32_t sc_half2(uint32_t lo4, uint32_t hi4, int s) {
   // (sc_s, sc_s) as f16x2 for sub-block s of a decoded scale pair of words.
@@ -224,117 +228,68 @@ __device__ __forceinline__ uint32_t sc_half2(uint32_t lo4, uint32_t hi4, int s) 
   return hsub2_u32(prmt(w, 0x64646464u, sel), 0x64006400u);
 }
 
-template <int NMG, int EPI>
-__global__ void __launch_bounds__(256) k_qmv_q4k(const uint8_t* __restrict__ W, int nblk,
-                                                 int64_t rows, const uint4* __restrict__ xfrag,
-                                                 const uint32_t* __restrict__ xsfrag,
-                                                 const float* __restrict__ xscale, int B,
-                                                 float* __restrict__ y) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const uint8_t* tile = W + (int64_t)blockIdx.x * nblk * 2304;
-  const int K32 = nblk * 8;
-  const uint32_t msel = (t & 1) ? 0x5342u : 0x5140u;
-  float tg[NMG], tg8[NMG];
+// One Q4_K unit (one block, 16 rows).  ld[mg] views MMA group mg.
+template <int NMG, typename Ld>
+__device__ __forceinline__ void unit_q4k(const Ld (&ld)[NMG], int lane, float (&tg)[NMG],
+                                         float (&tg8)[NMG]) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint4 h0 = ld[0].w16(16 * g), h1 = ld[0].w16(16 * (g + 8));
+  const uint32_t scl0 = h0.y & 0x3F3F3F3Fu, mnl0 = h0.z & 0x3F3F3F3Fu;
+  const uint32_t sch0 = (h0.w & 0x0F0F0F0Fu) | ((h0.y >> 2) & 0x30303030u);
+  const uint32_t mnh0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+  const uint32_t scl1 = h1.y & 0x3F3F3F3Fu, mnl1 = h1.z & 0x3F3F3F3Fu;
+  const uint32_t sch1 = (h1.w & 0x0F0F0F0Fu) | ((h1.y >> 2) & 0x30303030u);
+  const uint32_t mnh1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+  float C[NMG][4], Cm[NMG][4];
 #pragma unroll
-  for (int i = 0; i < NMG; i++) tg[i] = tg8[i] = 0.f;
-
-  Q4kRegs cur, nxt;
-  int b = warp;
-  if (b < nblk) q4k_load(cur, tile + (int64_t)b * 2304, g, lane);
-  pdl_wait();
-  for (; b < nblk; b += QMV_WARPS) {
-    const int bn = b + QMV_WARPS;
-    if (bn < nblk) q4k_load(nxt, tile + (int64_t)bn * 2304, g, lane);
-
-    // 6-bit scales and mins of rows g and g+8 (GetScaleMinK4, Quantization.cs:302-314),
-    // four per word.
-    const uint32_t scl0 = cur.h0.y & 0x3F3F3F3Fu, mnl0 = cur.h0.z & 0x3F3F3F3Fu;
-    const uint32_t sch0 = (cur.h0.w & 0x0F0F0F0Fu) | ((cur.h0.y >> 2) & 0x30303030u);
-    const uint32_t mnh0 = ((cur.h0.w >> 4) & 0x0F0F0F0Fu) | ((cur.h0.z >> 2) & 0x30303030u);
-    const uint32_t scl1 = cur.h1.y & 0x3F3F3F3Fu, mnl1 = cur.h1.z & 0x3F3F3F3Fu;
-    const uint32_t sch1 = (cur.h1.w & 0x0F0F0F0Fu) | ((cur.h1.y >> 2) & 0x30303030u);
-    const uint32_t mnh1 = ((cur.h1.w >> 4) & 0x0F0F0F0Fu) | ((cur.h1.z >> 2) & 0x30303030u);
-
-    float C[NMG][4], Cm[NMG][4];
+  for (int mg = 0; mg < NMG; mg++)
 #pragma unroll
-    for (int mg = 0; mg < NMG; mg++)
+    for (int i = 0; i < 4; i++) C[mg][i] = Cm[mg][i] = 0.f;
+  {  // mins: A[row][k] = m_k(row) for k < 8, B[k][col] = X_k(col) * 2^-5
+    const uint32_t msel = (t & 1) ? 0x5342u : 0x5140u;
+    const uint32_t am0 = hsub2_u32(prmt(t < 2 ? mnl0 : mnh0, 0x64646464u, msel), 0x64006400u);
+    const uint32_t am1 = hsub2_u32(prmt(t < 2 ? mnl1 : mnh1, 0x64646464u, msel), 0x64006400u);
 #pragma unroll
-      for (int i = 0; i < 4; i++) C[mg][i] = Cm[mg][i] = 0.f;
-
-    // mins: A[row][k] = m_k(row) for k < 8, B[k][col] = X_k(col) * 2^-5.
-    {
-      const uint32_t am0 = hsub2_u32(prmt(t < 2 ? mnl0 : mnh0, 0x64646464u, msel), 0x64006400u);
-      const uint32_t am1 = hsub2_u32(prmt(t < 2 ? mnl1 : mnh1, 0x64646464u, msel), 0x64006400u);
-#pragma unroll
-      for (int mg = 0; mg < NMG; mg++) {
-        const uint32_t xs = xsfrag[((int64_t)mg * nblk + b) * 32 + lane];
-        mma16816(Cm[mg], am0, am1, 0u, 0u, xs, 0u);
-      }
-    }
-#pragma unroll
-    for (int c = 0; c < 4; c++) {
-      uint4 xf[NMG][2];
-#pragma unroll
-      for (int mg = 0; mg < NMG; mg++) {
-        const uint4* xp = xfrag + ((int64_t)mg * K32 + (int64_t)b * 8 + 2 * c) * 32 + lane;
-        xf[mg][0] = xp[0];
-        xf[mg][1] = xp[32];
-      }
-#pragma unroll
-      for (int hs = 0; hs < 2; hs++) {  // sub-block s = 2c + hs
-        const int s = 2 * c + hs;
-        const uint32_t sg = sc_half2(scl0, sch0, s), sg8 = sc_half2(scl1, sch1, s);
-        const uint32_t nsg = hmul2_u32(sg, 0xE400E400u);  // -1024 * sc, exact
-        const uint32_t nsg8 = hmul2_u32(sg8, 0xE400E400u);
-#pragma unroll
-        for (int kk = 0; kk < 2; kk++) {
-          const int i = 2 * hs + kk;
-          const uint32_t w = i == 0 ? cur.q[c].x : i == 1 ? cur.q[c].y : i == 2 ? cur.q[c].z : cur.q[c].w;
-          const uint32_t w8 = w >> 8;
-          const uint32_t a0 = hfma2_u32(lop3_and_or(w, 0x000F000Fu, 0x64006400u), sg, nsg);
-          const uint32_t a1 = hfma2_u32(lop3_and_or(w, 0x00F000F0u, 0x64006400u), sg8, nsg8);
-          const uint32_t a2 = hfma2_u32(lop3_and_or(w8, 0x000F000Fu, 0x64006400u), sg, nsg);
-          const uint32_t a3 = hfma2_u32(lop3_and_or(w8, 0x00F000F0u, 0x64006400u), sg8, nsg8);
-#pragma unroll
-          for (int mg = 0; mg < NMG; mg++) {
-            const uint4& xv = xf[mg][hs];
-            mma16816(C[mg], a0, a1, a2, a3, kk ? xv.z : xv.x, kk ? xv.w : xv.y);
-          }
-        }
-      }
-    }
-    const float d0 = h2f_lo(cur.h0.x), dm0 = h2f_hi(cur.h0.x) * 32.f;
-    const float d1 = h2f_lo(cur.h1.x) * 0.0625f, dm1 = h2f_hi(cur.h1.x) * 32.f;
-#pragma unroll
-    for (int mg = 0; mg < NMG; mg++) {
-      tg[mg] += d0 * (C[mg][0] + C[mg][1]) - dm0 * (Cm[mg][0] + Cm[mg][1]);
-      tg8[mg] += d1 * (C[mg][2] + C[mg][3]) - dm1 * (Cm[mg][2] + Cm[mg][3]);
-    }
-    if (bn < nblk) cur = nxt;
+    for (int mg = 0; mg < NMG; mg++) mma16816(Cm[mg], am0, am1, 0u, 0u, ld[mg].xsum(), 0u);
   }
-  pdl_launch();
-  qmv_epilogue<NMG, EPI>(tg, tg8, xscale, B, rows, y);
-}
-
-// ---------------------------------------------------------------------------
-// Q6_K
-// ---------------------------------------------------------------------------
-struct Q6kRegs {
-  uint4 L[4];
-  uint2 H[4];
-  uint4 s0, s1;
-  uint32_t d;
-};
-
-__device__ __forceinline__ void q6k_load(Q6kRegs& r, const uint8_t* tb, int g, int lane) {
 #pragma unroll
   for (int c = 0; c < 4; c++) {
-    r.L[c] = ldg_nc_v4(tb + c * 768 + lane * 16);
-    r.H[c] = ldg_nc_v2(tb + c * 768 + 512 + lane * 8);
+    const uint4 q = ld[0].w16(256 + c * 512 + lane * 16);
+    uint4 xv[NMG][2];
+#pragma unroll
+    for (int mg = 0; mg < NMG; mg++) {
+      xv[mg][0] = ld[mg].frag(2 * c);
+      xv[mg][1] = ld[mg].frag(2 * c + 1);
+    }
+#pragma unroll
+    for (int hs = 0; hs < 2; hs++) {  // sub-block s = 2c + hs
+      const int s = 2 * c + hs;
+      const uint32_t sg = sc_half2(scl0, sch0, s), sg8 = sc_half2(scl1, sch1, s);
+#pragma unroll
+      for (int kk = 0; kk < 2; kk++) {
+        const int i = 2 * hs + kk;
+        const uint32_t w = i == 0 ? q.x : i == 1 ? q.y : i == 2 ? q.z : q.w;
+        const uint32_t w8 = w >> 8;
+        // nibble masked in place = f16 subnormal q*2^-24 (16q*2^-24 for row g+8)
+        const uint32_t a0 = hmul2_u32(w & 0x000F000Fu, sg);
+        const uint32_t a1 = hmul2_u32(w & 0x00F000F0u, sg8);
+        const uint32_t a2 = hmul2_u32(w8 & 0x000F000Fu, sg);
+        const uint32_t a3 = hmul2_u32(w8 & 0x00F000F0u, sg8);
+#pragma unroll
+        for (int mg = 0; mg < NMG; mg++)
+          mma16816(C[mg], a0, a1, a2, a3, kk ? xv[mg][hs].z : xv[mg][hs].x,
+                   kk ? xv[mg][hs].w : xv[mg][hs].y);
+      }
+    }
   }
-  r.s0 = ldg_nc_v4(tb + 3072 + 16 * g);
-  r.s1 = ldg_nc_v4(tb + 3072 + 16 * (g + 8));
-  r.d = *(const uint32_t*)(tb + 3328 + 4 * g);
+  const float d0 = h2f_lo(h0.x) * 16777216.f, dm0 = h2f_hi(h0.x) * 32.f;
+  const float d1 = h2f_lo(h1.x) * 1048576.f, dm1 = h2f_hi(h1.x) * 32.f;
+#pragma unroll
+  for (int mg = 0; mg < NMG; mg++) {
+    const float inv = ld[mg].inv();
+    tg[mg] += inv * (d0 * (C[mg][0] + C[mg][1]) - dm0 * (Cm[mg][0] + Cm[mg][1]));
+    tg8[mg] += inv * (d1 * (C[mg][2] + C[mg][3]) - dm1 * (Cm[mg][2] + Cm[mg][3]));
+  }
 }
 
 __device__ __forceinline__ float sbyte(uint4 v, int k) {
@@ -342,218 +297,464 @@ __device__ __forceinline__ float sbyte(uint4 v, int k) {
   return (float)(int8_t)((w >> (8 * (k & 3))) & 0xFF);
 }
 
-template <int NMG, int EPI>
-__global__ void __launch_bounds__(256) k_qmv_q6k(const uint8_t* __restrict__ W, int nblk,
-                                                 int64_t rows, const uint4* __restrict__ xfrag,
-                                                 const uint32_t* __restrict__ /*unused*/,
-                                                 const float* __restrict__ xscale, int B,
-                                                 float* __restrict__ y) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
-  const uint8_t* tile = W + (int64_t)blockIdx.x * nblk * 3360;
-  const int K32 = nblk * 8;
-  float tg[NMG], tg8[NMG];
+// One Q6_K unit (one block, 16 rows).
+template <int NMG, typename Ld>
+__device__ __forceinline__ void unit_q6k(const Ld (&ld)[NMG], int lane, float (&tg)[NMG],
+                                         float (&tg8)[NMG]) {
+  const int g = lane >> 2;
+  const uint4 s0 = ld[0].w16(3072 + 16 * g), s1 = ld[0].w16(3072 + 16 * (g + 8));
+  const uint32_t dp = ld[0].w4(3328 + 4 * g);
+  float acc[NMG], acc8[NMG];
 #pragma unroll
-  for (int i = 0; i < NMG; i++) tg[i] = tg8[i] = 0.f;
-  Q6kRegs cur, nxt;
-  int b = warp;
-  if (b < nblk) q6k_load(cur, tile + (int64_t)b * 3360, g, lane);
+  for (int mg = 0; mg < NMG; mg++) acc[mg] = acc8[mg] = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const uint4 Lq = ld[0].w16(c * 768 + lane * 16);
+    const uint2 Hq = ld[0].w8(c * 768 + 512 + lane * 8);
+    uint4 xv[NMG][2];
+#pragma unroll
+    for (int mg = 0; mg < NMG; mg++) {
+      xv[mg][0] = ld[mg].frag(2 * c);
+      xv[mg][1] = ld[mg].frag(2 * c + 1);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int kt = 4 * c + i;
+      const uint32_t L = i == 0 ? Lq.x : i == 1 ? Lq.y : i == 2 ? Lq.z : Lq.w;
+      const uint32_t Hw = (i < 2 ? Hq.x : Hq.y) >> (2 * (i & 1));
+      const uint32_t L8 = L >> 8, H8 = Hw >> 8, Hs = Hw << 8;
+      const uint32_t a0 = hsub2_u32(lop3_and_or(L, 0x000F000Fu, lop3_and_or(Hw, 0x00300030u, 0x64006400u)), 0x64206420u);
+      const uint32_t a1 = hsub2_u32(lop3_and_or(L, 0x00F000F0u, lop3_and_or(Hw, 0x03000300u, 0x64006400u)), 0x66006600u);
+      const uint32_t a2 = hsub2_u32(lop3_and_or(L8, 0x000F000Fu, lop3_and_or(H8, 0x00300030u, 0x64006400u)), 0x64206420u);
+      const uint32_t a3 = hsub2_u32(lop3_and_or(L8, 0x00F000F0u, lop3_and_or(Hs, 0x03000300u, 0x64006400u)), 0x66006600u);
+      const float f0 = sbyte(s0, kt), f1 = sbyte(s1, kt);
+#pragma unroll
+      for (int mg = 0; mg < NMG; mg++) {
+        float Cc[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint4& x = xv[mg][i >> 1];
+        mma16816(Cc, a0, a1, a2, a3, (i & 1) ? x.z : x.x, (i & 1) ? x.w : x.y);
+        acc[mg] += f0 * (Cc[0] + Cc[1]);
+        acc8[mg] += f1 * (Cc[2] + Cc[3]);
+      }
+    }
+  }
+  const float d0 = h2f_lo(dp), d1 = h2f_hi(dp) * 0.0625f;
+#pragma unroll
+  for (int mg = 0; mg < NMG; mg++) {
+    const float inv = ld[mg].inv();
+    tg[mg] += inv * d0 * acc[mg];
+    tg8[mg] += inv * d1 * acc8[mg];
+  }
+}
+
+// One Q8_0 unit: nq (<= 8) consecutive 32-column blocks, 16 rows.
+template <int NMG, typename Ld>
+__device__ __forceinline__ void unit_q80(const Ld (&ld)[NMG], int lane, int nq, float (&tg)[NMG],
+                                         float (&tg8)[NMG]) {
+  const int g = lane >> 2;
+  float acc[NMG], acc8[NMG];
+#pragma unroll
+  for (int mg = 0; mg < NMG; mg++) acc[mg] = acc8[mg] = 0.f;
+#pragma unroll 2
+  for (int qb = 0; qb < nq; qb++) {
+    const uint4 q = ld[0].w16(qb * 544 + lane * 16);
+    const uint32_t dp = ld[0].w4(qb * 544 + 512 + 4 * g);
+    float C[NMG][4];
+    uint4 xv[NMG];
+#pragma unroll
+    for (int mg = 0; mg < NMG; mg++) {
+      C[mg][0] = C[mg][1] = C[mg][2] = C[mg][3] = 0.f;
+      xv[mg] = ld[mg].frag(qb);
+    }
+#pragma unroll
+    for (int kt = 0; kt < 2; kt++) {
+      const uint32_t wg = (kt ? q.z : q.x) ^ 0x80808080u;
+      const uint32_t wg8 = (kt ? q.w : q.y) ^ 0x80808080u;
+      const uint32_t a0 = hsub2_u32(prmt(wg, 0x64646464u, 0x5140u), 0x64806480u);
+      const uint32_t a1 = hsub2_u32(prmt(wg8, 0x64646464u, 0x5140u), 0x64806480u);
+      const uint32_t a2 = hsub2_u32(prmt(wg, 0x64646464u, 0x5342u), 0x64806480u);
+      const uint32_t a3 = hsub2_u32(prmt(wg8, 0x64646464u, 0x5342u), 0x64806480u);
+#pragma unroll
+      for (int mg = 0; mg < NMG; mg++)
+        mma16816(C[mg], a0, a1, a2, a3, kt ? xv[mg].z : xv[mg].x, kt ? xv[mg].w : xv[mg].y);
+    }
+    const float d0 = h2f_lo(dp), d1 = h2f_hi(dp);
+#pragma unroll
+    for (int mg = 0; mg < NMG; mg++) {
+      acc[mg] += d0 * (C[mg][0] + C[mg][1]);
+      acc8[mg] += d1 * (C[mg][2] + C[mg][3]);
+    }
+  }
+#pragma unroll
+  for (int mg = 0; mg < NMG; mg++) {
+    const float inv = ld[mg].inv();
+    tg[mg] += inv * acc[mg];
+    tg8[mg] += inv * acc8[mg];
+  }
+}
+
+template <int QT>
+struct QtInfo;
+template <>
+struct QtInfo<SI_Q4_K> { static constexpr int TBB = 2304, QPU = 1; };
+template <>
+struct QtInfo<SI_Q6_K> { static constexpr int TBB = 3360, QPU = 1; };
+template <>
+struct QtInfo<SI_Q8_0> { static constexpr int TBB = 544, QPU = 8; };
+
+// ---------------------------------------------------------------------------
+// Streaming kernel (batch 1..4, one MMA group).  One persistent CTA of NW
+// warps per SM.  The units (16 rows x 256 columns) of all row tiles are
+// numbered tile-major -- which is also their order in memory -- and split
+// into one contiguous, equal range per warp of the grid.  Each warp streams
+// its range through its own NS-deep shared-memory ring (cp.async.bulk of the
+// unit's weights and prepared activations, one mbarrier per stage) and keeps
+// the partial sums of the tile it is in.  A tile that lies wholly in one
+// warp's range is written by that warp.  A tile split between warps leaves
+// one partial per contributing warp in global scratch; the last contributor
+// (per-tile arrival counter) adds them in warp order -- the result does not
+// depend on timing -- and writes y.
+// ---------------------------------------------------------------------------
+struct QmvScratch {
+  float* split;  // [tiles][maxc][64] partial sums of tiles split between warps
+  int* count;    // [tiles] arrivals (zero between launches; reset by the last)
+  int* err;      // device error word
+  int maxc;      // contributor slots per tile
+};
+
+template <int QT, int B, int NW, int NS>
+struct WarpCfg {
+  static constexpr int TBB = QtInfo<QT>::TBB, QPU = QtInfo<QT>::QPU;
+  static constexpr int LW = 8 * B, XB = 132 * LW + 16, WB = TBB * QPU, SB = WB + XB;
+  static constexpr int ZERO = 8 * LW * 16 + 32 * 16;  // zero region (covers every lane offset)
+  static constexpr int SMEM = NW * NS * SB + ZERO + NW * NS * 8;
+};
+
+template <int EPI, int B>
+__device__ __forceinline__ void store_tile(float* __restrict__ y, int64_t rows, int T, int lane,
+                                           float v0, float v8) {
+  const int g = lane >> 2, t = lane & 3;
+  if (t < B) {
+    const int64_t r0 = (int64_t)T * 16 + g, r1 = r0 + 8;
+    float* yb = y + (int64_t)t * rows;
+    if (r0 < rows) {
+      if (EPI == SI_EPI_ADD) yb[r0] += v0;
+      else yb[r0] = v0;
+    }
+    if (r1 < rows) {
+      if (EPI == SI_EPI_ADD) yb[r1] += v8;
+      else yb[r1] = v8;
+    }
+  }
+}
+
+template <int QT, int EPI, int B, int NW, int NS>
+__global__ void __launch_bounds__(NW * 32, 1)
+    k_qmv_warp(const uint8_t* __restrict__ W, int nblk, int64_t rows, int tiles,
+               const uint8_t* __restrict__ xprep, float* __restrict__ y, QmvScratch scr) {
+  using Cfg = WarpCfg<QT, B, NW, NS>;
+  constexpr int TBB = Cfg::TBB, QPU = Cfg::QPU, LW = Cfg::LW, XB = Cfg::XB, WB = Cfg::WB, SB = Cfg::SB;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* zero = smem + NW * NS * SB;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = lane & 3;
+  uint8_t* ring = smem + warp * NS * SB;
+  const uint32_t ring_s = smem_u32(ring);
+  const uint32_t bar0 = smem_u32(zero + Cfg::ZERO) + warp * NS * 8;
+
+  const int nunit = (nblk + QPU - 1) / QPU;
+  const int64_t U = (int64_t)tiles * nunit;
+  const int64_t GW = (int64_t)gridDim.x * NW, gw = (int64_t)blockIdx.x * NW + warp;
+  const int64_t ub = U * gw / GW, ue = U * (gw + 1) / GW;
+  const int total = (int)(ue - ub);
+
+  for (int i = threadIdx.x; i < Cfg::ZERO / 4; i += blockDim.x) ((uint32_t*)zero)[i] = 0u;
+  if (lane == 0) {
+    for (int s = 0; s < NS; s++) mbar_init(bar0 + 8 * s, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();  // zero region and barriers ready
+
+  // Units are contiguous in memory in range order, so the weight cursor only
+  // advances; the activation cursor wraps to unit 0 at each tile.
+  const int64_t c0T = ub / nunit;
+  const int c0U = (int)(ub - c0T * nunit);
+  const uint8_t* wsrc = W + (c0T * nblk + (int64_t)c0U * QPU) * TBB;
+  int iU = c0U;                      // unit index (in its tile) of the next copy to issue
+  const int pre = total < NS ? total : NS;
+  if (lane == 0) {
+    const uint8_t* p = wsrc;
+    int u = c0U;
+    for (int s = 0; s < pre; s++) {
+      const uint32_t wb = (uint32_t)(min(QPU, nblk - u * QPU) * TBB);
+      mbar_expect_tx(bar0 + 8 * s, wb);
+      bulk_g2s(ring_s + s * SB, p, wb, bar0 + 8 * s);
+      p += wb;
+      if (++u == nunit) u = 0;
+    }
+  }
   pdl_wait();
-  for (; b < nblk; b += QMV_WARPS) {
-    const int bn = b + QMV_WARPS;
-    if (bn < nblk) q6k_load(nxt, tile + (int64_t)bn * 3360, g, lane);
-    const float d0 = h2f_lo(cur.d), d1 = h2f_hi(cur.d) * 0.0625f;
+  if (lane == 0) {
+    int u = c0U;
+    for (int s = 0; s < pre; s++) {
+      mbar_arrive_expect_tx(bar0 + 8 * s, XB);
+      bulk_g2s(ring_s + s * SB + WB, xprep + (int64_t)u * XB, XB, bar0 + 8 * s);
+      if (++u == nunit) u = 0;
+    }
+  }
+  for (int s = 0; s < pre; s++) {
+    wsrc += (min(QPU, nblk - iU * QPU) * TBB);
+    if (++iU == nunit) iU = 0;
+  }
+  int issued = pre;
+
+  const bool on = lane < LW, oni = 8 * t < LW;
+  const int xf_off = on ? WB + lane * 16 : -1;  // -1: read the zero region
+  float tg[1] = {0.f}, tg8[1] = {0.f};
+  bool ok = true;
+  uint32_t ph = 0;
+  int cT = (int)c0T, cU = c0U;
+  int left = min(nunit - c0U, total);  // units of the current tile in this range
+  int64_t tile_first = c0T * nunit;
+  for (int k0 = 0; k0 < total; k0 += NS) {
 #pragma unroll
-    for (int c = 0; c < 4; c++) {
-      uint4 xf[NMG][2];
-#pragma unroll
-      for (int mg = 0; mg < NMG; mg++) {
-        const uint4* xp = xfrag + ((int64_t)mg * K32 + (int64_t)b * 8 + 2 * c) * 32 + lane;
-        xf[mg][0] = xp[0];
-        xf[mg][1] = xp[32];
+    for (int s = 0; s < NS; s++) {
+      if (k0 + s >= total) break;
+      if (!mbar_wait_bounded(bar0 + 8 * s, ph)) {  // waited even after a failure
+        if (ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
+        ok = false;
       }
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const int kt = 4 * c + i;
-        const uint32_t L = i == 0 ? cur.L[c].x : i == 1 ? cur.L[c].y : i == 2 ? cur.L[c].z : cur.L[c].w;
-        const uint32_t Hw = (i < 2 ? cur.H[c].x : cur.H[c].y) >> (2 * (i & 1));
-        const uint32_t L8 = L >> 8, H8 = Hw >> 8, Hs = Hw << 8;
-        const uint32_t a0 = hsub2_u32(lop3_and_or(L, 0x000F000Fu, lop3_and_or(Hw, 0x00300030u, 0x64006400u)), 0x64206420u);
-        const uint32_t a1 = hsub2_u32(lop3_and_or(L, 0x00F000F0u, lop3_and_or(Hw, 0x03000300u, 0x64006400u)), 0x66006600u);
-        const uint32_t a2 = hsub2_u32(lop3_and_or(L8, 0x000F000Fu, lop3_and_or(H8, 0x00300030u, 0x64006400u)), 0x64206420u);
-        const uint32_t a3 = hsub2_u32(lop3_and_or(L8, 0x00F000F0u, lop3_and_or(Hs, 0x03000300u, 0x64006400u)), 0x66006600u);
-        const float f0 = d0 * sbyte(cur.s0, kt), f1 = d1 * sbyte(cur.s1, kt);
-#pragma unroll
-        for (int mg = 0; mg < NMG; mg++) {
-          float Cc[4] = {0.f, 0.f, 0.f, 0.f};
-          const uint4& xv = xf[mg][i >> 1];
-          mma16816(Cc, a0, a1, a2, a3, (i & 1) ? xv.z : xv.x, (i & 1) ? xv.w : xv.y);
-          tg[mg] += f0 * (Cc[0] + Cc[1]);
-          tg8[mg] += f1 * (Cc[2] + Cc[3]);
+      if (ok) {
+        const uint8_t* st = ring + s * SB;
+        SmemLd ld[1];
+        ld[0].w = st;
+        ld[0].xf = xf_off >= 0 ? st + xf_off : zero + lane * 16;
+        ld[0].xs = on ? st + WB + 8 * LW * 16 + lane * 4 : zero;
+        ld[0].xi = oni ? st + WB + 132 * LW + 4 * t : zero;
+        ld[0].fstride = LW * 16;
+        if (QT == SI_Q4_K) unit_q4k<1>(ld, lane, tg, tg8);
+        else if (QT == SI_Q6_K) unit_q6k<1>(ld, lane, tg, tg8);
+        else unit_q80<1>(ld, lane, min(QPU, nblk - cU * QPU), tg, tg8);
+      }
+      __syncwarp();
+      if (issued < total) {  // refill this stage with the next unit of the range
+        const uint32_t wb = (uint32_t)(min(QPU, nblk - iU * QPU) * TBB);
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar0 + 8 * s, wb + XB);
+          bulk_g2s(ring_s + s * SB, wsrc, wb, bar0 + 8 * s);
+          bulk_g2s(ring_s + s * SB + WB, xprep + (int64_t)iU * XB, XB, bar0 + 8 * s);
         }
+        wsrc += wb;
+        if (++iU == nunit) iU = 0;
+        issued++;
+      }
+      cU++;
+      if (--left == 0) {
+        // ---- this warp's part of tile cT is done ----
+        const int64_t t0 = tile_first, t1 = tile_first + nunit;  // tile's unit range
+        if (t0 >= ub && t1 <= ue) {
+          store_tile<EPI, B>(y, rows, cT, lane, tg[0], tg8[0]);
+        } else {
+          // contributors: the warps owning units t0 .. t1-1 (owner(x) = the last
+          // warp whose range starts at or before x; every range is non-empty)
+          const int64_t wf = ((t0 + 1) * GW - 1) / U, wl = (t1 * GW - 1) / U;
+          const int ncon = (int)(wl - wf + 1), slot = (int)(gw - wf);
+          float* base = scr.split + (int64_t)cT * scr.maxc * 64;
+          base[slot * 64 + lane] = tg[0];
+          base[slot * 64 + 32 + lane] = tg8[0];
+          __threadfence();
+          __syncwarp();
+          int prev = 0;
+          if (lane == 0) prev = atomicAdd(scr.count + cT, 1);
+          prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
+          if (prev == ncon - 1) {  // last contributor: add the slots in warp order
+            __threadfence();
+            float a = 0.f, b8 = 0.f;
+            for (int j = 0; j < ncon; j++) {
+              a += *(volatile float*)(base + j * 64 + lane);
+              b8 += *(volatile float*)(base + j * 64 + 32 + lane);
+            }
+            store_tile<EPI, B>(y, rows, cT, lane, a, b8);
+            if (lane == 0) scr.count[cT] = 0;
+          }
+        }
+        tg[0] = tg8[0] = 0.f;
+        cU = 0;
+        cT++;
+        tile_first += nunit;
+        left = min(nunit, total - (k0 + s) - 1);
       }
     }
-    if (bn < nblk) cur = nxt;
+    ph ^= 1u;
   }
   pdl_launch();
-  qmv_epilogue<NMG, EPI>(tg, tg8, xscale, B, rows, y);
 }
 
 // ---------------------------------------------------------------------------
-// Q8_0 (32-element blocks; four blocks per warp iteration)
+// Global-memory kernel (batch 5..16): one 16-row tile per CTA of 8 warps,
+// weights and activations read straight from global memory.
 // ---------------------------------------------------------------------------
-template <int NMG, int EPI>
-__global__ void __launch_bounds__(256) k_qmv_q80(const uint8_t* __restrict__ W, int nblk,
-                                                 int64_t rows, const uint4* __restrict__ xfrag,
-                                                 const uint32_t* __restrict__ /*unused*/,
-                                                 const float* __restrict__ xscale, int B,
-                                                 float* __restrict__ y) {
-  constexpr int U = 4;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
-  const uint8_t* tile = W + (int64_t)blockIdx.x * nblk * 544;
-  const int K32 = nblk;
+template <int QT, int NMG, int EPI>
+__global__ void __launch_bounds__(256) k_qmv_reg(const uint8_t* __restrict__ W, int nblk,
+                                                 int64_t rows, const uint8_t* __restrict__ xprep,
+                                                 int B, float* __restrict__ y) {
+  constexpr int TBB = QtInfo<QT>::TBB, QPU = QtInfo<QT>::QPU;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = lane & 3;
+  const int nunit = (nblk + QPU - 1) / QPU;
+  const uint8_t* tile = W + (int64_t)blockIdx.x * nblk * TBB;
+  int LW[NMG];
+#pragma unroll
+  for (int mg = 0; mg < NMG; mg++) LW[mg] = 8 * min(4, B - 4 * mg);
   float tg[NMG], tg8[NMG];
 #pragma unroll
-  for (int i = 0; i < NMG; i++) tg[i] = tg8[i] = 0.f;
-  bool waited = false;
-  for (int b0 = warp * U; b0 < nblk; b0 += QMV_WARPS * U) {
-    uint4 q[U];
-    uint32_t dp[U];
+  for (int mg = 0; mg < NMG; mg++) tg[mg] = tg8[mg] = 0.f;
+  pdl_wait();
+  for (int u = warp; u < nunit; u += QMV_WARPS) {
+    GlobLd ld[NMG];
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      if (b0 + u < nblk) {
-        const uint8_t* tb = tile + (int64_t)(b0 + u) * 544;
-        q[u] = ldg_nc_v4(tb + lane * 16);
-        dp[u] = *(const uint32_t*)(tb + 512 + 4 * g);
-      } else {
-        q[u] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
-        dp[u] = 0;
-      }
+    for (int mg = 0; mg < NMG; mg++) {
+      const uint8_t* xu = xprep + xprep_off(mg, nunit, u, LW[mg]);
+      ld[mg].w = tile + (int64_t)u * QPU * TBB;
+      ld[mg].xf = xu + lane * 16;
+      ld[mg].xs = xu + 8 * LW[mg] * 16 + lane * 4;
+      ld[mg].xi = xu + 132 * LW[mg] + 4 * t;
+      ld[mg].fstride = LW[mg] * 16;
+      ld[mg].on = lane < LW[mg];
+      ld[mg].oni = 8 * t < LW[mg];
     }
-    if (!waited) {
-      pdl_wait();
-      waited = true;
-    }
-#pragma unroll
-    for (int u = 0; u < U; u++) {
-      const int bb = b0 + u < nblk ? b0 + u : nblk - 1;
-      float C[NMG][4];
-#pragma unroll
-      for (int mg = 0; mg < NMG; mg++) C[mg][0] = C[mg][1] = C[mg][2] = C[mg][3] = 0.f;
-      uint4 xf[NMG];
-#pragma unroll
-      for (int mg = 0; mg < NMG; mg++) xf[mg] = xfrag[((int64_t)mg * K32 + bb) * 32 + lane];
-#pragma unroll
-      for (int kt = 0; kt < 2; kt++) {
-        const uint32_t wg = (kt ? q[u].z : q[u].x) ^ 0x80808080u;
-        const uint32_t wg8 = (kt ? q[u].w : q[u].y) ^ 0x80808080u;
-        const uint32_t a0 = hsub2_u32(prmt(wg, 0x64646464u, 0x5140u), 0x64806480u);
-        const uint32_t a1 = hsub2_u32(prmt(wg8, 0x64646464u, 0x5140u), 0x64806480u);
-        const uint32_t a2 = hsub2_u32(prmt(wg, 0x64646464u, 0x5342u), 0x64806480u);
-        const uint32_t a3 = hsub2_u32(prmt(wg8, 0x64646464u, 0x5342u), 0x64806480u);
-#pragma unroll
-        for (int mg = 0; mg < NMG; mg++)
-          mma16816(C[mg], a0, a1, a2, a3, kt ? xf[mg].z : xf[mg].x, kt ? xf[mg].w : xf[mg].y);
-      }
-      const float d0 = h2f_lo(dp[u]), d1 = h2f_hi(dp[u]);
-#pragma unroll
-      for (int mg = 0; mg < NMG; mg++) {
-        tg[mg] += d0 * (C[mg][0] + C[mg][1]);
-        tg8[mg] += d1 * (C[mg][2] + C[mg][3]);
-      }
-    }
+    if (QT == SI_Q4_K) unit_q4k<NMG>(ld, lane, tg, tg8);
+    else if (QT == SI_Q6_K) unit_q6k<NMG>(ld, lane, tg, tg8);
+    else unit_q80<NMG>(ld, lane, min(QPU, nblk - u * QPU), tg, tg8);
   }
-  if (!waited) pdl_wait();
   pdl_launch();
-  qmv_epilogue<NMG, EPI>(tg, tg8, xscale, B, rows, y);
+  qmv_epilogue<NMG, EPI>(tg, tg8, B, rows, y, (int)blockIdx.x);
 }
 
-template <typename Kern>
-int launch_k(Kern kern, cudaStream_t s, dim3 grid, dim3 block, size_t smem, bool pdl,
-             const uint8_t* W, int nblk, int64_t rows, const uint4* xfrag, const uint32_t* xsfrag,
-             const float* xscale, int B, float* y) {
+cudaLaunchConfig_t make_cfg(cudaStream_t s, dim3 grid, dim3 block, size_t smem, bool pdl,
+                            cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  SI_CUDA(cudaLaunchKernelEx(&cfg, kern, W, nblk, rows, xfrag, xsfrag, xscale, B, y));
+  return cfg;
+}
+
+constexpr int WARP_SMEM_MAX = 220 * 1024;
+
+struct ScratchCap {
+  QmvScratch scr;
+  size_t split_bytes;
+  int64_t count_n;
+};
+
+template <int QT, int EPI, int B, int NW, int NS>
+int launch_warp_cfg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y,
+                    const ScratchCap& scr_cap, int sms, bool pdl) {
+  using Cfg = WarpCfg<QT, B, NW, NS>;
+  static_assert(Cfg::SMEM <= WARP_SMEM_MAX, "ring too large");
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  SI_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !(attr_set & (1ull << dev))) {
+    SI_CUDA(cudaFuncSetAttribute(k_qmv_warp<QT, EPI, B, NW, NS>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    attr_set |= 1ull << dev;
+  }
+  // every warp gets a non-empty range: GW = grid * NW <= units
+  const int64_t nunit = (w->nblk + Cfg::QPU - 1) / Cfg::QPU;
+  const int64_t units = w->tiles * nunit;
+  const int64_t grid = qmv_warp_grid(units, NW, sms);
+  const int64_t minr = units / (grid * NW);
+  const int maxc = (int)((nunit - 1 + minr - 1) / minr + 1);
+  if ((size_t)w->tiles * maxc * 64 * 4 > scr_cap.split_bytes || w->tiles > scr_cap.count_n)
+    SI_FAIL(SI_ERR_INVALID, "qmatvec: scratch too small (need %lld tiles x %d slots)",
+            (long long)w->tiles, maxc);
+  QmvScratch scr = scr_cap.scr;
+  scr.maxc = maxc;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)grid), dim3(NW * 32), Cfg::SMEM, pdl, attr);
+  SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv_warp<QT, EPI, B, NW, NS>, (const uint8_t*)w->dev,
+                             (int)w->nblk, w->rows, (int)w->tiles, xprep, y, scr));
   return SI_OK;
 }
 
-template <int NMG, int EPI>
-int qmv_dispatch_qt(cudaStream_t s, const si_weight* w, const uint4* xfrag,
-                    const uint32_t* xsfrag, const float* xscale, int B, float* y, bool pdl) {
-  dim3 grid((unsigned)w->tiles), block(256);
-  const uint8_t* W = (const uint8_t*)w->dev;
-  switch (w->qtype) {
-    case SI_Q4_K:
-      return launch_k(k_qmv_q4k<NMG, EPI>, s, grid, block, 0, pdl, W, (int)w->nblk, w->rows, xfrag,
-                      xsfrag, xscale, B, y);
-    case SI_Q6_K:
-      return launch_k(k_qmv_q6k<NMG, EPI>, s, grid, block, 0, pdl, W, (int)w->nblk, w->rows, xfrag,
-                      xsfrag, xscale, B, y);
-    case SI_Q8_0:
-      return launch_k(k_qmv_q80<NMG, EPI>, s, grid, block, 0, pdl, W, (int)w->nblk, w->rows, xfrag,
-                      xsfrag, xscale, B, y);
-    default:
-      SI_FAIL(SI_ERR_UNSUPPORTED, "qmatvec: unsupported quant type %d", w->qtype);
+// 16 warps with the deepest ring (<= 4) that fits, else 8 warps.
+template <int QT, int EPI, int B>
+int launch_warp(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y,
+                const ScratchCap& scr, int sms, bool pdl) {
+  if constexpr (WarpCfg<QT, B, 16, 4>::SMEM <= WARP_SMEM_MAX)
+    return launch_warp_cfg<QT, EPI, B, 16, 4>(s, w, xprep, y, scr, sms, pdl);
+  else if constexpr (WarpCfg<QT, B, 16, 3>::SMEM <= WARP_SMEM_MAX)
+    return launch_warp_cfg<QT, EPI, B, 16, 3>(s, w, xprep, y, scr, sms, pdl);
+  else if constexpr (WarpCfg<QT, B, 16, 2>::SMEM <= WARP_SMEM_MAX)
+    return launch_warp_cfg<QT, EPI, B, 16, 2>(s, w, xprep, y, scr, sms, pdl);
+  else
+    return launch_warp_cfg<QT, EPI, B, 8, 2>(s, w, xprep, y, scr, sms, pdl);
+}
+
+template <int QT, int NMG, int EPI>
+int launch_reg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, bool pdl) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)w->tiles), dim3(256), 0, pdl, attr);
+  SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv_reg<QT, NMG, EPI>, (const uint8_t*)w->dev, (int)w->nblk,
+                             w->rows, xprep, B, y));
+  return SI_OK;
+}
+
+template <int QT, int EPI>
+int dispatch_b(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y,
+               const ScratchCap& scr, int sms, bool pdl) {
+  const int64_t units = w->tiles * ((w->nblk + QtInfo<QT>::QPU - 1) / QtInfo<QT>::QPU);
+  if (units < 16) B = B <= 4 ? -B : B;  // too small to stream: one CTA per tile
+  switch (B) {
+    case 1: return launch_warp<QT, EPI, 1>(s, w, xprep, y, scr, sms, pdl);
+    case 2: return launch_warp<QT, EPI, 2>(s, w, xprep, y, scr, sms, pdl);
+    case 3: return launch_warp<QT, EPI, 3>(s, w, xprep, y, scr, sms, pdl);
+    case 4: return launch_warp<QT, EPI, 4>(s, w, xprep, y, scr, sms, pdl);
+    default: break;
+  }
+  if (B < 0) return launch_reg<QT, 1, EPI>(s, w, xprep, -B, y, pdl);
+  switch ((B + 3) / 4) {
+    case 2: return launch_reg<QT, 2, EPI>(s, w, xprep, B, y, pdl);
+    case 3: return launch_reg<QT, 3, EPI>(s, w, xprep, B, y, pdl);
+    case 4: return launch_reg<QT, 4, EPI>(s, w, xprep, B, y, pdl);
+    default: SI_FAIL(SI_ERR_INVALID, "qmatvec: batch %d outside 1..16", B);
   }
 }
 
 template <int EPI>
-int qmv_dispatch_nmg(cudaStream_t s, const si_weight* w, const uint4* xfrag,
-                     const uint32_t* xsfrag, const float* xscale, int B, float* y, bool pdl) {
-  switch ((B + 3) / 4) {
-    case 1: return qmv_dispatch_qt<1, EPI>(s, w, xfrag, xsfrag, xscale, B, y, pdl);
-    case 2: return qmv_dispatch_qt<2, EPI>(s, w, xfrag, xsfrag, xscale, B, y, pdl);
-    case 3: return qmv_dispatch_qt<3, EPI>(s, w, xfrag, xsfrag, xscale, B, y, pdl);
-    case 4: return qmv_dispatch_qt<4, EPI>(s, w, xfrag, xsfrag, xscale, B, y, pdl);
-    default: SI_FAIL(SI_ERR_INVALID, "qmatvec: batch %d outside 1..16", B);
+int dispatch_qt(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y,
+                const ScratchCap& scr, int sms, bool pdl) {
+  switch (w->qtype) {
+    case SI_Q4_K: return dispatch_b<SI_Q4_K, EPI>(s, w, xprep, B, y, scr, sms, pdl);
+    case SI_Q6_K: return dispatch_b<SI_Q6_K, EPI>(s, w, xprep, B, y, scr, sms, pdl);
+    case SI_Q8_0: return dispatch_b<SI_Q8_0, EPI>(s, w, xprep, B, y, scr, sms, pdl);
+    default: SI_FAIL(SI_ERR_UNSUPPORTED, "qmatvec: unsupported quant type %d", w->qtype);
   }
 }
 
 }  // namespace
 
-int prep_smem_bytes(int K) { return K * 4; }
-
-int launch_prep(cudaStream_t s, const float* x, const float* x2, const float* norm_w, float eps,
-                int mode, int K, int B, float* xout, uint4* xfrag, uint32_t* xsfrag,
-                float* xscale, bool pdl) {
+int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const float* norm_w,
+                float eps, int mode, int K, int B, float* xout, uint8_t* xprep, bool pdl) {
   if (K <= 0 || (K & 31)) SI_FAIL(SI_ERR_INVALID, "prep: K=%d must be a positive multiple of 32", K);
   if (K > SI_MAX_K) SI_FAIL(SI_ERR_INVALID, "prep: K=%d above the supported maximum %d", K, SI_MAX_K);
-  const int nmg = (B + 3) / 4;
-  size_t smem = (size_t)K * 4;
-  static uint64_t attr_set = 0;  // one bit per device
-  int dev = 0;
-  SI_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !(attr_set & (1ull << dev))) {
-    SI_CUDA(cudaFuncSetAttribute(k_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, SI_MAX_K * 4));
-    attr_set |= 1ull << dev;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nmg * 4);
-  cfg.blockDim = dim3(512);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
+  if (B < 1 || B > SI_MAX_BATCH) SI_FAIL(SI_ERR_INVALID, "prep: batch %d outside 1..%d", B, SI_MAX_BATCH);
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  SI_CUDA(cudaLaunchKernelEx(&cfg, k_prep, x, x2, norm_w, eps, mode, K, B, xout, xfrag, xsfrag,
-                             xscale));
+  cudaLaunchConfig_t cfg = make_cfg(s, dim3(xprep_units(K), B), dim3(256), 0, pdl, attr);
+  SI_CUDA(cudaLaunchKernelEx(&cfg, k_prep, x, ldx, x2, norm_w, eps, mode, K, B, xout, xprep));
   return SI_OK;
 }
 
-int launch_qmv(cudaStream_t s, const si_weight* w, const uint4* xfrag, const uint32_t* xsfrag,
-               const float* xscale, int B, float* y, int epi, bool pdl) {
-  if (epi == SI_EPI_ADD) return qmv_dispatch_nmg<SI_EPI_ADD>(s, w, xfrag, xsfrag, xscale, B, y, pdl);
-  return qmv_dispatch_nmg<SI_EPI_STORE>(s, w, xfrag, xsfrag, xscale, B, y, pdl);
+int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
+               const QmvBuffers& qb, bool pdl) {
+  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0}, qb.split_bytes, qb.count_n};
+  if (epi == SI_EPI_ADD) return dispatch_qt<SI_EPI_ADD>(s, w, xprep, B, y, scr, qb.sms, pdl);
+  return dispatch_qt<SI_EPI_STORE>(s, w, xprep, B, y, scr, qb.sms, pdl);
 }
 
 }  // namespace si

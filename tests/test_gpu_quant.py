@@ -54,7 +54,11 @@ def test_device_generator_matches_host(ctx, qt, recipe):
     assert np.array_equal(canon(got.cpu().numpy()), canon(ref))
 
 
-SHAPES = [(1, 256), (16, 256), (255, 512), (257, 1024), (4096, 4096), (1000, 14336)]
+# Row tiles of 16; the streaming kernel splits the tiles' 256-column units
+# evenly over one CTA per SM, so some shapes put a tile across two CTAs
+# (e.g. 4800 x 768 and 4096 x 4096) and others do not (2384 x 256).
+SHAPES = [(1, 256), (16, 256), (255, 512), (257, 1024), (2384, 256), (4800, 768), (4096, 4096),
+          (1000, 14336)]
 
 
 @pytest.mark.parametrize("qt", QTS)
@@ -74,6 +78,19 @@ def test_qmatvec_parity(ctx, qt, rows, cols, batch):
     assert err < TOL, err
     # much tighter than required: hi/lo activations keep f32-level accuracy
     assert err < 2e-5, err
+
+
+@pytest.mark.parametrize("qt", QTS)
+@pytest.mark.parametrize("batch", [1, 4, 7])
+def test_qmatvec_is_deterministic(ctx, qt, batch):
+    """Repeated calls give bit-identical results (shared row tiles are combined in a fixed order)."""
+    import torch
+    rows, cols = 4800, 768 if qt != N.SI_Q8_0 else 800
+    w = ctx.synth_weight(qt, rows, cols, 3, 4)
+    x = torch.from_numpy(synth_f32_host(batch * cols, 3, 5).reshape(batch, cols)).cuda()
+    ys = [ctx.qmatvec(w, x).cpu().numpy() for _ in range(3)]
+    ctx.synchronize()
+    assert np.array_equal(ys[0], ys[1]) and np.array_equal(ys[1], ys[2])
 
 
 @pytest.mark.parametrize("qt", QTS)
