@@ -160,6 +160,85 @@ SI_EXPORT int si_qmatvec_prepared(si_ctx* ctx, const si_weight* w, float* y_dev,
 SI_EXPORT int si_qmatvec_host(si_ctx* ctx, const si_weight* w, const float* x_host,
                               float* y_host, int batch);
 
+/* ------------------------------------------------------------ decode model */
+
+/* A Llama/Mistral-architecture model resident on one GPU: the forward pass of
+ * Transformer.Forward (src/SharpInfer.Core/Layers/Transformer.cs:67-162) --
+ * RmsNorm, Q/K/V projections, RoPE, KV store, GQA attention, O projection,
+ * residual, RmsNorm, gate/up, SiLU*up, down, residual; final RmsNorm, lm_head
+ * and greedy ArgMax (SamplingPipeline.cs:64-65) -- for `batch` sequences at
+ * once, one token each, all at the same position.  Field names follow the
+ * reference's ModelConfig (Transformer.cs:43-56, KVCache.cs:28-36). */
+typedef struct {
+  int n_layers;        /* NumLayers */
+  int hidden;          /* HiddenSize */
+  int intermediate;    /* IntermediateSize */
+  int n_heads;         /* NumAttentionHeads */
+  int n_kv_heads;      /* NumKvHeads */
+  int head_dim;        /* HeadDim (128) */
+  int vocab;           /* VocabSize */
+  int max_seq;         /* KV positions per sequence (MaxSequenceLength) */
+  int max_batch;       /* sequences decoded together (1..16) */
+  float rms_eps;       /* RmsNormEps */
+  float rope_theta;    /* RopeTheta */
+  int weight_qtype;    /* projections: SI_Q4_K, SI_Q6_K or SI_Q8_0 */
+  int lm_head_qtype;   /* OutputWeight */
+  int emb_qtype;       /* TokenEmbedding (one row is dequantised per token) */
+} si_model_config;
+
+typedef struct si_model si_model;
+
+/* Tensor ids for si_model_set_tensor / si_model_tensor_recipe. */
+typedef enum {
+  SI_T_Q = 0, SI_T_K = 1, SI_T_V = 2, SI_T_O = 3, SI_T_GATE = 4, SI_T_UP = 5, SI_T_DOWN = 6,
+  SI_T_ATTN_NORM = 7, SI_T_FFN_NORM = 8,               /* layer >= 0 */
+  SI_T_EMB = 100, SI_T_LM_HEAD = 101, SI_T_FINAL_NORM = 102 /* layer = -1 */
+} si_tensor;
+
+/* Allocate the model (weights, f16 KV cache, activations) on the context's
+ * GPU.  Weights are undefined until set or synthesised. */
+SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model** out);
+SI_EXPORT int si_model_free(si_model* m);
+
+/* Upload one weight tensor as raw GGUF blocks, row-major [rows][cols] of the
+ * configured type (norms: f32[hidden]).  The projection shapes are those of
+ * LayerWeights (Transformer.cs:89-151). */
+SI_EXPORT int si_model_set_tensor(si_model* m, int layer, int tensor, const void* host);
+
+/* Fill every weight and norm with the seeded synthetic recipe (benchmarks,
+ * tests).  si_model_tensor_recipe reports, per tensor, the si_synth_* call
+ * that reproduces its bytes on the host: generator tag, type, recipe, sigma
+ * and shape (mean/sigma of the f32 norms in sigma/mean). */
+SI_EXPORT int si_model_synth(si_model* m, uint64_t seed);
+SI_EXPORT int si_model_tensor_recipe(const si_model_config* cfg, int layer, int tensor,
+                                     uint64_t* tag, int* qtype, int* recipe, float* sigma,
+                                     float* mean, int64_t* rows, int64_t* cols);
+
+/* Fill cache positions [0, len) of every layer and sequence with f16 values
+ * f16(N(0,1)) (seeded).  The K values of (layer l, sequence b) are
+ * si_synth_f16_host(len*n_kv*head_dim, seed, si_model_kv_tag(l, b, 0), 1)
+ * in the reference layout [pos][kv head][dim] (KVCache.cs:60-71). */
+SI_EXPORT int si_model_kv_synth(si_model* m, int len, uint64_t seed);
+SI_EXPORT uint64_t si_model_kv_tag(int layer, int seq, int is_value);
+
+/* Write n cache positions from host f16 arrays in the reference layout
+ * [n][kv head][dim] (KVCache.Store, KVCache.cs:46-57). */
+SI_EXPORT int si_model_kv_write(si_model* m, int layer, int seq, int pos0, int n,
+                                const uint16_t* k_host, const uint16_t* v_host);
+
+/* One decode step: token ids tokens_host[batch] at position pos (the same for
+ * every sequence; 0 <= pos < max_seq).  Writes the greedy next token of each
+ * sequence to argmax_host[batch] and, if logits_host is not NULL, the logits
+ * [batch][vocab].  Replayed as one CUDA graph per batch size. */
+SI_EXPORT int si_decode_step(si_model* m, const int* tokens_host, int batch, int pos,
+                             int* argmax_host, float* logits_host);
+
+/* Attention of one layer alone (RoPE, KV append at pos, attention) for
+ * qkv_dev [batch][(n_heads + 2 n_kv_heads) * head_dim] -> out_dev
+ * [batch][n_heads * head_dim] (test hook for the attention kernel). */
+SI_EXPORT int si_model_attention(si_model* m, int layer, const float* qkv_dev, float* out_dev,
+                                 int batch, int pos);
+
 #ifdef __cplusplus
 }
 #endif

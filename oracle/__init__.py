@@ -173,3 +173,63 @@ def matmul(a, b):
 
 def round_f16(x):
     return load().or_round_f16(x)
+
+
+class OracleModel:
+    """The reference forward pass (or_model_*, Transformer.Forward) over host GGUF tensors."""
+
+    QKVO = ("q", "k", "v", "o", "gate", "up", "down")
+
+    def __init__(self, cfg, n_seq, threads=None):
+        L = load()
+        self.cfg = cfg
+        self.handle = L.or_model_create(cfg.n_layers, cfg.hidden, cfg.intermediate, cfg.n_heads, cfg.n_kv_heads,
+                                        cfg.head_dim, cfg.vocab, cfg.max_seq, cfg.rms_eps, cfg.rope_theta, n_seq,
+                                        threads or nthreads())
+        self.keep = []
+
+    def set(self, layer, which, qtype, data):
+        data = np.ascontiguousarray(data)
+        self.keep.append(data)
+        load().or_model_set(self.handle, layer, which, qtype, _p(data))
+
+    def kv_fill(self, seq, layer, k, v):
+        k = np.ascontiguousarray(k, np.uint16)
+        v = np.ascontiguousarray(v, np.uint16)
+        load().or_model_kv_fill(self.handle, seq, layer, _p(k), _p(v), k.size // (self.cfg.n_kv_heads * self.cfg.head_dim))
+
+    def forward(self, seq, token, pos, kv_round_f16=True):
+        logits = np.empty(self.cfg.vocab, np.float32)
+        rc = load().or_model_forward(self.handle, seq, token, pos, int(kv_round_f16), _p(logits))
+        if rc:
+            raise ValueError("oracle forward failed (%d)" % rc)
+        return logits
+
+    def __del__(self):
+        try:
+            load().or_model_free(self.handle)
+        except Exception:
+            pass
+
+
+def synthetic_model(cfg, seed, n_seq, kv_len, threads=None):
+    """OracleModel holding exactly the tensors and KV prefix that si_model_synth / si_model_kv_synth
+    put on the device (generated on the host by the library's seeded generators)."""
+    from sharpinfer_b200 import native as N
+    from sharpinfer_b200.model import host_kv, host_tensor
+    om = OracleModel(cfg, n_seq, threads)
+    ids = [N.T_Q, N.T_K, N.T_V, N.T_O, N.T_GATE, N.T_UP, N.T_DOWN]
+    for l in range(cfg.n_layers):
+        for which, t in enumerate(ids):
+            om.set(l, which, cfg.weight_qtype, host_tensor(cfg, seed, l, t))
+        om.set(l, 7, 0, host_tensor(cfg, seed, l, N.T_ATTN_NORM))
+        om.set(l, 8, 0, host_tensor(cfg, seed, l, N.T_FFN_NORM))
+    om.set(-1, 0, cfg.emb_qtype, host_tensor(cfg, seed, -1, N.T_EMB))
+    om.set(-1, 1, cfg.lm_head_qtype, host_tensor(cfg, seed, -1, N.T_LM_HEAD))
+    om.set(-1, 2, 0, host_tensor(cfg, seed, -1, N.T_FINAL_NORM))
+    if kv_len:
+        for b in range(n_seq):
+            for l in range(cfg.n_layers):
+                k, v = host_kv(cfg, seed, l, b, kv_len)
+                om.kv_fill(b, l, k, v)
+    return om

@@ -1,0 +1,709 @@
+// Decode model: weights, f16 KV cache, and the decode step of
+// Transformer.Forward (src/SharpInfer.Core/Layers/Transformer.cs:67-162) as a
+// sequence of fused kernels, captured once per batch size as a CUDA graph.
+//
+// Per layer (batch B, position pos):
+//   prep   RmsNorm(x) * attn_norm -> activation fragments        (:86)
+//   qmv    [Wq; Wk; Wv] -> qkv                                    (:89-91)
+//   attn   RoPE(q, k), KV append, split-KV attention -> attn      (:94-129)
+//   prep   attn -> fragments
+//   qmv    Wo, accumulated into x (the residual add)              (:132-135)
+//   prep   RmsNorm(x) * ffn_norm                                  (:140)
+//   qmv    [Wgate; Wup] -> gu                                     (:143-144)
+//   prep   SiLU(gate) * up                                        (:147-148)
+//   qmv    Wdown, accumulated into x                              (:151-154)
+// then RmsNorm(x) * final_norm, lm_head -> logits, ArgMax.         (:158-159)
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <map>
+#include <vector>
+
+#include "model.cuh"
+#include "quantfmt.cuh"
+#include "synth.h"
+
+namespace si {
+namespace {
+
+// Element `col` of row r of a device-layout weight (reference rounding).
+__device__ __forceinline__ float weight_elem(int qt, const uint8_t* __restrict__ W, int64_t nblk,
+                                             int64_t r, int col) {
+  const int64_t T = r >> 4;
+  const int ri = (int)(r & 15);
+  if (qt == SI_Q4_K) {
+    const int64_t b = col >> 8;
+    const int e = col & 255, j = e >> 5;
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 2304);
+    const uint8_t* hdr = (const uint8_t*)(tbw + 4 * ri);
+    const float d = h2f(hdr[0] | (hdr[1] << 8)), dmin = h2f(hdr[2] | (hdr[3] << 8));
+    const uint8_t* q = hdr + 4;
+    uint32_t sc, mn;
+    if (j < 4) {
+      sc = q[j] & 63;
+      mn = q[j + 4] & 63;
+    } else {
+      sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+      mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+    const float d1 = __fmul_rn(d, (float)sc), m1f = __fmul_rn(dmin, (float)mn);
+    return __fsub_rn(__fmul_rn(d1, (float)dev_q4k_code(tbw, ri, e)), m1f);
+  } else if (qt == SI_Q6_K) {
+    const int64_t b = col >> 8;
+    const int e = col & 255;
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 3360);
+    const int8_t* scales = (const int8_t*)(tbw + 768) + 16 * ri;
+    const uint32_t dw = tbw[832 + (ri & 7)];
+    const float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
+    const float ds = __fmul_rn(d, (float)scales[e >> 4]);
+    return __fmul_rn(ds, (float)((int)dev_q6k_code(tbw, ri, e) - 32));
+  } else {
+    const int64_t b = col >> 5;
+    const int e = col & 31;
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 544);
+    const uint32_t dw = tbw[128 + (ri & 7)];
+    const float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
+    return __fmul_rn((float)dev_q80_code(tbw, ri, e), d);
+  }
+}
+
+// x[b] = row tokens[b] of the token embedding (Transformer.cs:76).
+__global__ void k_embed(const StepParams* __restrict__ p, int qt, const uint8_t* __restrict__ W,
+                        int64_t nblk, int64_t vocab, int h, float* __restrict__ x) {
+  pdl_wait();
+  const int b = blockIdx.y;
+  const int col = blockIdx.x * blockDim.x + threadIdx.x;
+  const int tok = p->tokens[b];
+  if (col < h && tok >= 0 && tok < vocab) x[(int64_t)b * h + col] = weight_elem(qt, W, nblk, tok, col);
+  pdl_launch();
+}
+
+// Greedy selection (SamplingPipeline.ArgMax, SamplingPipeline.cs:83-89):
+// first index of the maximum under strict '>'; NaNs never win, and a NaN at
+// index 0 makes the answer 0.
+__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logits, int64_t vocab,
+                                                 int* __restrict__ out) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_wait();
+  const int b = blockIdx.x;
+  const float* x = logits + (int64_t)b * vocab;
+  float bv = -INFINITY;
+  int bi = -1;
+  for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float v = x[i];
+    if (v > bv || (bi < 0 && v == bv)) {  // -inf candidates still record an index
+      bv = v;
+      bi = (int)i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+    const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (w == 0) {
+    bv = l < (int)(blockDim.x >> 5) ? sv[l] : -INFINITY;
+    bi = l < (int)(blockDim.x >> 5) ? si[l] : -1;
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (l == 0) out[b] = (isnan(x[0]) || bi < 0) ? 0 : bi;
+  }
+  pdl_launch();
+}
+
+// Seeded f16 N(0,1) for positions [0, len) of one (layer, seq) cache; the
+// generator index follows the reference layout [pos][kv head][dim].
+__global__ void k_kv_synth(__half* __restrict__ cache, uint64_t key, int len, int nkv, int max_seq) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t n = (int64_t)len * nkv * 128;
+  if (i >= n) return;
+  const int d = (int)(i % 128), kvh = (int)((i / 128) % nkv);
+  const int64_t pos = i / (128 * nkv);
+  cache[((int64_t)kvh * max_seq + pos) * 128 + d] = __ushort_as_half(si_synth_f16(key, (uint64_t)i, 1.0f));
+}
+
+__global__ void k_f32_synth(float* __restrict__ out, uint64_t key, int64_t n, float mean, float sigma) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = si_synth_f32(key, (uint64_t)i, mean, sigma);
+}
+
+// [n][nkv][128] (reference layout) -> [nkv][max_seq][128] at pos0.
+__global__ void k_kv_scatter(__half* __restrict__ cache, const uint16_t* __restrict__ src, int pos0,
+                             int n, int nkv, int max_seq) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n * nkv * 128) return;
+  const int d = (int)(i % 128), kvh = (int)((i / 128) % nkv);
+  const int64_t t = i / (128 * nkv);
+  cache[((int64_t)kvh * max_seq + pos0 + t) * 128 + d] = __ushort_as_half(src[i]);
+}
+
+cudaLaunchConfig_t cfg_of(cudaStream_t s, dim3 g, dim3 b, size_t smem, bool pdl, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = g;
+  cfg.blockDim = b;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cfg;
+}
+
+float recipe_sigma(int qt, int recipe, int64_t cols) {
+  const float rc = sqrtf((float)cols);
+  if (qt == SI_Q4_K) return recipe == SI_SYNTH_MODEL ? 1.0f / (23.3f * rc) : 0.01f;
+  if (qt == SI_Q6_K) return 1.0f / (348.0f * rc);
+  return 1.0f / (73.9f * rc);  // Q8_0: rms of a uniform int8 is ~73.9
+}
+
+}  // namespace
+}  // namespace si
+
+using namespace si;
+
+struct si_model {
+  si_ctx* c = nullptr;
+  si_model_config cfg{};
+  int G = 0, qkv_rows = 0, Kmax = 0;
+  int splits_max = 0, chunk_max = 0;
+  std::vector<si_weight*> wqkv, wo, wgu, wdown;
+  si_weight* emb = nullptr;
+  si_weight* lm_head = nullptr;
+  float* norms = nullptr;  // [L][2][h], then final [h]
+  __half* kcache = nullptr;
+  __half* vcache = nullptr;
+  float* rope = nullptr;
+  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *logits = nullptr;
+  int* argmax = nullptr;
+  uint8_t* xprep = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr;
+  int* attn_cnt = nullptr;
+  StepParams* dparams = nullptr;
+  StepParams* hparams = nullptr;  // pinned
+  int* hargmax = nullptr;         // pinned
+  std::map<int, cudaGraphExec_t> graphs;
+  std::vector<void*> allocs;
+};
+
+namespace {
+
+int dev_alloc(si_model* m, void** p, size_t bytes) {
+  cudaError_t e = cudaMalloc(p, bytes);
+  if (e != cudaSuccess)
+    SI_FAIL(e == cudaErrorMemoryAllocation ? SI_ERR_OOM : SI_ERR_CUDA, "model allocation of %zu bytes failed: %s",
+            bytes, cudaGetErrorString(e));
+  m->allocs.push_back(*p);
+  return SI_OK;
+}
+
+int make_weight(si_model* m, int qt, int64_t rows, int64_t cols, si_weight** out) {
+  si_weight* w = new si_weight();
+  w->qtype = qt;
+  w->rows = rows;
+  w->cols = cols;
+  w->tiles = (rows + 15) / 16;
+  w->nblk = cols / block_elems(qt);
+  w->bytes = (size_t)(w->tiles * w->nblk * tile_block_bytes(qt));
+  w->device = m->c->device;
+  cudaError_t e = cudaMalloc(&w->dev, w->bytes);
+  if (e != cudaSuccess) {
+    delete w;
+    SI_FAIL(e == cudaErrorMemoryAllocation ? SI_ERR_OOM : SI_ERR_CUDA, "weight allocation failed: %s",
+            cudaGetErrorString(e));
+  }
+  *out = w;
+  return SI_OK;
+}
+
+// (weight, first row) of a projection tensor inside its fused weight.
+int tensor_slot(si_model* m, int layer, int t, si_weight** w, int64_t* row0, int64_t* rows,
+                int64_t* cols) {
+  const si_model_config& c = m->cfg;
+  const int64_t hd = c.head_dim, qr = (int64_t)c.n_heads * hd, kr = (int64_t)c.n_kv_heads * hd;
+  if (layer < 0) {
+    if (t == SI_T_EMB) { *w = m->emb; *row0 = 0; *rows = c.vocab; *cols = c.hidden; return SI_OK; }
+    if (t == SI_T_LM_HEAD) { *w = m->lm_head; *row0 = 0; *rows = c.vocab; *cols = c.hidden; return SI_OK; }
+    SI_FAIL(SI_ERR_INVALID, "tensor %d is not a global quantised tensor", t);
+  }
+  if (layer >= c.n_layers) SI_FAIL(SI_ERR_INVALID, "layer %d out of range", layer);
+  switch (t) {
+    case SI_T_Q: *w = m->wqkv[layer]; *row0 = 0; *rows = qr; *cols = c.hidden; return SI_OK;
+    case SI_T_K: *w = m->wqkv[layer]; *row0 = qr; *rows = kr; *cols = c.hidden; return SI_OK;
+    case SI_T_V: *w = m->wqkv[layer]; *row0 = qr + kr; *rows = kr; *cols = c.hidden; return SI_OK;
+    case SI_T_O: *w = m->wo[layer]; *row0 = 0; *rows = c.hidden; *cols = qr; return SI_OK;
+    case SI_T_GATE: *w = m->wgu[layer]; *row0 = 0; *rows = c.intermediate; *cols = c.hidden; return SI_OK;
+    case SI_T_UP: *w = m->wgu[layer]; *row0 = c.intermediate; *rows = c.intermediate; *cols = c.hidden; return SI_OK;
+    case SI_T_DOWN: *w = m->wdown[layer]; *row0 = 0; *rows = c.hidden; *cols = c.intermediate; return SI_OK;
+    default: SI_FAIL(SI_ERR_INVALID, "tensor %d is not a quantised layer tensor", t);
+  }
+}
+
+float* norm_ptr(si_model* m, int layer, int t) {
+  const int64_t h = m->cfg.hidden;
+  if (layer < 0) return m->norms + (int64_t)m->cfg.n_layers * 2 * h;
+  return m->norms + ((int64_t)layer * 2 + (t == SI_T_FFN_NORM ? 1 : 0)) * h;
+}
+
+int check_config(const si_model_config* c) {
+  if (!c) SI_FAIL(SI_ERR_INVALID, "model config is NULL");
+  if (c->n_layers <= 0 || c->hidden <= 0 || c->intermediate <= 0 || c->vocab <= 0 || c->max_seq <= 0)
+    SI_FAIL(SI_ERR_INVALID, "model config has non-positive sizes");
+  if (c->head_dim != 128) SI_FAIL(SI_ERR_UNSUPPORTED, "head_dim %d (this build supports 128)", c->head_dim);
+  if (c->n_heads <= 0 || c->n_kv_heads <= 0 || c->n_heads % c->n_kv_heads)
+    SI_FAIL(SI_ERR_INVALID, "n_heads %d must be a positive multiple of n_kv_heads %d", c->n_heads, c->n_kv_heads);
+  const int G = c->n_heads / c->n_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8) SI_FAIL(SI_ERR_UNSUPPORTED, "%d q heads per kv head", G);
+  if (c->max_batch < 1 || c->max_batch > SI_MAX_BATCH) SI_FAIL(SI_ERR_INVALID, "max_batch %d outside 1..16", c->max_batch);
+  for (int qt : {c->weight_qtype, c->lm_head_qtype, c->emb_qtype})
+    if (qt != SI_Q4_K && qt != SI_Q6_K && qt != SI_Q8_0) SI_FAIL(SI_ERR_UNSUPPORTED, "quant type %d", qt);
+  auto blk = [](int qt) { return qt == SI_Q8_0 ? 32 : 256; };
+  if (c->hidden % blk(c->weight_qtype) || c->intermediate % blk(c->weight_qtype) ||
+      (c->n_heads * c->head_dim) % blk(c->weight_qtype) || c->hidden % blk(c->lm_head_qtype) ||
+      c->hidden % blk(c->emb_qtype))
+    SI_FAIL(SI_ERR_INVALID, "hidden/intermediate must be multiples of the quant block size");
+  if (c->hidden % 16 || c->intermediate % 16) SI_FAIL(SI_ERR_INVALID, "hidden and intermediate must be multiples of 16");
+  if (c->hidden > SI_MAX_K || c->intermediate > SI_MAX_K) SI_FAIL(SI_ERR_UNSUPPORTED, "hidden/intermediate above %d", SI_MAX_K);
+  return SI_OK;
+}
+
+// Splits of the attention kernel for batch B: enough CTAs for two per SM,
+// and at most 1024 positions per split at the longest context.
+int attn_splits(const si_model* m, int B) {
+  const int want = (2 * m->c->sm_count + B * m->cfg.n_kv_heads - 1) / (B * m->cfg.n_kv_heads);
+  const int need = (m->cfg.max_seq + 1023) / 1024;
+  return std::min(std::max(want, need), m->splits_max);
+}
+
+int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int B, bool pdl) {
+  const si_model_config& c = m->cfg;
+  AttnArgs a;
+  a.params = m->dparams;
+  a.layer = layer;
+  a.max_batch = c.max_batch;
+  a.max_seq = c.max_seq;
+  a.nh = c.n_heads;
+  a.kcache = m->kcache;
+  a.vcache = m->vcache;
+  a.qkv = qkv;
+  a.qkv_ld = m->qkv_rows;
+  a.rope = m->rope;
+  a.scale = 1.0f / sqrtf((float)c.head_dim);  // Transformer.cs:101
+  const int S = attn_splits(m, B);
+  a.chunk_max = (c.max_seq + S - 1) / S;
+  a.part_o = m->part_o;
+  a.part_ml = m->part_ml;
+  a.counters = m->attn_cnt;
+  a.out = out;
+  a.out_ld = (int64_t)c.n_heads * c.head_dim;
+  a.err = m->c->dev_err;
+  return launch_attn(m->c->stream, a, m->G, S, B, c.n_kv_heads, pdl);
+}
+
+// The whole decode step on the context stream (eager or under capture).
+int enqueue_step(si_model* m, int B) {
+  const si_model_config& c = m->cfg;
+  cudaStream_t s = m->c->stream;
+  const int h = c.hidden, inter = c.intermediate, qd = c.n_heads * c.head_dim;
+  const QmvBuffers qb = m->c->qmv();
+  SI_CUDA(cudaMemcpyAsync(m->dparams, m->hparams, sizeof(StepParams), cudaMemcpyHostToDevice, s));
+  {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = cfg_of(s, dim3((h + 255) / 256, B), dim3(256), 0, false, attr);
+    SI_CUDA(cudaLaunchKernelEx(&cfg, k_embed, (const StepParams*)m->dparams, m->emb->qtype,
+                               (const uint8_t*)m->emb->dev, m->emb->nblk, (int64_t)c.vocab, h, m->x));
+  }
+  for (int l = 0; l < c.n_layers; l++) {
+    SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
+                       nullptr, m->xprep, true));
+    SI_TRY(launch_qmv(s, m->wqkv[l], m->xprep, B, m->qkv, SI_EPI_STORE, qb, true));
+    SI_TRY(enqueue_attention(m, l, m->qkv, m->attn, B, true));
+    SI_TRY(launch_prep(s, m->attn, qd, nullptr, nullptr, 0.f, SI_PREP_PLAIN, qd, B, nullptr, m->xprep, true));
+    SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
+    SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
+                       nullptr, m->xprep, true));
+    SI_TRY(launch_qmv(s, m->wgu[l], m->xprep, B, m->gu, SI_EPI_STORE, qb, true));
+    SI_TRY(launch_prep(s, m->gu, 2 * inter, m->gu + inter, nullptr, 0.f, SI_PREP_SILU_MUL, inter, B, nullptr,
+                       m->xprep, true));
+    SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
+  }
+  SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, -1, SI_T_FINAL_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
+                     nullptr, m->xprep, true));
+  SI_TRY(launch_qmv(s, m->lm_head, m->xprep, B, m->logits, SI_EPI_STORE, qb, true));
+  {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = cfg_of(s, dim3(B), dim3(1024), 0, true, attr);
+    SI_CUDA(cudaLaunchKernelEx(&cfg, k_argmax, (const float*)m->logits, (int64_t)c.vocab, m->argmax));
+  }
+  SI_CUDA(cudaMemcpyAsync(m->hargmax, m->argmax, sizeof(int) * B, cudaMemcpyDeviceToHost, s));
+  return SI_OK;
+}
+
+int get_graph(si_model* m, int B, cudaGraphExec_t* out) {
+  auto it = m->graphs.find(B);
+  if (it != m->graphs.end()) {
+    *out = it->second;
+    return SI_OK;
+  }
+  cudaStream_t s = m->c->stream;
+  SI_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  int st = enqueue_step(m, B);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s, &g);
+  if (st != SI_OK) {
+    if (g) cudaGraphDestroy(g);
+    return st;
+  }
+  if (e != cudaSuccess) SI_FAIL(SI_ERR_CUDA, "decode-step capture failed: %s", cudaGetErrorString(e));
+  cudaGraphExec_t ge = nullptr;
+  e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) SI_FAIL(SI_ERR_CUDA, "decode-step graph instantiation failed: %s", cudaGetErrorString(e));
+  m->graphs[B] = ge;
+  *out = ge;
+  return SI_OK;
+}
+
+// Host-side cos/sin table with exactly the float arithmetic of
+// RotaryEmbedding.ApplyToHead (RotaryEmbedding.cs:42-61): freq =
+// 1 / powf(theta, i / headDim), angle = position * freq.
+void fill_rope(std::vector<float>& t, int npos, int hd, float theta) {
+  t.resize((size_t)npos * hd);
+  for (int p = 0; p < npos; p++)
+    for (int i = 0; i < hd; i += 2) {
+      const float fi = (float)i / (float)hd;
+      const float freq = 1.0f / powf(theta, fi);
+      const float angle = (float)p * freq;
+      t[((size_t)p * (hd / 2) + i / 2) * 2 + 0] = cosf(angle);
+      t[((size_t)p * (hd / 2) + i / 2) * 2 + 1] = sinf(angle);
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+SI_EXPORT int si_model_tensor_recipe(const si_model_config* c, int layer, int t, uint64_t* tag, int* qt,
+                                     int* recipe, float* sigma, float* mean, int64_t* rows, int64_t* cols) {
+  clear_error();
+  SI_TRY(check_config(c));
+  const int64_t hd = c->head_dim, qr = (int64_t)c->n_heads * hd, kr = (int64_t)c->n_kv_heads * hd;
+  int64_t r = 0, k = 0;
+  int q = c->weight_qtype, rc = SI_SYNTH_MODEL;
+  float mu = 0.f, sg = 0.f;
+  uint64_t tg;
+  if (layer < 0) {
+    tg = (uint64_t)(t - SI_T_EMB + 1);
+    if (t == SI_T_EMB) { q = c->emb_qtype; r = c->vocab; k = c->hidden; }
+    else if (t == SI_T_LM_HEAD) { q = c->lm_head_qtype; r = c->vocab; k = c->hidden; rc = SI_SYNTH_PLAIN; }
+    else if (t == SI_T_FINAL_NORM) { q = SI_F32; r = 1; k = c->hidden; }
+    else SI_FAIL(SI_ERR_INVALID, "unknown global tensor %d", t);
+  } else {
+    if (layer >= c->n_layers) SI_FAIL(SI_ERR_INVALID, "layer %d out of range", layer);
+    tg = 1000ull * (uint64_t)(layer + 1) + (uint64_t)t;
+    switch (t) {
+      case SI_T_Q: r = qr; k = c->hidden; break;
+      case SI_T_K: case SI_T_V: r = kr; k = c->hidden; break;
+      case SI_T_O: r = c->hidden; k = qr; break;
+      case SI_T_GATE: case SI_T_UP: r = c->intermediate; k = c->hidden; break;
+      case SI_T_DOWN: r = c->hidden; k = c->intermediate; break;
+      case SI_T_ATTN_NORM: case SI_T_FFN_NORM: q = SI_F32; r = 1; k = c->hidden; break;
+      default: SI_FAIL(SI_ERR_INVALID, "unknown layer tensor %d", t);
+    }
+  }
+  if (q == SI_F32) {
+    mu = 1.0f;
+    sg = 0.01f;
+    rc = 0;
+  } else if (t == SI_T_EMB) {
+    sg = q == SI_Q4_K ? 1.0f / 23.3f : recipe_sigma(q, rc, 1);
+  } else {
+    sg = recipe_sigma(q, rc, k);
+  }
+  if (tag) *tag = tg;
+  if (qt) *qt = q;
+  if (recipe) *recipe = rc;
+  if (sigma) *sigma = sg;
+  if (mean) *mean = mu;
+  if (rows) *rows = r;
+  if (cols) *cols = k;
+  return SI_OK;
+}
+
+SI_EXPORT uint64_t si_model_kv_tag(int layer, int seq, int is_value) {
+  return 0x4B560000ull + ((uint64_t)layer * 64 + (uint64_t)seq) * 2 + (uint64_t)(is_value != 0);
+}
+
+SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model** out) {
+  clear_error();
+  if (!ctx || !out) SI_FAIL(SI_ERR_INVALID, "si_model_create: NULL argument");
+  *out = nullptr;
+  SI_TRY(check_config(cfg));
+  SI_TRY(bind_device(ctx));
+  si_model* m = new si_model();
+  m->c = ctx;
+  m->cfg = *cfg;
+  const si_model_config& c = m->cfg;
+  m->G = c.n_heads / c.n_kv_heads;
+  m->qkv_rows = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+  const int qd = c.n_heads * c.head_dim;
+  m->Kmax = std::max(std::max(c.hidden, c.intermediate), qd);
+  const int B = c.max_batch;
+  int st = SI_OK;
+  auto fail = [&](int code) {
+    si_model_free(m);
+    return code;
+  };
+  m->wqkv.assign(c.n_layers, nullptr);
+  m->wo.assign(c.n_layers, nullptr);
+  m->wgu.assign(c.n_layers, nullptr);
+  m->wdown.assign(c.n_layers, nullptr);
+  for (int l = 0; l < c.n_layers && st == SI_OK; l++) {
+    st = make_weight(m, c.weight_qtype, m->qkv_rows, c.hidden, &m->wqkv[l]);
+    if (st == SI_OK) st = make_weight(m, c.weight_qtype, c.hidden, qd, &m->wo[l]);
+    if (st == SI_OK) st = make_weight(m, c.weight_qtype, 2 * (int64_t)c.intermediate, c.hidden, &m->wgu[l]);
+    if (st == SI_OK) st = make_weight(m, c.weight_qtype, c.hidden, c.intermediate, &m->wdown[l]);
+  }
+  if (st == SI_OK) st = make_weight(m, c.emb_qtype, c.vocab, c.hidden, &m->emb);
+  if (st == SI_OK) st = make_weight(m, c.lm_head_qtype, c.vocab, c.hidden, &m->lm_head);
+  if (st != SI_OK) return fail(st);
+  const int64_t h = c.hidden;
+  const size_t kv_elems = (size_t)c.n_layers * B * c.n_kv_heads * c.max_seq * c.head_dim;
+  m->splits_max = std::max((2 * ctx->sm_count + c.n_kv_heads - 1) / c.n_kv_heads, (c.max_seq + 1023) / 1024);
+  m->chunk_max = 1024;
+  void* p;
+#define ALLOC(field, bytes)                                      \
+  do {                                                           \
+    if ((st = dev_alloc(m, &p, (size_t)(bytes))) != SI_OK) return fail(st); \
+    m->field = (decltype(m->field))p;                            \
+  } while (0)
+  ALLOC(norms, ((int64_t)c.n_layers * 2 + 1) * h * 4);
+  ALLOC(kcache, kv_elems * 2);
+  ALLOC(vcache, kv_elems * 2);
+  ALLOC(rope, (size_t)c.max_seq * c.head_dim * 4);
+  ALLOC(x, (size_t)B * h * 4);
+  ALLOC(qkv, (size_t)B * m->qkv_rows * 4);
+  ALLOC(attn, (size_t)B * qd * 4);
+  ALLOC(gu, (size_t)B * 2 * c.intermediate * 4);
+  ALLOC(logits, (size_t)B * c.vocab * 4);
+  ALLOC(argmax, (size_t)SI_MAX_BATCH * 4);
+  ALLOC(xprep, xprep_bytes(m->Kmax, B));
+  ALLOC(part_o, (size_t)B * c.n_heads * m->splits_max * c.head_dim * 4);
+  ALLOC(part_ml, (size_t)B * c.n_heads * m->splits_max * 2 * 4);
+  ALLOC(attn_cnt, (size_t)B * c.n_kv_heads * 4);
+  ALLOC(dparams, sizeof(StepParams));
+#undef ALLOC
+  cudaError_t e = cudaMemset(m->attn_cnt, 0, (size_t)B * c.n_kv_heads * 4);
+  if (e == cudaSuccess) e = cudaMemset(m->kcache, 0, kv_elems * 2);
+  if (e == cudaSuccess) e = cudaMemset(m->vcache, 0, kv_elems * 2);
+  if (e == cudaSuccess) e = cudaMallocHost(&m->hparams, sizeof(StepParams));
+  if (e == cudaSuccess) e = cudaMallocHost(&m->hargmax, sizeof(int) * SI_MAX_BATCH);
+  if (e != cudaSuccess) {
+    si::set_error("model set-up failed: %s", cudaGetErrorString(e));
+    return fail(SI_ERR_CUDA);
+  }
+  std::vector<float> rope;
+  fill_rope(rope, c.max_seq, c.head_dim, c.rope_theta);
+  e = cudaMemcpy(m->rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    si::set_error("rope table upload failed: %s", cudaGetErrorString(e));
+    return fail(SI_ERR_CUDA);
+  }
+  for (si_weight* w : {m->wqkv[0], m->wo[0], m->wgu[0], m->wdown[0], m->lm_head})
+    if ((st = ensure_qmv_scratch(ctx, w)) != SI_OK) return fail(st);
+  *out = m;
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_free(si_model* m) {
+  clear_error();
+  if (!m) return SI_OK;
+  cudaSetDevice(m->c->device);
+  cudaStreamSynchronize(m->c->stream);
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto* v : {&m->wqkv, &m->wo, &m->wgu, &m->wdown})
+    for (si_weight* w : *v) si_weight_free(w);
+  si_weight_free(m->emb);
+  si_weight_free(m->lm_head);
+  for (void* p : m->allocs) cudaFree(p);
+  if (m->hparams) cudaFreeHost(m->hparams);
+  if (m->hargmax) cudaFreeHost(m->hargmax);
+  delete m;
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_set_tensor(si_model* m, int layer, int t, const void* host) {
+  clear_error();
+  if (!m || !host) SI_FAIL(SI_ERR_INVALID, "si_model_set_tensor: NULL argument");
+  si_ctx* c = m->c;
+  SI_TRY(bind_device(c));
+  if (t == SI_T_ATTN_NORM || t == SI_T_FFN_NORM || t == SI_T_FINAL_NORM) {
+    if ((layer < 0) != (t == SI_T_FINAL_NORM)) SI_FAIL(SI_ERR_INVALID, "norm tensor %d with layer %d", t, layer);
+    if (layer >= m->cfg.n_layers) SI_FAIL(SI_ERR_INVALID, "layer %d out of range", layer);
+    SI_CUDA(cudaMemcpy(norm_ptr(m, layer, t), host, (size_t)m->cfg.hidden * 4, cudaMemcpyHostToDevice));
+    return SI_OK;
+  }
+  si_weight* w;
+  int64_t row0, rows, cols;
+  SI_TRY(tensor_slot(m, layer, t, &w, &row0, &rows, &cols));
+  const int64_t rb = w->nblk * gguf_block_bytes(w->qtype);
+  const int64_t cr = std::max<int64_t>(16, ((64ll << 20) / rb) / 16 * 16);
+  SI_TRY(ensure(c->stage[0], (size_t)(std::min(cr, rows) * rb)));
+  for (int64_t r = 0; r < rows; r += cr) {
+    const int64_t nr = std::min(cr, rows - r);
+    SI_CUDA(cudaMemcpyAsync(c->stage[0].ptr, (const uint8_t*)host + r * rb, (size_t)(nr * rb),
+                            cudaMemcpyHostToDevice, c->stream));
+    SI_TRY(launch_repack(c, w->qtype, (const uint8_t*)c->stage[0].ptr, row0 + rows, w->cols, row0 + r, nr, w->dev));
+    SI_CUDA(cudaStreamSynchronize(c->stream));
+  }
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_synth(si_model* m, uint64_t seed) {
+  clear_error();
+  if (!m) SI_FAIL(SI_ERR_INVALID, "si_model_synth: NULL model");
+  si_ctx* c = m->c;
+  SI_TRY(bind_device(c));
+  const si_model_config& cfg = m->cfg;
+  std::vector<std::pair<int, int>> items;
+  for (int l = 0; l < cfg.n_layers; l++)
+    for (int t = SI_T_Q; t <= SI_T_FFN_NORM; t++) items.push_back({l, t});
+  for (int t : {SI_T_EMB, SI_T_LM_HEAD, SI_T_FINAL_NORM}) items.push_back({-1, t});
+  for (auto& it : items) {
+    const int layer = it.first, t = it.second;
+    uint64_t tag;
+    int qt, rc;
+    float sg, mu;
+    int64_t rows, cols;
+    SI_TRY(si_model_tensor_recipe(&cfg, layer, t, &tag, &qt, &rc, &sg, &mu, &rows, &cols));
+    if (qt == SI_F32) {
+      const int64_t n = cols;
+      k_f32_synth<<<(unsigned)((n + 255) / 256), 256, 0, c->stream>>>(norm_ptr(m, layer, t), si_key(seed, tag), n,
+                                                                      mu, sg);
+      SI_CUDA(cudaGetLastError());
+      continue;
+    }
+    si_weight* w;
+    int64_t row0, r2, c2;
+    SI_TRY(tensor_slot(m, layer, t, &w, &row0, &r2, &c2));
+    const int64_t rb = w->nblk * gguf_block_bytes(qt);
+    const int64_t cr = std::max<int64_t>(16, ((64ll << 20) / rb) / 16 * 16);
+    SI_TRY(ensure(c->stage[0], (size_t)(std::min(cr, rows) * rb)));
+    for (int64_t r = 0; r < rows; r += cr) {
+      const int64_t nr = std::min(cr, rows - r);
+      SI_TRY(launch_synth_blocks(c, qt, seed, tag, rc, sg, r * w->nblk, nr * w->nblk, (uint8_t*)c->stage[0].ptr));
+      SI_TRY(launch_repack(c, qt, (const uint8_t*)c->stage[0].ptr, row0 + rows, w->cols, row0 + r, nr, w->dev));
+      SI_CUDA(cudaStreamSynchronize(c->stream));
+    }
+  }
+  SI_CUDA(cudaStreamSynchronize(c->stream));
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_kv_synth(si_model* m, int len, uint64_t seed) {
+  clear_error();
+  if (!m) SI_FAIL(SI_ERR_INVALID, "si_model_kv_synth: NULL model");
+  const si_model_config& c = m->cfg;
+  if (len < 0 || len > c.max_seq) SI_FAIL(SI_ERR_INVALID, "kv length %d outside [0, %d]", len, c.max_seq);
+  SI_TRY(bind_device(m->c));
+  const int64_t per = (int64_t)c.n_kv_heads * c.max_seq * c.head_dim;
+  const int64_t n = (int64_t)len * c.n_kv_heads * c.head_dim;
+  if (n == 0) return SI_OK;
+  for (int l = 0; l < c.n_layers; l++)
+    for (int b = 0; b < c.max_batch; b++) {
+      const int64_t off = ((int64_t)l * c.max_batch + b) * per;
+      for (int v = 0; v < 2; v++) {
+        __half* base = (v ? m->vcache : m->kcache) + off;
+        k_kv_synth<<<(unsigned)((n + 255) / 256), 256, 0, m->c->stream>>>(
+            base, si_key(seed, si_model_kv_tag(l, b, v)), len, c.n_kv_heads, c.max_seq);
+      }
+    }
+  SI_CUDA(cudaGetLastError());
+  SI_CUDA(cudaStreamSynchronize(m->c->stream));
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_kv_write(si_model* m, int layer, int seq, int pos0, int n, const uint16_t* k,
+                                const uint16_t* v) {
+  clear_error();
+  if (!m || !k || !v) SI_FAIL(SI_ERR_INVALID, "si_model_kv_write: NULL argument");
+  const si_model_config& c = m->cfg;
+  if (layer < 0 || layer >= c.n_layers || seq < 0 || seq >= c.max_batch || pos0 < 0 || n < 0 ||
+      pos0 + n > c.max_seq)
+    SI_FAIL(SI_ERR_INVALID, "si_model_kv_write: range outside the cache");
+  si_ctx* ctx = m->c;
+  SI_TRY(bind_device(ctx));
+  const size_t bytes = (size_t)n * c.n_kv_heads * c.head_dim * 2;
+  if (!bytes) return SI_OK;
+  SI_TRY(ensure(ctx->stage[3], bytes));
+  const int64_t per = (int64_t)c.n_kv_heads * c.max_seq * c.head_dim;
+  const int64_t off = ((int64_t)layer * c.max_batch + seq) * per;
+  const int64_t cnt = (int64_t)n * c.n_kv_heads * c.head_dim;
+  for (int which = 0; which < 2; which++) {
+    SI_CUDA(cudaMemcpyAsync(ctx->stage[3].ptr, which ? v : k, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    k_kv_scatter<<<(unsigned)((cnt + 255) / 256), 256, 0, ctx->stream>>>(
+        (which ? m->vcache : m->kcache) + off, (const uint16_t*)ctx->stage[3].ptr, pos0, n, c.n_kv_heads, c.max_seq);
+    SI_CUDA(cudaGetLastError());
+    SI_CUDA(cudaStreamSynchronize(ctx->stream));
+  }
+  return SI_OK;
+}
+
+SI_EXPORT int si_decode_step(si_model* m, const int* tokens, int batch, int pos, int* argmax_out,
+                             float* logits_out) {
+  clear_error();
+  if (!m || !tokens || !argmax_out) SI_FAIL(SI_ERR_INVALID, "si_decode_step: NULL argument");
+  const si_model_config& c = m->cfg;
+  if (batch < 1 || batch > c.max_batch) SI_FAIL(SI_ERR_INVALID, "batch %d outside 1..%d", batch, c.max_batch);
+  if (pos < 0 || pos >= c.max_seq)
+    SI_FAIL(SI_ERR_INVALID, "position %d exceeds max sequence length %d", pos, c.max_seq);  // KVCache.cs:48-49
+  for (int b = 0; b < batch; b++)
+    if (tokens[b] < 0 || tokens[b] >= c.vocab) SI_FAIL(SI_ERR_INVALID, "token id %d outside the vocabulary", tokens[b]);
+  SI_TRY(bind_device(m->c));
+  cudaGraphExec_t ge;
+  SI_TRY(get_graph(m, batch, &ge));
+  m->hparams->pos = pos;
+  m->hparams->batch = batch;
+  for (int b = 0; b < batch; b++) m->hparams->tokens[b] = tokens[b];
+  SI_CUDA(cudaGraphLaunch(ge, m->c->stream));
+  if (logits_out)
+    SI_CUDA(cudaMemcpyAsync(logits_out, m->logits, (size_t)batch * c.vocab * 4, cudaMemcpyDeviceToHost, m->c->stream));
+  SI_CUDA(cudaStreamSynchronize(m->c->stream));
+  SI_TRY(check_device_errors(m->c));
+  for (int b = 0; b < batch; b++) argmax_out[b] = m->hargmax[b];
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_attention(si_model* m, int layer, const float* qkv, float* out, int batch, int pos) {
+  clear_error();
+  if (!m || !qkv || !out) SI_FAIL(SI_ERR_INVALID, "si_model_attention: NULL argument");
+  const si_model_config& c = m->cfg;
+  if (layer < 0 || layer >= c.n_layers || batch < 1 || batch > c.max_batch || pos < 0 || pos >= c.max_seq)
+    SI_FAIL(SI_ERR_INVALID, "si_model_attention: bad layer/batch/position");
+  SI_TRY(bind_device(m->c));
+  m->hparams->pos = pos;
+  m->hparams->batch = batch;
+  SI_CUDA(cudaMemcpyAsync(m->dparams, m->hparams, sizeof(StepParams), cudaMemcpyHostToDevice, m->c->stream));
+  SI_TRY(enqueue_attention(m, layer, qkv, out, batch, false));
+  SI_CUDA(cudaStreamSynchronize(m->c->stream));
+  return check_device_errors(m->c);
+}
+
+}  // extern "C"

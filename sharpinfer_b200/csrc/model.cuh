@@ -1,0 +1,36 @@
+// Decode-model internals shared by model.cu and attn.cu.
+#pragma once
+#include "common.cuh"
+
+namespace si {
+
+// Per-step parameters, copied from pinned host memory at the start of each
+// decode-step graph.
+struct StepParams {
+  int pos;
+  int batch;
+  int tokens[SI_MAX_BATCH];
+};
+
+struct AttnArgs {
+  const StepParams* params;
+  int layer, max_batch, max_seq, nh;
+  __half* kcache;
+  __half* vcache;
+  const float* qkv;
+  int64_t qkv_ld;
+  const float* rope;  // [max_seq][head_dim/2][2] cos, sin
+  float scale;        // 1 / sqrtf(head_dim)
+  int chunk_max;      // positions per split at the longest context
+  float* part_o;      // [batch][nh][splits][head_dim]
+  float* part_ml;     // [batch][nh][splits][2]
+  int* counters;      // [batch][nkv], zero between launches
+  float* out;
+  int64_t out_ld;
+  int* err;
+};
+
+size_t attn_smem_bytes(int G, int chunk_max);
+int launch_attn(cudaStream_t s, const AttnArgs& a, int G, int splits, int batch, int nkv, bool pdl);
+
+}  // namespace si

@@ -33,6 +33,7 @@
 #include <stdio.h>
 
 #include "common.cuh"
+#include "quantfmt.cuh"
 #include "synth.h"
 
 namespace si {
@@ -159,94 +160,15 @@ __global__ void k_repack(int qt, const uint8_t* __restrict__ src, int64_t row0, 
   dst[(T * nblk + b) * wpt + wi] = out;
 }
 
-// ---- reading the device layout back (dequantisation) ----
-
-__device__ __forceinline__ int frag_lane_pos(int k, int* pos) {
-  // k in [0,16) -> (t, slot) with slot 0..3 for k = 2t, 2t+1, 2t+8, 2t+9
-  int hi = k >> 3, kk = k & 7;
-  *pos = 2 * hi + (kk & 1);
-  return kk >> 1;
-}
-
-__device__ __forceinline__ uint32_t dev_q4k_code(const uint32_t* tbw, int ri, int e) {
-  int kt = e >> 4, pos, t = frag_lane_pos(e & 15, &pos);
-  int g = ri & 7, upper = ri >> 3, lane = 4 * g + t;
-  uint32_t w = tbw[64 + (kt >> 2) * 128 + lane * 4 + (kt & 3)];
-  const int sh0[4] = {0, 16, 8, 24}, sh1[4] = {4, 20, 12, 28};
-  return (w >> (upper ? sh1[pos] : sh0[pos])) & 0xF;
-}
-
-__device__ __forceinline__ uint32_t dev_q6k_code(const uint32_t* tbw, int ri, int e) {
-  int kt = e >> 4, pos, t = frag_lane_pos(e & 15, &pos);
-  int g = ri & 7, upper = ri >> 3, lane = 4 * g + t;
-  int c = kt >> 2, i = kt & 3;
-  uint32_t lw = tbw[c * 192 + lane * 4 + i];
-  uint32_t hw = tbw[c * 192 + 128 + lane * 2 + (i >> 1)];
-  const int sh0[4] = {0, 16, 8, 24}, sh1[4] = {4, 20, 12, 28};
-  const int hb0[4] = {4, 20, 12, 28}, hb1[4] = {8, 24, 0, 16};
-  uint32_t lo = (lw >> (upper ? sh1[pos] : sh0[pos])) & 0xF;
-  uint32_t hi = (hw >> ((upper ? hb1[pos] : hb0[pos]) + 2 * (i & 1))) & 3;
-  return lo | (hi << 4);
-}
-
-__device__ __forceinline__ int dev_q80_code(const uint32_t* tbw, int ri, int e) {
-  int kt = e >> 4, pos, t = frag_lane_pos(e & 15, &pos);
-  int g = ri & 7, upper = ri >> 3, lane = 4 * g + t;
-  uint32_t w = tbw[lane * 4 + kt * 2 + upper];
-  return (int)(int8_t)((w >> (8 * pos)) & 0xFF);
-}
-
-__device__ __forceinline__ float h2f(uint32_t bits16) {
-  return __half2float(__ushort_as_half((unsigned short)bits16));
-}
-
 // One thread per (row, quant block): writes the block's elements in
 // reference order with the reference's rounding (no FMA contraction).
 __global__ void k_dequant(int qt, const uint8_t* __restrict__ W, int64_t rows, int64_t nblk,
                           float* __restrict__ out) {
   int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= rows * nblk) return;
-  int64_t r = idx / nblk, b = idx % nblk;
-  int64_t T = r >> 4;
-  int ri = (int)(r & 15);
-  if (qt == SI_Q4_K) {
-    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 2304);
-    const uint8_t* hdr = (const uint8_t*)(tbw + 4 * ri);
-    float d = h2f(hdr[0] | (hdr[1] << 8)), dmin = h2f(hdr[2] | (hdr[3] << 8));
-    const uint8_t* q = hdr + 4;
-    float* o = out + r * nblk * 256 + b * 256;
-    for (int j = 0; j < 8; j++) {  // GetScaleMinK4 (Quantization.cs:302-314)
-      uint32_t sc, mn;
-      if (j < 4) {
-        sc = q[j] & 63;
-        mn = q[j + 4] & 63;
-      } else {
-        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
-        mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
-      }
-      float d1 = __fmul_rn(d, (float)sc), m1f = __fmul_rn(dmin, (float)mn);
-      for (int l = 0; l < 32; l++) {
-        int e = 32 * j + l;
-        o[e] = __fsub_rn(__fmul_rn(d1, (float)dev_q4k_code(tbw, ri, e)), m1f);
-      }
-    }
-  } else if (qt == SI_Q6_K) {
-    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 3360);
-    const int8_t* scales = (const int8_t*)(tbw + 768) + 16 * ri;
-    uint32_t dw = tbw[832 + (ri & 7)];
-    float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
-    float* o = out + r * nblk * 256 + b * 256;
-    for (int e = 0; e < 256; e++) {
-      float ds = __fmul_rn(d, (float)scales[e >> 4]);
-      o[e] = __fmul_rn(ds, (float)((int)dev_q6k_code(tbw, ri, e) - 32));
-    }
-  } else {
-    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 544);
-    uint32_t dw = tbw[128 + (ri & 7)];
-    float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
-    float* o = out + r * nblk * 32 + b * 32;
-    for (int e = 0; e < 32; e++) o[e] = __fmul_rn((float)dev_q80_code(tbw, ri, e), d);
-  }
+  const int64_t r = idx / nblk, b = idx % nblk;
+  const int be = qt == SI_Q8_0 ? 32 : 256;
+  dequant_block(qt, W, nblk, r, b, out + r * nblk * be + b * be);
 }
 
 __global__ void k_synth_blocks(int qt, uint64_t key, int recipe, float sigma, int64_t blk0,

@@ -1,0 +1,111 @@
+"""Decode model over the C ABI (si_model_*): a Llama/Mistral-architecture
+transformer resident on one B200, stepped one token per sequence at a time
+(Transformer.Forward, src/SharpInfer.Core/Layers/Transformer.cs:67-162).
+"""
+import ctypes
+
+import numpy as np
+
+from . import native as N
+
+
+def config(n_layers, hidden, intermediate, n_heads, n_kv_heads, vocab, max_seq, max_batch=1,
+           head_dim=128, rms_eps=1e-5, rope_theta=500000.0, weight_qtype=N.SI_Q4_K,
+           lm_head_qtype=N.SI_Q6_K, emb_qtype=N.SI_Q4_K):
+    return N.ModelConfig(n_layers, hidden, intermediate, n_heads, n_kv_heads, head_dim, vocab, max_seq,
+                         max_batch, rms_eps, rope_theta, weight_qtype, lm_head_qtype, emb_qtype)
+
+
+def llama3_8b(max_seq=4160, max_batch=1):
+    """Llama-3-8B architecture: 32 layers, hidden 4096, 32 q / 8 kv heads, FFN 14336, vocab 128256."""
+    return config(32, 4096, 14336, 32, 8, 128256, max_seq, max_batch)
+
+
+def llama3_70b(max_seq=8256, max_batch=1):
+    """Llama-3-70B architecture: 80 layers, hidden 8192, 64 q / 8 kv heads, FFN 28672, vocab 128256."""
+    return config(80, 8192, 28672, 64, 8, 128256, max_seq, max_batch)
+
+
+def tensor_recipe(cfg, layer, tensor):
+    """(tag, qtype, recipe, sigma, mean, rows, cols) of a synthetic tensor."""
+    tag, qt, rc = ctypes.c_uint64(), ctypes.c_int(), ctypes.c_int()
+    sg, mu = ctypes.c_float(), ctypes.c_float()
+    rows, cols = ctypes.c_int64(), ctypes.c_int64()
+    N.call("si_model_tensor_recipe", ctypes.byref(cfg), layer, tensor, ctypes.byref(tag), ctypes.byref(qt),
+           ctypes.byref(rc), ctypes.byref(sg), ctypes.byref(mu), ctypes.byref(rows), ctypes.byref(cols))
+    return tag.value, qt.value, rc.value, sg.value, mu.value, rows.value, cols.value
+
+
+def host_tensor(cfg, seed, layer, tensor):
+    """Host bytes (GGUF blocks, or f32 norms) identical to what si_model_synth puts on the device."""
+    from .backend import synth_blocks_host, synth_f32_host
+    tag, qt, rc, sg, mu, rows, cols = tensor_recipe(cfg, layer, tensor)
+    if qt == N.SI_F32:
+        return synth_f32_host(cols, seed, tag, mu, sg)
+    return synth_blocks_host(qt, rows, cols, seed, tag, rc, sg)
+
+
+def host_kv(cfg, seed, layer, seq, length):
+    """f16 K and V of cache positions [0, length) in the reference layout [pos][kv head][dim]."""
+    from .backend import synth_f16_host
+    n = length * cfg.n_kv_heads * cfg.head_dim
+    lib = N.load()
+    k = synth_f16_host(n, seed, lib.si_model_kv_tag(layer, seq, 0))
+    v = synth_f16_host(n, seed, lib.si_model_kv_tag(layer, seq, 1))
+    return k, v
+
+
+class DecodeModel:
+    """si_model*: weights, f16 KV cache and the graph-captured decode step."""
+
+    def __init__(self, ctx, cfg):
+        self.ctx, self.cfg = ctx, cfg
+        h = ctypes.c_void_p()
+        N.call("si_model_create", ctx.handle, ctypes.byref(cfg), ctypes.byref(h))
+        self.handle = h
+
+    def free(self):
+        if self.handle:
+            N.call("si_model_free", self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+    def synth(self, seed):
+        N.call("si_model_synth", self.handle, seed)
+
+    def set_tensor(self, layer, tensor, data):
+        data = np.ascontiguousarray(data)
+        N.call("si_model_set_tensor", self.handle, layer, tensor, N.ptr(data))
+
+    def kv_synth(self, length, seed):
+        N.call("si_model_kv_synth", self.handle, length, seed)
+
+    def kv_write(self, layer, seq, pos0, k, v):
+        k = np.ascontiguousarray(k, np.uint16)
+        v = np.ascontiguousarray(v, np.uint16)
+        n = k.size // (self.cfg.n_kv_heads * self.cfg.head_dim)
+        N.call("si_model_kv_write", self.handle, layer, seq, pos0, n, N.ptr(k), N.ptr(v))
+
+    def step(self, tokens, pos, logits=False):
+        """Greedy next token of each sequence (and optionally the logits)."""
+        tok = np.ascontiguousarray(tokens, np.int32).ravel()
+        out = np.empty(tok.size, np.int32)
+        lg = np.empty((tok.size, self.cfg.vocab), np.float32) if logits else None
+        N.call("si_decode_step", self.handle, N.ptr(tok), tok.size, pos, N.ptr(out), N.ptr(lg))
+        return (out, lg) if logits else out
+
+    def attention(self, layer, qkv, pos, out=None):
+        """Attention of one layer for qkv [batch][(nh + 2 nkv) * hd] (CUDA f32 tensor)."""
+        import torch
+        batch = qkv.shape[0]
+        if out is None:
+            out = torch.empty((batch, self.cfg.n_heads * self.cfg.head_dim), dtype=torch.float32,
+                              device=qkv.device)
+        torch.cuda.synchronize()
+        N.call("si_model_attention", self.handle, layer, N.ptr(qkv), N.ptr(out), batch, pos)
+        return out

@@ -24,6 +24,19 @@ _u64 = ctypes.c_uint64
 _f32 = ctypes.c_float
 
 
+class ModelConfig(ctypes.Structure):
+    """si_model_config (field names of the reference's ModelConfig)."""
+    _fields_ = [("n_layers", ctypes.c_int), ("hidden", ctypes.c_int), ("intermediate", ctypes.c_int),
+                ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("vocab", ctypes.c_int), ("max_seq", ctypes.c_int), ("max_batch", ctypes.c_int),
+                ("rms_eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("weight_qtype", ctypes.c_int),
+                ("lm_head_qtype", ctypes.c_int), ("emb_qtype", ctypes.c_int)]
+
+
+T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_ATTN_NORM, T_FFN_NORM = range(9)
+T_EMB, T_LM_HEAD, T_FINAL_NORM = 100, 101, 102
+
+
 class SIError(RuntimeError):
     """A sharpinfer_b200 call returned a non-zero si_status."""
 
@@ -54,6 +67,18 @@ _SIGS = {
     "si_act_prepare": (_i32, [_c_p, _c_p, _i64, _i32]),
     "si_qmatvec_prepared": (_i32, [_c_p, _c_p, _c_p, _i32, _i32]),
     "si_qmatvec_host": (_i32, [_c_p, _c_p, _c_p, _c_p, _i32]),
+    "si_model_create": (_i32, [_c_p, ctypes.POINTER(ModelConfig), ctypes.POINTER(_c_p)]),
+    "si_model_free": (_i32, [_c_p]),
+    "si_model_set_tensor": (_i32, [_c_p, _i32, _i32, _c_p]),
+    "si_model_synth": (_i32, [_c_p, _u64]),
+    "si_model_tensor_recipe": (_i32, [ctypes.POINTER(ModelConfig), _i32, _i32, ctypes.POINTER(_u64),
+                                      ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_f32),
+                                      ctypes.POINTER(_f32), ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "si_model_kv_synth": (_i32, [_c_p, _i32, _u64]),
+    "si_model_kv_tag": (_u64, [_i32, _i32, _i32]),
+    "si_model_kv_write": (_i32, [_c_p, _i32, _i32, _i32, _i32, _c_p, _c_p]),
+    "si_decode_step": (_i32, [_c_p, _c_p, _i32, _i32, _c_p, _c_p]),
+    "si_model_attention": (_i32, [_c_p, _i32, _c_p, _c_p, _i32, _i32]),
 }
 
 _lib = None
