@@ -233,6 +233,14 @@ SI_EXPORT int si_model_kv_write(si_model* m, int layer, int seq, int pos0, int n
 SI_EXPORT int si_decode_step(si_model* m, const int* tokens_host, int batch, int pos,
                              int* argmax_host, float* logits_host);
 
+/* Greedy generation: nsteps decode steps from tokens_host[batch] at
+ * positions pos0, pos0+1, ..., each step's argmax feeding the next step on
+ * the device (the decode loop of InferenceEngine.GenerateAsync,
+ * src/SharpInfer.Core/Engine/InferenceEngine.cs:96-131, with Temperature <= 0).
+ * out_tokens_host[nsteps][batch] receives the generated tokens. */
+SI_EXPORT int si_decode_generate(si_model* m, const int* tokens_host, int batch, int pos0,
+                                 int nsteps, int* out_tokens_host);
+
 /* Attention of one layer alone (RoPE, KV append at pos, attention) for
  * qkv_dev [batch][(n_heads + 2 n_kv_heads) * head_dim] -> out_dev
  * [batch][n_heads * head_dim] (test hook for the attention kernel). */

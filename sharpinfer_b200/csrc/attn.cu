@@ -237,20 +237,49 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   if (tid == 0) stat[2 * G] = (float)atomicAdd(cnt, 1);
   __syncthreads();
   if (stat[2 * G] == (float)(S - 1)) {
+    // Partials of the other CTAs are read through L2 (ld.global.cg) after the
+    // fence: their statistics first, then all S partial outputs of a
+    // (head, dim) pair with the loads of one thread independent of each other.
     __threadfence();
+    float* pm = ored;           // [G][S] partial max, then merge weight
+    float* pl = ored + G * S;   // [G][S] partial sum
+    float* inv = pl + G * S;    // [G] 1 / merged denominator
+    for (int i = tid; i < G * S; i += blockDim.x) {
+      const int h = i / S, s = i - h * S;
+      const int64_t e = ((int64_t)b * a.nh + kvh * G + h) * S + s;
+      pm[i] = __ldcg(a.part_ml + e * 2);
+      pl[i] = __ldcg(a.part_ml + e * 2 + 1);
+    }
+    __syncthreads();
+    for (int h = warp; h < G; h += AT_WARPS) {
+      float M = -INFINITY;
+      for (int s = lane; s < S; s += 32) M = fmaxf(M, pm[h * S + s]);
+      M = warp_max(M);
+      float den = 0.f;
+      for (int s = lane; s < S; s += 32) {
+        const float m = pm[h * S + s];
+        const float w = m == -INFINITY ? 0.f : expf(m - M);
+        pm[h * S + s] = w;
+        den = fmaf(w, pl[h * S + s], den);
+      }
+      den = warp_sum(den);
+      if (lane == 0) inv[h] = 1.0f / den;
+    }
+    __syncthreads();
     for (int i = tid; i < G * HD; i += blockDim.x) {
       const int h = i / HD, d = i % HD;
-      const int64_t hb = ((int64_t)b * a.nh + kvh * G + h) * S;
-      float M = -INFINITY;
-      for (int s = 0; s < S; s++) M = fmaxf(M, *(volatile float*)(a.part_ml + (hb + s) * 2));
-      float num = 0.f, den = 0.f;
-      for (int s = 0; s < S; s++) {
-        const float m = *(volatile float*)(a.part_ml + (hb + s) * 2);
-        const float w = m == -INFINITY ? 0.f : expf(m - M);
-        num = fmaf(w, *(volatile float*)(a.part_o + (hb + s) * HD + d), num);
-        den = fmaf(w, *(volatile float*)(a.part_ml + (hb + s) * 2 + 1), den);
+      const float* po = a.part_o + ((int64_t)b * a.nh + kvh * G + h) * S * HD + d;
+      const float* wh = pm + h * S;
+      float num0 = 0.f, num1 = 0.f, num2 = 0.f, num3 = 0.f;
+      int s = 0;
+      for (; s + 4 <= S; s += 4) {
+        num0 = fmaf(wh[s], __ldcg(po + (int64_t)s * HD), num0);
+        num1 = fmaf(wh[s + 1], __ldcg(po + (int64_t)(s + 1) * HD), num1);
+        num2 = fmaf(wh[s + 2], __ldcg(po + (int64_t)(s + 2) * HD), num2);
+        num3 = fmaf(wh[s + 3], __ldcg(po + (int64_t)(s + 3) * HD), num3);
       }
-      a.out[(int64_t)b * a.out_ld + (int64_t)(kvh * G + h) * HD + d] = num / den;
+      for (; s < S; s++) num0 = fmaf(wh[s], __ldcg(po + (int64_t)s * HD), num0);
+      a.out[(int64_t)b * a.out_ld + (int64_t)(kvh * G + h) * HD + d] = ((num0 + num1) + (num2 + num3)) * inv[h];
     }
     if (tid == 0) *cnt = 0;
   }

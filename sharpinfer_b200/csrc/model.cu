@@ -128,6 +128,27 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
   pdl_launch();
 }
 
+// End of a step: the greedy tokens become the next step's inputs at the next
+// position (the decode loop of InferenceEngine.GenerateAsync,
+// InferenceEngine.cs:96-131, with greedy sampling) and are appended to the
+// history.
+__global__ void k_advance(StepParams* __restrict__ p, const int* __restrict__ argmax) {
+  pdl_wait();
+  const int b = threadIdx.x;
+  const int B = p->batch;
+  __syncthreads();
+  if (b < B) {
+    const int t = argmax[b];
+    if (p->hist && p->step < p->hist_cap) p->hist[(int64_t)p->step * B + b] = t;
+    p->tokens[b] = t;
+  }
+  __syncthreads();
+  if (b == 0) {
+    p->pos += 1;
+    p->step += 1;
+  }
+}
+
 // Seeded f16 N(0,1) for positions [0, len) of one (layer, seq) cache; the
 // generator index follows the reference layout [pos][kv head][dim].
 __global__ void k_kv_synth(__half* __restrict__ cache, uint64_t key, int len, int nkv, int max_seq) {
@@ -199,6 +220,8 @@ struct si_model {
   StepParams* dparams = nullptr;
   StepParams* hparams = nullptr;  // pinned
   int* hargmax = nullptr;         // pinned
+  int* hist = nullptr;            // device token history of si_decode_generate
+  int64_t hist_cap = 0;           // ints
   std::map<int, cudaGraphExec_t> graphs;
   std::vector<void*> allocs;
 };
@@ -272,6 +295,8 @@ int check_config(const si_model_config* c) {
   const int G = c->n_heads / c->n_kv_heads;
   if (G != 1 && G != 2 && G != 4 && G != 8) SI_FAIL(SI_ERR_UNSUPPORTED, "%d q heads per kv head", G);
   if (c->max_batch < 1 || c->max_batch > SI_MAX_BATCH) SI_FAIL(SI_ERR_INVALID, "max_batch %d outside 1..16", c->max_batch);
+  // split-KV attention: at most 511 splits of at most 1024 positions
+  if (c->max_seq > 511 * 1024) SI_FAIL(SI_ERR_UNSUPPORTED, "max_seq %d above %d", c->max_seq, 511 * 1024);
   for (int qt : {c->weight_qtype, c->lm_head_qtype, c->emb_qtype})
     if (qt != SI_Q4_K && qt != SI_Q6_K && qt != SI_Q8_0) SI_FAIL(SI_ERR_UNSUPPORTED, "quant type %d", qt);
   auto blk = [](int qt) { return qt == SI_Q8_0 ? 32 : 256; };
@@ -323,7 +348,6 @@ int enqueue_step(si_model* m, int B) {
   cudaStream_t s = m->c->stream;
   const int h = c.hidden, inter = c.intermediate, qd = c.n_heads * c.head_dim;
   const QmvBuffers qb = m->c->qmv();
-  SI_CUDA(cudaMemcpyAsync(m->dparams, m->hparams, sizeof(StepParams), cudaMemcpyHostToDevice, s));
   {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cfg_of(s, dim3((h + 255) / 256, B), dim3(256), 0, false, attr);
@@ -352,7 +376,11 @@ int enqueue_step(si_model* m, int B) {
     cudaLaunchConfig_t cfg = cfg_of(s, dim3(B), dim3(1024), 0, true, attr);
     SI_CUDA(cudaLaunchKernelEx(&cfg, k_argmax, (const float*)m->logits, (int64_t)c.vocab, m->argmax));
   }
-  SI_CUDA(cudaMemcpyAsync(m->hargmax, m->argmax, sizeof(int) * B, cudaMemcpyDeviceToHost, s));
+  {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg = cfg_of(s, dim3(1), dim3(SI_MAX_BATCH), 0, true, attr);
+    SI_CUDA(cudaLaunchKernelEx(&cfg, k_advance, m->dparams, (const int*)m->argmax));
+  }
   return SI_OK;
 }
 
@@ -486,7 +514,7 @@ SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model*
   if (st != SI_OK) return fail(st);
   const int64_t h = c.hidden;
   const size_t kv_elems = (size_t)c.n_layers * B * c.n_kv_heads * c.max_seq * c.head_dim;
-  m->splits_max = std::max((2 * ctx->sm_count + c.n_kv_heads - 1) / c.n_kv_heads, (c.max_seq + 1023) / 1024);
+  m->splits_max = std::min(511, std::max((2 * ctx->sm_count + c.n_kv_heads - 1) / c.n_kv_heads, (c.max_seq + 1023) / 1024));
   m->chunk_max = 1024;
   void* p;
 #define ALLOC(field, bytes)                                      \
@@ -545,6 +573,7 @@ SI_EXPORT int si_model_free(si_model* m) {
   for (void* p : m->allocs) cudaFree(p);
   if (m->hparams) cudaFreeHost(m->hparams);
   if (m->hargmax) cudaFreeHost(m->hargmax);
+  if (m->hist) cudaFree(m->hist);
   delete m;
   return SI_OK;
 }
@@ -682,13 +711,55 @@ SI_EXPORT int si_decode_step(si_model* m, const int* tokens, int batch, int pos,
   m->hparams->pos = pos;
   m->hparams->batch = batch;
   for (int b = 0; b < batch; b++) m->hparams->tokens[b] = tokens[b];
-  SI_CUDA(cudaGraphLaunch(ge, m->c->stream));
+  m->hparams->step = 0;
+  m->hparams->hist_cap = 0;
+  m->hparams->hist = nullptr;
+  cudaStream_t s = m->c->stream;
+  SI_CUDA(cudaMemcpyAsync(m->dparams, m->hparams, sizeof(StepParams), cudaMemcpyHostToDevice, s));
+  SI_CUDA(cudaGraphLaunch(ge, s));
+  SI_CUDA(cudaMemcpyAsync(m->hargmax, m->argmax, sizeof(int) * batch, cudaMemcpyDeviceToHost, s));
   if (logits_out)
-    SI_CUDA(cudaMemcpyAsync(logits_out, m->logits, (size_t)batch * c.vocab * 4, cudaMemcpyDeviceToHost, m->c->stream));
-  SI_CUDA(cudaStreamSynchronize(m->c->stream));
+    SI_CUDA(cudaMemcpyAsync(logits_out, m->logits, (size_t)batch * c.vocab * 4, cudaMemcpyDeviceToHost, s));
+  SI_CUDA(cudaStreamSynchronize(s));
   SI_TRY(check_device_errors(m->c));
   for (int b = 0; b < batch; b++) argmax_out[b] = m->hargmax[b];
   return SI_OK;
+}
+
+SI_EXPORT int si_decode_generate(si_model* m, const int* tokens, int batch, int pos0, int nsteps,
+                                 int* out_tokens) {
+  clear_error();
+  if (!m || !tokens || !out_tokens) SI_FAIL(SI_ERR_INVALID, "si_decode_generate: NULL argument");
+  const si_model_config& c = m->cfg;
+  if (batch < 1 || batch > c.max_batch) SI_FAIL(SI_ERR_INVALID, "batch %d outside 1..%d", batch, c.max_batch);
+  if (nsteps < 0 || pos0 < 0 || (int64_t)pos0 + nsteps > c.max_seq)
+    SI_FAIL(SI_ERR_INVALID, "positions %d..%d exceed max sequence length %d", pos0, pos0 + nsteps, c.max_seq);
+  for (int b = 0; b < batch; b++)
+    if (tokens[b] < 0 || tokens[b] >= c.vocab) SI_FAIL(SI_ERR_INVALID, "token id %d outside the vocabulary", tokens[b]);
+  if (nsteps == 0) return SI_OK;
+  SI_TRY(bind_device(m->c));
+  cudaGraphExec_t ge;
+  SI_TRY(get_graph(m, batch, &ge));
+  const int64_t need = (int64_t)nsteps * batch;
+  if (need > m->hist_cap) {
+    if (m->hist) cudaFree(m->hist);
+    m->hist = nullptr;
+    m->hist_cap = 0;
+    SI_CUDA(cudaMalloc(&m->hist, (size_t)need * 4));
+    m->hist_cap = need;
+  }
+  m->hparams->pos = pos0;
+  m->hparams->batch = batch;
+  for (int b = 0; b < batch; b++) m->hparams->tokens[b] = tokens[b];
+  m->hparams->step = 0;
+  m->hparams->hist_cap = nsteps;
+  m->hparams->hist = m->hist;
+  cudaStream_t s = m->c->stream;
+  SI_CUDA(cudaMemcpyAsync(m->dparams, m->hparams, sizeof(StepParams), cudaMemcpyHostToDevice, s));
+  for (int i = 0; i < nsteps; i++) SI_CUDA(cudaGraphLaunch(ge, s));
+  SI_CUDA(cudaMemcpyAsync(out_tokens, m->hist, (size_t)need * 4, cudaMemcpyDeviceToHost, s));
+  SI_CUDA(cudaStreamSynchronize(s));
+  return check_device_errors(m->c);
 }
 
 SI_EXPORT int si_model_attention(si_model* m, int layer, const float* qkv, float* out, int batch, int pos) {

@@ -10,6 +10,9 @@ struct StepParams {
   int pos;
   int batch;
   int tokens[SI_MAX_BATCH];
+  int step;      // steps taken since the parameters were last written by the host
+  int hist_cap;  // steps the history buffer holds
+  int* hist;     // [hist_cap][batch] greedy tokens of consecutive steps
 };
 
 struct AttnArgs {

@@ -99,6 +99,13 @@ class DecodeModel:
         N.call("si_decode_step", self.handle, N.ptr(tok), tok.size, pos, N.ptr(out), N.ptr(lg))
         return (out, lg) if logits else out
 
+    def generate(self, tokens, pos0, nsteps):
+        """nsteps greedy tokens per sequence, decoded on the device: [nsteps][batch]."""
+        tok = np.ascontiguousarray(tokens, np.int32).ravel()
+        out = np.empty((nsteps, tok.size), np.int32)
+        N.call("si_decode_generate", self.handle, N.ptr(tok), tok.size, pos0, nsteps, N.ptr(out))
+        return out
+
     def attention(self, layer, qkv, pos, out=None):
         """Attention of one layer for qkv [batch][(nh + 2 nkv) * hd] (CUDA f32 tensor)."""
         import torch

@@ -78,6 +78,7 @@ _SIGS = {
     "si_model_kv_tag": (_u64, [_i32, _i32, _i32]),
     "si_model_kv_write": (_i32, [_c_p, _i32, _i32, _i32, _i32, _c_p, _c_p]),
     "si_decode_step": (_i32, [_c_p, _c_p, _i32, _i32, _c_p, _c_p]),
+    "si_decode_generate": (_i32, [_c_p, _c_p, _i32, _i32, _i32, _c_p]),
     "si_model_attention": (_i32, [_c_p, _i32, _c_p, _c_p, _i32, _i32]),
 }
 

@@ -125,3 +125,26 @@ def test_step_rejects_bad_arguments(ctx):
     with pytest.raises(N.SIError):
         m.step([1, 2], 0)  # batch above max_batch
     m.free()
+
+
+def test_generate_matches_stepping(ctx):
+    """The device-resident loop (si_decode_generate) equals host-driven steps and the oracle."""
+    cfg = small_cfg(4, layers=2, max_batch=2)
+    m = DecodeModel(ctx, cfg)
+    m.synth(SEED)
+    m.kv_synth(30, SEED)
+    gen = m.generate([3, 500], 30, 6)
+    m.kv_synth(30, SEED)
+    toks = [3, 500]
+    stepped = []
+    for s in range(6):
+        toks = list(m.step(toks, 30 + s))
+        stepped.append(toks)
+    assert np.array_equal(gen, np.array(stepped))
+    om = oracle.synthetic_model(cfg, SEED, n_seq=2, kv_len=30)
+    for b, t0 in enumerate([3, 500]):
+        tok = t0
+        for s in range(6):
+            tok = oracle.argmax(om.forward(b, tok, 30 + s))
+            assert tok == gen[s, b]
+    m.free()
