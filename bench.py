@@ -112,20 +112,31 @@ def dist_setup():
             int(os.environ.get("LOCAL_RANK", "0")))
 
 
-def model_cfg(steps, warmup):
-    from sharpinfer_b200.model import llama3_8b
-    return llama3_8b(max_seq=KV_LEN + 2 * (steps + warmup) + 8, max_batch=1)
+def model_cfg(args):
+    from sharpinfer_b200.model import config, llama3_8b
+    c = llama3_8b(max_seq=args.ctx + 2 * (args.steps + args.warmup) + 8, max_batch=1)
+    if args.layers != c.n_layers:
+        c = config(args.layers, c.hidden, c.intermediate, c.n_heads, c.n_kv_heads, c.vocab, c.max_seq, 1)
+    return c
 
 
-def cpu_decode(cfg, ntokens, warmup, max_seconds=None):
+def workload_name(args):
+    name = "decode8b: Llama-3-8B arch (32 layers, hidden 4096, 32/8 heads, FFN 14336, vocab 128256) Q4_K_M, " \
+           "f16 KV prefilled to %d, batch 1, greedy" % args.ctx
+    if args.layers != 32:
+        name = name.replace("32 layers", "%d of its 32 layers" % args.layers)
+    return name
+
+
+def cpu_decode(cfg, ctx_len, ntokens, warmup, max_seconds=None):
     """The reference CPU path (oracle restatement of Transformer.Forward) on
     the host cores: greedy tokens/s over the same synthetic model."""
     import oracle
     t0 = time.time()
-    om = oracle.synthetic_model(cfg, SEED, n_seq=1, kv_len=KV_LEN)
+    om = oracle.synthetic_model(cfg, SEED, n_seq=1, kv_len=ctx_len)
     build_s = time.time() - t0
     tok = START_TOKEN
-    pos = KV_LEN
+    pos = ctx_len
     for _ in range(warmup):
         tok = oracle.argmax(om.forward(0, tok, pos))
         pos += 1
@@ -140,20 +151,19 @@ def cpu_decode(cfg, ntokens, warmup, max_seconds=None):
     return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port", "tokens": n,
             "ms_per_step": dt / n * 1e3, "build_s": build_s,
             "sample": "%d greedy decode steps of the same 8B Q4_K_M model at ctx %d (weights dequantised row by row, "
-                      "f32 arithmetic of TensorOps, KV values rounded through f16), %d threads" % (n, KV_LEN, threads)}
+                      "f32 arithmetic of TensorOps, KV values rounded through f16), %d threads" % (n, ctx_len, threads)}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
-    cfg = model_cfg(args.steps, args.warmup)
-    r = cpu_decode(cfg, args.steps, min(args.warmup, 2), max_seconds=args.ref_seconds)
+    cfg = model_cfg(args)
+    r = cpu_decode(cfg, args.ctx, args.steps, min(args.warmup, 2), max_seconds=args.ref_seconds)
     line = {"metric": METRIC, "value": round(r["value"], 4), "unit": "tok/s", "n_gpus": args.gpus,
             "steps": r["tokens"], "warmup": min(args.warmup, 2), "ms_per_step": round(r["ms_per_step"], 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Q4_K_M weights, f16-exact KV prefix)", "impl": "reference",
-            "config": {"workload": "decode8b: Llama-3-8B arch Q4_K_M, ctx 4096, batch 1, greedy",
-                       "parallelism": "cpu"},
+            "config": {"workload": workload_name(args), "seq_len": args.ctx, "parallelism": "cpu"},
             "cpu_baseline": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()
                              if k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(r["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -200,14 +210,14 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     ctx = B200Context(local)
     torch.cuda.set_stream(ctx.torch_stream)
-    cfg = model_cfg(args.steps, args.warmup)
+    cfg = model_cfg(args)
     m = DecodeModel(ctx, cfg)
     m.synth(SEED)
-    m.kv_synth(KV_LEN, SEED)
+    m.kv_synth(args.ctx, SEED)
     stream = ctx.torch_stream
     # warm-up (captures the decode graph)
-    wtok = m.generate([START_TOKEN], KV_LEN, args.warmup)
-    pos = KV_LEN + args.warmup
+    wtok = m.generate([START_TOKEN], args.ctx, args.warmup)
+    pos = args.ctx + args.warmup
     tok = int(wtok[-1, 0])
     ctx.synchronize()
     if world > 1:
@@ -244,7 +254,7 @@ def run_ours(args, world, rank, local):
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
-        tb = token_bytes(cfg, KV_LEN + args.warmup + args.steps // 2)
+        tb = token_bytes(cfg, args.ctx + args.warmup + args.steps // 2)
         traffic = None
         tp = os.path.join(ROOT, "profiles", "traffic.json")
         if os.path.exists(tp):
@@ -255,10 +265,9 @@ def run_ours(args, world, rank, local):
             "scaling": "weak", "vs_baseline": None,
             "dtype": "q4_k/q6_k weights x f32 activations (f16 hi/lo MMA, f32 accumulate), f16 KV",
             "data": "synthetic (seeded Q4_K_M weights and f16 KV prefix; no checkpoint offline)",
-            "config": {"workload": "decode8b: Llama-3-8B arch (32 layers, hidden 4096, 32/8 heads, FFN 14336, "
-                                   "vocab 128256) Q4_K_M, f16 KV prefilled to 4096, batch 1, greedy",
-                       "global_batch": world, "seq_len": KV_LEN, "parallelism": "replicas" if world > 1 else "single",
-                       "l2": "inputs larger than L2 (4.9 GB streamed per step)"},
+            "config": {"workload": workload_name(args),
+                       "global_batch": world, "seq_len": args.ctx, "parallelism": "replicas" if world > 1 else "single",
+                       "l2": "inputs larger than L2 (%.2f GB streamed per step)" % (tb / 1e9)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
                          "kernel": "k_qmv_warp Q4_K, fused gate/up 28672x4096 (66 MB), batch 1",
@@ -272,7 +281,7 @@ def run_ours(args, world, rank, local):
             "tokens_head": [int(v) for v in gen[:8, 0]],
         }
         if not args.no_cpu_baseline:
-            cb = cpu_decode(cfg, 100, 1, max_seconds=args.cpu_seconds)
+            cb = cpu_decode(cfg, args.ctx, 100, 1, max_seconds=args.cpu_seconds)
             line["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cb.items()
                                     if k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
@@ -292,6 +301,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=32, help="transformer layers (32 = the full 8B model)")
+    ap.add_argument("--ctx", type=int, default=KV_LEN, help="prefilled KV positions")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
