@@ -160,6 +160,20 @@ SI_EXPORT int si_qmatvec_prepared(si_ctx* ctx, const si_weight* w, float* y_dev,
 SI_EXPORT int si_qmatvec_host(si_ctx* ctx, const si_weight* w, const float* x_host,
                               float* y_host, int batch);
 
+/* si_qmatvec for callers that cannot allocate device memory: no counterpart
+ * in the reference.  It takes no context and calls no cudaMalloc/cudaFree.
+ * Its scratch is one fixed 4 MiB array of device memory inside the library,
+ * held by every GPU that loads the library until the process exits.
+ * Limits: rows <= 32768, cols <= 16384, batch 1..16; larger shapes return
+ * SI_ERR_UNSUPPORTED.  x [batch][cols] and y [batch][rows] are f32 device
+ * pointers on w's device; `stream` is a cudaStream_t (NULL = legacy default
+ * stream).  The call is synchronous on that stream.  The first call on a
+ * device looks up the array's device address; make that first call before
+ * any stream capture.  All calls on one GPU share the array: calls whose
+ * work overlaps on the GPU (other streams or threads) race -- serialise them. */
+SI_EXPORT int si_qmatvec_noalloc(const si_weight* w, const float* x_dev, float* y_dev, int batch,
+                                 void* stream);
+
 /* ------------------------------------------------------------ decode model */
 
 /* A Llama/Mistral-architecture model resident on one GPU: the forward pass of
