@@ -14,7 +14,7 @@ value: tokens/s of the device-resident greedy loop (si_decode_generate),
 timed with CUDA events.  e2e: tokens/s through the host-facing per-token call
 (si_decode_step: token id copied in, argmax copied out, every step).
 roofline: the dominant kernel, the fused gate/up Q4_K matvec (28672 x 4096,
-66 MB), timed alone with CUDA events over rotating weight copies; the whole
+66 MB), timed alone with CUDA events over 40 graph-captured launches on rotating weight copies; the whole
 step's bytes per token against the same peak are reported beside it.
 --impl reference times the reference's CPU path -- the oracle restatement of
 SharpInfer's managed forward pass over the same weights -- on the host cores.
@@ -173,7 +173,8 @@ def run_reference(args, world, rank):
 
 def matvec_roofline(ctx, torch, dev, reps=40):
     """Average duration of the fused gate/up Q4_K matvec (28672 x 4096) over
-    back-to-back launches on 4 rotating weight copies (264 MB > L2)."""
+    `reps` launches on 4 rotating weight copies (264 MB > L2), captured in one
+    CUDA graph so that host launch overhead does not enter the timing."""
     from sharpinfer_b200 import native as N
     from sharpinfer_b200.backend import synth_f32_host
     rows, cols = 2 * 14336, 4096
@@ -184,14 +185,20 @@ def matvec_roofline(ctx, torch, dev, reps=40):
     for i in range(8):
         ctx.qmatvec_prepared(ws[i % 4], 1, out=y)
     s = ctx.torch_stream
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ctx.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(reps):
+            ctx.qmatvec_prepared(ws[i % 4], 1, out=y)
+    g.replay()
+    ctx.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(s)
-    for i in range(reps):
-        ctx.qmatvec_prepared(ws[i % 4], 1, out=y)
+    g.replay()
     e1.record(s)
     ctx.synchronize()
     ms = e0.elapsed_time(e1) / reps
+    del g
     for w in ws:
         w.free()
     return ms, q4k_bytes(rows, cols) + 4 * (cols + rows)
@@ -276,7 +283,7 @@ def run_ours(args, world, rank, local):
                                 "frac": round(tb / (ms * 1e-3) / 1e9 / peak, 4)},
             "e2e": {"value": round(world * 1e3 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4},
-            "gpu_launches": 293 * args.steps,
+            "gpu_launches": (9 * cfg.n_layers + 5) * args.steps,
             "clocks": clk,
             "tokens_head": [int(v) for v in gen[:8, 0]],
         }

@@ -1,5 +1,5 @@
 // Decode attention over the f16 KV cache: RoPE, KV append and split-KV
-// flash-decoding with an online-softmax merge.
+// flash-decoding with an online-softmax merge, on the tensor cores.
 //
 // Semantics follow the attention block of Transformer.Forward
 // (src/SharpInfer.Core/Layers/Transformer.cs:94-129): RotaryEmbedding.Apply
@@ -10,14 +10,22 @@
 // softmax over t <= pos of Dot(q_h, K_t) * (1/sqrt(hd)) and the weighted sum
 // of V_t.
 //
-// Cache layout: [layer][seq][kv head][position][128] f16, so the positions of
+// Cache layout: [layer][seq][kv head][position][128] f16 with the 16-byte
+// chunks of each row XOR-swizzled by position (kv_swz), so the positions of
 // one (seq, kv head) are contiguous and a 64-position chunk is one 16 KB bulk
 // copy.  Grid (split, kv head, seq): CTA s handles positions
-// [s*chunk, min(len, (s+1)*chunk)), len = pos + 1.  Its 8 warps first score
-// all its positions for the G = nh/nkv q heads of the kv head, then
-// accumulate p * V; K and V chunks stream through a shared-memory ring filled
-// by thread 0 (cp.async.bulk + mbarriers, bounded waits).  Each CTA writes
-// (max, sum, o[128]) per head; the last CTA of a (seq, kv head) merges them.
+// [s*chunk, min(len, (s+1)*chunk)), len = pos + 1, with 4 warps, each taking
+// one 16-position block of every 64-position ring stage:
+//  * scores: mma.m16n8k16 with A = 16 cached K rows x 16 dims (ldmatrix) and
+//    B = the G q heads split into f16 hi + lo columns (q scaled by a power of
+//    two per head), f32 accumulation;
+//  * softmax over the CTA's positions (max, expf, sum), probabilities stored
+//    as f16 hi + lo;
+//  * output: mma with A = V^T (ldmatrix.trans), B = the probabilities.
+// Each CTA writes (max, sum, o[128]) per head; the kernel that prepares the
+// O-projection input merges the splits (k_prep, SI_PREP_ATTN_MERGE).  CTAs
+// whose positions are all in the cache already start their K/V copies before
+// waiting for the kernel that produces q.
 #include "common.cuh"
 #include "model.cuh"
 
@@ -25,82 +33,80 @@ namespace si {
 namespace {
 
 constexpr int HD = 128;
-constexpr int AT_WARPS = 8;
-constexpr int AT_SUB = 64;                 // positions per ring stage
+constexpr int AT_WARPS = 4;
+constexpr int AT_SUB = 64;                 // positions per ring stage (4 blocks of 16)
 constexpr int AT_NS = 4;                   // ring stages
 constexpr int AT_STAGE = AT_SUB * HD * 2;  // 16 KB
-constexpr int AT_QSTRIDE = 36;             // floats per 32-dim quarter of q (padded)
 
-__device__ __forceinline__ float f16lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFF))); }
-__device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& a0, uint32_t& a1, uint32_t& a2, uint32_t& a3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& a0, uint32_t& a1, uint32_t& a2, uint32_t& a3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+               : "r"(addr)
+               : "memory");
+}
+// f16 hi (part 0) or lo (part 1) of v, two values packed
+__device__ __forceinline__ uint32_t split2(float v0, float v1, int part) {
+  const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+  if (part == 0) return (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+  const __half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+  return (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+}
 
 struct AttnSmem {
-  // ring of K/V chunks, then q, scores, partial outputs, barriers
-  static constexpr int RING = AT_NS * AT_STAGE;
+  int G, cp;  // heads per kv head, positions per split rounded up to 64
+  __host__ __device__ size_t qs() const { return (size_t)AT_NS * AT_STAGE; }           // f32 [G][128]
+  __host__ __device__ size_t qsc() const { return qs() + (size_t)G * HD * 4; }          // f32 [16]
+  __host__ __device__ size_t sc() const { return qsc() + 64; }                          // f32 [G][cp]
+  __host__ __device__ size_t pp() const { return sc() + (size_t)G * cp * 4; }           // f16 [2][G][cp]
+  __host__ __device__ size_t ored() const { return pp() + (size_t)2 * G * cp * 2; }     // f32 [W][G][128]
+  __host__ __device__ size_t stat() const { return ored() + (size_t)AT_WARPS * G * HD * 4; }  // f32 [G][2] + 2
+  __host__ __device__ size_t bars() const { return (stat() + (2 * G + 2) * 4 + 7) & ~(size_t)7; }
+  __host__ __device__ size_t total() const { return bars() + AT_NS * 8; }
 };
 
 template <int G>
 __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
+  constexpr int NT = (2 * G + 7) / 8;  // n-tiles of 8 (head, hi/lo) columns
   extern __shared__ __align__(128) uint8_t smem[];
   const int s_idx = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int S = gridDim.x, nkv = gridDim.y;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+  const AttnSmem L{G, (a.chunk_max + 63) & ~63};
+  const int cp = L.cp;
   uint8_t* ring = smem;
-  const int cpad = (a.chunk_max + 3) & ~3;                 // keeps the next region 16-B aligned
-  float* qs = (float*)(smem + AttnSmem::RING);           // [G][4][AT_QSTRIDE]
-  float* sc = qs + G * 4 * AT_QSTRIDE;                    // [G][cpad]
-  float* ored = sc + G * cpad;                            // [AT_WARPS][G][HD]
-  float* stat = ored + AT_WARPS * G * HD;                 // [G][2] max, sum + flag
-  uint64_t* bars = (uint64_t*)(stat + 2 * G + 2);         // aligned below
-  bars = (uint64_t*)(((uintptr_t)bars + 7) & ~(uintptr_t)7);
-  const uint32_t bar0 = smem_u32(bars);
+  float* qs = (float*)(smem + L.qs());
+  float* qsc = (float*)(smem + L.qsc());  // [0, G): score factor, [8, 8 + G): q multiplier
+  float* sc = (float*)(smem + L.sc());
+  uint16_t* pp = (uint16_t*)(smem + L.pp());
+  float* ored = (float*)(smem + L.ored());
+  float* stat = (float*)(smem + L.stat());
+  const uint32_t bar0 = smem_u32(smem + L.bars());
 
-  pdl_wait();
+  pdl_launch();  // dependents may start their independent prologue now
+  // The position comes from the step parameters, which no kernel of the step
+  // writes, and positions < pos are already in the cache: both may be read
+  // before the producer of q has finished.
   const int pos = a.params->pos;
   const int len = pos + 1;
   const int chunk = (len + S - 1) / S;
   const int t0 = s_idx * chunk, t1 = min(len, t0 + chunk);
   const int n = max(0, t1 - t0);
   const int nsub = (n + AT_SUB - 1) / AT_SUB;
+  const bool appends = t1 == len && n > 0;  // this split stores position pos
   const int64_t cache_off = (((int64_t)a.layer * a.max_batch + b) * nkv + kvh) * a.max_seq * HD;
   __half* kc = a.kcache + cache_off;
   __half* vc = a.vcache + cache_off;
-  const float* qkv = a.qkv + (int64_t)b * a.qkv_ld;
-  const float2* rope = (const float2*)(a.rope + (int64_t)pos * HD);  // [HD/2] (cos, sin)
-
-  // q heads of this kv head, roped (RotaryEmbedding.ApplyToHead), into smem
-  for (int i = tid; i < G * HD / 2; i += blockDim.x) {
-    const int h = i / (HD / 2), p = i % (HD / 2);
-    const float* qh = qkv + (int64_t)(kvh * G + h) * HD;
-    const float x0 = qh[2 * p], x1 = qh[2 * p + 1];
-    const float2 cs = rope[p];
-    const float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-    const float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-    const int d0 = 2 * p;
-    qs[(h * 4 + (d0 >> 5)) * AT_QSTRIDE + (d0 & 31)] = r0;
-    qs[(h * 4 + ((d0 + 1) >> 5)) * AT_QSTRIDE + ((d0 + 1) & 31)] = r1;
-  }
-  // the split holding `pos` appends the roped k and v (KVCache.Store)
-  if (t1 == len && n > 0 && tid < HD / 2) {
-    const int p = tid;
-    const float* kh = qkv + (int64_t)(a.nh + kvh) * HD;
-    const float* vh = qkv + (int64_t)(a.nh + nkv + kvh) * HD;
-    const float2 cs = rope[p];
-    const float x0 = kh[2 * p], x1 = kh[2 * p + 1];
-    const float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
-    const float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
-    *(__half2*)(kc + (int64_t)pos * HD + 2 * p) = __halves2half2(__float2half_rn(r0), __float2half_rn(r1));
-    *(__half2*)(vc + (int64_t)pos * HD + 2 * p) =
-        __halves2half2(__float2half_rn(vh[2 * p]), __float2half_rn(vh[2 * p + 1]));
-    // make these generic-proxy writes visible to the bulk (async-proxy) reads below
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-  }
   if (tid == 0) {
     for (int i = 0; i < AT_NS; i++) mbar_init(bar0 + 8 * i, 1);
     mbar_fence_init();
   }
   __syncthreads();
-
   // ring items: K sub-chunks 0..nsub-1, then V sub-chunks 0..nsub-1
   const int items = 2 * nsub;
   auto issue = [&](int it) {
@@ -113,56 +119,107 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
     mbar_arrive_expect_tx(bar0 + 8 * st, bytes);
     bulk_g2s(smem_u32(ring + st * AT_STAGE), base + (int64_t)p0 * HD, bytes, bar0 + 8 * st);
   };
-  if (tid == 0)
+  if (tid == 0 && !appends)
+    for (int it = 0; it < min(items, AT_NS); it++) issue(it);
+  pdl_wait();
+  const float* qkv = a.qkv + (int64_t)b * a.qkv_ld;
+  const float2* rope = (const float2*)(a.rope + (int64_t)pos * HD);  // [HD/2] (cos, sin)
+
+  // q heads of this kv head, roped (RotaryEmbedding.ApplyToHead), into smem
+  for (int i = tid; i < G * HD / 2; i += blockDim.x) {
+    const int h = i / (HD / 2), p = i % (HD / 2);
+    const float* qh = qkv + (int64_t)(kvh * G + h) * HD;
+    const float x0 = qh[2 * p], x1 = qh[2 * p + 1];
+    const float2 cs = rope[p];
+    qs[h * HD + 2 * p] = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+    qs[h * HD + 2 * p + 1] = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+  }
+  // the split holding `pos` appends the roped k and v (KVCache.Store), then
+  // starts its copies
+  if (appends && tid < HD / 2) {
+    const int p = tid;
+    const float* kh = qkv + (int64_t)(a.nh + kvh) * HD;
+    const float* vh = qkv + (int64_t)(a.nh + nkv + kvh) * HD;
+    const float2 cs = rope[p];
+    const float x0 = kh[2 * p], x1 = kh[2 * p + 1];
+    const float r0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+    const float r1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
+    const int o = kv_swz(2 * p, pos);  // dims 2p, 2p+1 stay adjacent
+    *(__half2*)(kc + (int64_t)pos * HD + o) = __halves2half2(__float2half_rn(r0), __float2half_rn(r1));
+    *(__half2*)(vc + (int64_t)pos * HD + o) = __halves2half2(__float2half_rn(vh[2 * p]), __float2half_rn(vh[2 * p + 1]));
+    // make these generic-proxy writes visible to the bulk (async-proxy) reads below
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+  }
+  __syncthreads();
+  if (tid == 0 && appends)
     for (int it = 0; it < min(items, AT_NS); it++) issue(it);
 
+  // per-head power-of-two scale of q: max |q 2^e| in [2^13, 2^14)
+  for (int h = warp; h < G; h += AT_WARPS) {
+    float m = 0.f;
+    for (int d = lane; d < HD; d += 32) m = fmaxf(m, fabsf(qs[h * HD + d]));
+    m = warp_max(m);
+    int e = 0;
+    if (m > 0.f && m <= 3.0e38f) {
+      int E;
+      frexpf(m, &E);
+      e = 14 - E;
+      e = e < -100 ? -100 : (e > 100 ? 100 : e);
+    }
+    if (lane == 0) {
+      qsc[h] = a.scale * ldexpf(1.0f, -e);
+      qsc[8 + h] = ldexpf(1.0f, e);
+    }
+  }
+  __syncthreads();
+  // q B fragments: column n = g is (head 4 nt + g/2, part g%2)
+  uint32_t qb[NT][8][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; nt++) {
+    const int h = 4 * nt + (g >> 1), part = g & 1;
+#pragma unroll
+    for (int ks = 0; ks < 8; ks++) {
+      if (h < G) {
+        const float mul = qsc[8 + h];
+        const float* q = qs + h * HD + 16 * ks + 2 * t;
+        qb[nt][ks][0] = split2(q[0] * mul, q[1] * mul, part);
+        qb[nt][ks][1] = split2(q[8] * mul, q[9] * mul, part);
+      } else {
+        qb[nt][ks][0] = qb[nt][ks][1] = 0u;
+      }
+    }
+  }
+
   bool ok = true;
-  const float scale = a.scale;
+  const int p0 = 16 * warp;  // this warp's block in every stage
   // ---- pass 1: scores ----
-  // warp handles 8 positions per step: lane (pp = lane/4, quarter qq = lane%4)
-  const int pp = lane >> 2, qq = lane & 3;
   for (int it = 0; it < nsub; it++) {
     const int st = it % AT_NS;
     if (!mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / AT_NS) & 1))) ok = false;
-    const int p0 = t0 + it * AT_SUB;
-    const int np = min(AT_SUB, t1 - p0);
-    const uint8_t* kst = ring + st * AT_STAGE;
-    for (int tl = warp * 8 + pp; tl < AT_SUB; tl += AT_WARPS * 8) {
-      float acc[G];
+    const int rb = it * AT_SUB;
+    const int np = min(AT_SUB, n - rb);
+    if (ok && p0 < np) {
+      const int m = lane >> 3, r = p0 + (lane & 7) + 8 * (m & 1), cadd = m >> 1;
+      const uint32_t rowaddr = smem_u32(ring + st * AT_STAGE + r * 256);
+      const int key = (t0 + rb + r) & 7;
+      float acc[NT][4];
 #pragma unroll
-      for (int h = 0; h < G; h++) acc[h] = 0.f;
-      if (tl < np && ok) {
-        const uint4* kr = (const uint4*)(kst + tl * HD * 2 + qq * 64);
-        float kf[32];
+      for (int nt = 0; nt < NT; nt++) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const uint4 v = kr[i];
-          kf[8 * i + 0] = f16lo(v.x); kf[8 * i + 1] = f16hi(v.x);
-          kf[8 * i + 2] = f16lo(v.y); kf[8 * i + 3] = f16hi(v.y);
-          kf[8 * i + 4] = f16lo(v.z); kf[8 * i + 5] = f16hi(v.z);
-          kf[8 * i + 6] = f16lo(v.w); kf[8 * i + 7] = f16hi(v.w);
-        }
+      for (int ks = 0; ks < 8; ks++) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(rowaddr + (uint32_t)(((2 * ks + cadd) ^ key) << 4), a0, a1, a2, a3);
 #pragma unroll
-        for (int h = 0; h < G; h++) {
-          const float4* q4 = (const float4*)(qs + (h * 4 + qq) * AT_QSTRIDE);
-          float d = 0.f;
-#pragma unroll
-          for (int i = 0; i < 8; i++) {
-            const float4 qv = q4[i];
-            d = fmaf(qv.x, kf[4 * i + 0], d);
-            d = fmaf(qv.y, kf[4 * i + 1], d);
-            d = fmaf(qv.z, kf[4 * i + 2], d);
-            d = fmaf(qv.w, kf[4 * i + 3], d);
-          }
-          acc[h] = d;
-        }
+        for (int nt = 0; nt < NT; nt++) mma16816(acc[nt], a0, a1, a2, a3, qb[nt][ks][0], qb[nt][ks][1]);
       }
 #pragma unroll
-      for (int h = 0; h < G; h++) {
-        float d = acc[h];
-        d += __shfl_xor_sync(0xFFFFFFFFu, d, 1);
-        d += __shfl_xor_sync(0xFFFFFFFFu, d, 2);
-        if (qq == 0 && tl < np) sc[h * cpad + it * AT_SUB + tl] = d * scale;
+      for (int nt = 0; nt < NT; nt++) {
+        const int h = 4 * nt + t;
+        if (h < G) {
+          const float f = qsc[h];
+          if (p0 + g < np) sc[h * cp + rb + p0 + g] = (acc[nt][0] + acc[nt][1]) * f;
+          if (p0 + g + 8 < np) sc[h * cp + rb + p0 + g + 8] = (acc[nt][2] + acc[nt][3]) * f;
+        }
       }
     }
     __syncthreads();  // stage consumed by every warp
@@ -171,13 +228,20 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   // ---- softmax statistics per head (TensorOps.Softmax: max, exp, sum) ----
   for (int h = warp; h < G; h += AT_WARPS) {
     float m = -INFINITY;
-    for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h * cpad + i]);
+    for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h * cp + i]);
     m = warp_max(m);
     float l = 0.f;
-    for (int i = lane; i < n; i += 32) {
-      const float p = expf(sc[h * cpad + i] - m);
-      sc[h * cpad + i] = p;
-      l += p;
+    uint16_t* ph = pp + (size_t)h * cp;
+    uint16_t* pl = pp + (size_t)(G + h) * cp;
+    for (int i = lane; i < nsub * AT_SUB; i += 32) {
+      float p = 0.f;
+      if (i < n) {
+        p = expf(sc[h * cp + i] - m);
+        l += p;
+      }
+      const __half hi = __float2half_rn(p);
+      ph[i] = __half_as_ushort(hi);
+      pl[i] = __half_as_ushort(__float2half_rn(p - __half2float(hi)));
     }
     l = warp_sum(l);
     if (lane == 0) {
@@ -186,42 +250,71 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
     }
   }
   __syncthreads();
-  // ---- pass 2: o[h][d] = sum_t p[h][t] * V_t[d]; lane holds dims 4*lane..+3 ----
-  float o[G][4];
+  // ---- pass 2: o^T[d][h] = sum_t V_t[d] p[h][t] ----
+  float o[NT][8][4];
 #pragma unroll
-  for (int h = 0; h < G; h++) o[h][0] = o[h][1] = o[h][2] = o[h][3] = 0.f;
+  for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+    for (int mt = 0; mt < 8; mt++) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
   for (int it = nsub; it < items; it++) {
     const int st = it % AT_NS;
     if (!mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / AT_NS) & 1))) ok = false;
-    const int sub = it - nsub;
-    const int np = min(AT_SUB, t1 - (t0 + sub * AT_SUB));
-    const uint8_t* vst = ring + st * AT_STAGE;
-    if (ok) {
-      for (int tl = warp; tl < np; tl += AT_WARPS) {
-        const uint2 v = *(const uint2*)(vst + tl * HD * 2 + lane * 8);
-        const float v0 = f16lo(v.x), v1 = f16hi(v.x), v2 = f16lo(v.y), v3 = f16hi(v.y);
+    const int rb = (it - nsub) * AT_SUB;
+    const int np = min(AT_SUB, n - rb);
+    uint8_t* vst = ring + st * AT_STAGE;
+    if (ok && p0 < np) {
+      if (np - p0 < 16) {  // rows past the chunk: zero them (their p is 0, 0 * stale could be NaN)
+        uint4* z = (uint4*)(vst + np * 256);
+        for (int i = lane; i < (p0 + 16 - np) * 16; i += 32) z[i] = make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+      }
+      uint32_t pb[NT][2];
 #pragma unroll
-        for (int h = 0; h < G; h++) {
-          const float p = sc[h * cpad + sub * AT_SUB + tl];
-          o[h][0] = fmaf(p, v0, o[h][0]);
-          o[h][1] = fmaf(p, v1, o[h][1]);
-          o[h][2] = fmaf(p, v2, o[h][2]);
-          o[h][3] = fmaf(p, v3, o[h][3]);
+      for (int nt = 0; nt < NT; nt++) {
+        const int h = 4 * nt + (g >> 1), part = g & 1;
+        if (h < G) {
+          const uint16_t* pr = pp + (size_t)(part * G + h) * cp + rb + p0 + 2 * t;
+          pb[nt][0] = *(const uint32_t*)pr;
+          pb[nt][1] = *(const uint32_t*)(pr + 8);
+        } else {
+          pb[nt][0] = pb[nt][1] = 0u;
         }
+      }
+      const int m = lane >> 3, r = p0 + (lane & 7) + 8 * (m >> 1), cadd = m & 1;
+      const uint32_t rowaddr = smem_u32(vst + r * 256);
+      const int key = (t0 + rb + r) & 7;
+#pragma unroll
+      for (int mt = 0; mt < 8; mt++) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4_t(rowaddr + (uint32_t)(((2 * mt + cadd) ^ key) << 4), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) mma16816(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
       }
     }
     __syncthreads();
-    if (tid == 0 && it + AT_NS < items) issue(it + AT_NS);
+    if (tid == 0 && it + AT_NS < items) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // zeroed rows before the refill
+      issue(it + AT_NS);
+    }
   }
-  // reduce the 8 warps' partial outputs
+  // reduce the warps' partial outputs
 #pragma unroll
-  for (int h = 0; h < G; h++)
-    *(float4*)(ored + (warp * G + h) * HD + lane * 4) = make_float4(o[h][0], o[h][1], o[h][2], o[h][3]);
+  for (int nt = 0; nt < NT; nt++) {
+    const int h = 4 * nt + t;
+    if (h < G) {
+#pragma unroll
+      for (int mt = 0; mt < 8; mt++) {
+        ored[(warp * G + h) * HD + 16 * mt + g] = o[nt][mt][0] + o[nt][mt][1];
+        ored[(warp * G + h) * HD + 16 * mt + g + 8] = o[nt][mt][2] + o[nt][mt][3];
+      }
+    }
+  }
   __syncthreads();
   const int64_t pbase = (((int64_t)b * a.nh + kvh * G) * S + s_idx);  // head h: + h*S
   for (int i = tid; i < G * HD; i += blockDim.x) {
     const int h = i / HD, d = i % HD;
     float v = 0.f;
+#pragma unroll
     for (int w = 0; w < AT_WARPS; w++) v += ored[(w * G + h) * HD + d];
     a.part_o[(pbase + (int64_t)h * S) * HD + d] = v;
   }
@@ -230,68 +323,13 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
     a.part_ml[(pbase + (int64_t)tid * S) * 2 + 1] = stat[2 * tid + 1];
   }
   if (!ok && tid == 0) atomicOr(a.err, SI_DEVERR_WAIT_TIMEOUT);
-  // ---- last CTA of (seq, kv head) merges the S partials ----
-  __threadfence();
-  __syncthreads();
-  int* cnt = a.counters + (int64_t)b * nkv + kvh;
-  if (tid == 0) stat[2 * G] = (float)atomicAdd(cnt, 1);
-  __syncthreads();
-  if (stat[2 * G] == (float)(S - 1)) {
-    // Partials of the other CTAs are read through L2 (ld.global.cg) after the
-    // fence: their statistics first, then all S partial outputs of a
-    // (head, dim) pair with the loads of one thread independent of each other.
-    __threadfence();
-    float* pm = ored;           // [G][S] partial max, then merge weight
-    float* pl = ored + G * S;   // [G][S] partial sum
-    float* inv = pl + G * S;    // [G] 1 / merged denominator
-    for (int i = tid; i < G * S; i += blockDim.x) {
-      const int h = i / S, s = i - h * S;
-      const int64_t e = ((int64_t)b * a.nh + kvh * G + h) * S + s;
-      pm[i] = __ldcg(a.part_ml + e * 2);
-      pl[i] = __ldcg(a.part_ml + e * 2 + 1);
-    }
-    __syncthreads();
-    for (int h = warp; h < G; h += AT_WARPS) {
-      float M = -INFINITY;
-      for (int s = lane; s < S; s += 32) M = fmaxf(M, pm[h * S + s]);
-      M = warp_max(M);
-      float den = 0.f;
-      for (int s = lane; s < S; s += 32) {
-        const float m = pm[h * S + s];
-        const float w = m == -INFINITY ? 0.f : expf(m - M);
-        pm[h * S + s] = w;
-        den = fmaf(w, pl[h * S + s], den);
-      }
-      den = warp_sum(den);
-      if (lane == 0) inv[h] = 1.0f / den;
-    }
-    __syncthreads();
-    for (int i = tid; i < G * HD; i += blockDim.x) {
-      const int h = i / HD, d = i % HD;
-      const float* po = a.part_o + ((int64_t)b * a.nh + kvh * G + h) * S * HD + d;
-      const float* wh = pm + h * S;
-      float num0 = 0.f, num1 = 0.f, num2 = 0.f, num3 = 0.f;
-      int s = 0;
-      for (; s + 4 <= S; s += 4) {
-        num0 = fmaf(wh[s], __ldcg(po + (int64_t)s * HD), num0);
-        num1 = fmaf(wh[s + 1], __ldcg(po + (int64_t)(s + 1) * HD), num1);
-        num2 = fmaf(wh[s + 2], __ldcg(po + (int64_t)(s + 2) * HD), num2);
-        num3 = fmaf(wh[s + 3], __ldcg(po + (int64_t)(s + 3) * HD), num3);
-      }
-      for (; s < S; s++) num0 = fmaf(wh[s], __ldcg(po + (int64_t)s * HD), num0);
-      a.out[(int64_t)b * a.out_ld + (int64_t)(kvh * G + h) * HD + d] = ((num0 + num1) + (num2 + num3)) * inv[h];
-    }
-    if (tid == 0) *cnt = 0;
-  }
-  pdl_launch();
 }
 
 }  // namespace
 
 size_t attn_smem_bytes(int G, int chunk_max) {
-  const int cpad = (chunk_max + 3) & ~3;
-  return (size_t)AT_NS * AT_STAGE + (size_t)G * 4 * AT_QSTRIDE * 4 + (size_t)G * cpad * 4 +
-         (size_t)AT_WARPS * G * HD * 4 + (2 * G + 2) * 4 + 8 + AT_NS * 8;
+  const AttnSmem L{G, (chunk_max + 63) & ~63};
+  return L.total();
 }
 
 int launch_attn(cudaStream_t s, const AttnArgs& a, int G, int splits, int batch, int nkv, bool pdl) {

@@ -65,8 +65,10 @@ inline int64_t qmv_warp_grid(int64_t units, int nw, int sms) {
 inline void qmv_scratch_need(int64_t tiles, int64_t nunit, int sms, size_t* split_bytes,
                              int64_t* counts) {
   int64_t worst = 0;
-  for (int nw : {8, 16}) {
-    const int64_t units = tiles * nunit, grid = qmv_warp_grid(units, nw, sms);
+  const int cfgs[4][2] = {{8, 1}, {16, 1}, {8, 2}, {4, 2}};  // (warps, grid cap in SMs)
+  for (const auto& cf : cfgs) {
+    const int nw = cf[0];
+    const int64_t units = tiles * nunit, grid = qmv_warp_grid(units, nw, cf[1] * sms);
     const int64_t minr = units / (grid * nw);
     const int64_t maxc = minr > 0 ? (nunit - 1 + minr - 1) / minr + 1 : nunit + 1;
     if (maxc > worst) worst = maxc;
@@ -146,7 +148,8 @@ int launch_repack(si_ctx* c, int qt, const uint8_t* gguf, int64_t rows, int64_t 
                   int64_t row0, int64_t nrows, void* dst);
 int launch_dequant(si_ctx* c, const si_weight* w, float* out);
 // Activation preparation modes and matvec epilogues.
-enum { SI_PREP_PLAIN = 0, SI_PREP_RMSNORM = 1, SI_PREP_SILU_MUL = 2 };
+enum { SI_PREP_PLAIN = 0, SI_PREP_RMSNORM = 1, SI_PREP_SILU_MUL = 2, SI_PREP_ATTN_MERGE = 3 };
+constexpr int SI_ATTN_MAX_SPLITS = 511;
 enum { SI_EPI_STORE = 0, SI_EPI_ADD = 1 };
 constexpr int SI_MAX_K = 49152;  // activation length limit of the prep kernel (smem)
 constexpr int SI_MAX_BATCH = 16;

@@ -5,8 +5,8 @@
 // Per layer (batch B, position pos):
 //   prep   RmsNorm(x) * attn_norm -> activation fragments        (:86)
 //   qmv    [Wq; Wk; Wv] -> qkv                                    (:89-91)
-//   attn   RoPE(q, k), KV append, split-KV attention -> attn      (:94-129)
-//   prep   attn -> fragments
+//   attn   RoPE(q, k), KV append, split-KV attention -> partials   (:94-129)
+//   prep   merge of the splits -> fragments
 //   qmv    Wo, accumulated into x (the residual add)              (:132-135)
 //   prep   RmsNorm(x) * ffn_norm                                  (:140)
 //   qmv    [Wgate; Wup] -> gu                                     (:143-144)
@@ -71,12 +71,12 @@ __device__ __forceinline__ float weight_elem(int qt, const uint8_t* __restrict__
 // x[b] = row tokens[b] of the token embedding (Transformer.cs:76).
 __global__ void k_embed(const StepParams* __restrict__ p, int qt, const uint8_t* __restrict__ W,
                         int64_t nblk, int64_t vocab, int h, float* __restrict__ x) {
+  pdl_launch();  // dependents may start their independent prologue now
   pdl_wait();
   const int b = blockIdx.y;
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   const int tok = p->tokens[b];
   if (col < h && tok >= 0 && tok < vocab) x[(int64_t)b * h + col] = weight_elem(qt, W, nblk, tok, col);
-  pdl_launch();
 }
 
 // Greedy selection (SamplingPipeline.ArgMax, SamplingPipeline.cs:83-89):
@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
                                                  int* __restrict__ out) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_launch();  // dependents may start their independent prologue now
   pdl_wait();
   const int b = blockIdx.x;
   const float* x = logits + (int64_t)b * vocab;
@@ -125,7 +126,6 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
     }
     if (l == 0) out[b] = (isnan(x[0]) || bi < 0) ? 0 : bi;
   }
-  pdl_launch();
 }
 
 // End of a step: the greedy tokens become the next step's inputs at the next
@@ -133,6 +133,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
 // InferenceEngine.cs:96-131, with greedy sampling) and are appended to the
 // history.
 __global__ void k_advance(StepParams* __restrict__ p, const int* __restrict__ argmax) {
+  pdl_launch();  // dependents may start their independent prologue now
   pdl_wait();
   const int b = threadIdx.x;
   const int B = p->batch;
@@ -157,7 +158,8 @@ __global__ void k_kv_synth(__half* __restrict__ cache, uint64_t key, int len, in
   if (i >= n) return;
   const int d = (int)(i % 128), kvh = (int)((i / 128) % nkv);
   const int64_t pos = i / (128 * nkv);
-  cache[((int64_t)kvh * max_seq + pos) * 128 + d] = __ushort_as_half(si_synth_f16(key, (uint64_t)i, 1.0f));
+  cache[((int64_t)kvh * max_seq + pos) * 128 + kv_swz(d, (int)pos)] =
+      __ushort_as_half(si_synth_f16(key, (uint64_t)i, 1.0f));
 }
 
 __global__ void k_f32_synth(float* __restrict__ out, uint64_t key, int64_t n, float mean, float sigma) {
@@ -172,7 +174,7 @@ __global__ void k_kv_scatter(__half* __restrict__ cache, const uint16_t* __restr
   if (i >= (int64_t)n * nkv * 128) return;
   const int d = (int)(i % 128), kvh = (int)((i / 128) % nkv);
   const int64_t t = i / (128 * nkv);
-  cache[((int64_t)kvh * max_seq + pos0 + t) * 128 + d] = __ushort_as_half(src[i]);
+  cache[((int64_t)kvh * max_seq + pos0 + t) * 128 + kv_swz(d, (int)(pos0 + t))] = __ushort_as_half(src[i]);
 }
 
 cudaLaunchConfig_t cfg_of(cudaStream_t s, dim3 g, dim3 b, size_t smem, bool pdl, cudaLaunchAttribute* attr) {
@@ -212,11 +214,10 @@ struct si_model {
   __half* kcache = nullptr;
   __half* vcache = nullptr;
   float* rope = nullptr;
-  float *x = nullptr, *qkv = nullptr, *attn = nullptr, *gu = nullptr, *logits = nullptr;
+  float *x = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr;
   int* argmax = nullptr;
   uint8_t* xprep = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
-  int* attn_cnt = nullptr;
   StepParams* dparams = nullptr;
   StepParams* hparams = nullptr;  // pinned
   int* hargmax = nullptr;         // pinned
@@ -335,18 +336,18 @@ int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int 
   a.chunk_max = (c.max_seq + S - 1) / S;
   a.part_o = m->part_o;
   a.part_ml = m->part_ml;
-  a.counters = m->attn_cnt;
-  a.out = out;
-  a.out_ld = (int64_t)c.n_heads * c.head_dim;
   a.err = m->c->dev_err;
-  return launch_attn(m->c->stream, a, m->G, S, B, c.n_kv_heads, pdl);
+  SI_TRY(launch_attn(m->c->stream, a, m->G, S, B, c.n_kv_heads, pdl));
+  // merge the splits into the O-projection's prepared input (and into `out`)
+  return launch_prep(m->c->stream, m->part_o, S, m->part_ml, nullptr, 0.f, SI_PREP_ATTN_MERGE,
+                     c.n_heads * c.head_dim, B, out, m->xprep, pdl);
 }
 
 // The whole decode step on the context stream (eager or under capture).
 int enqueue_step(si_model* m, int B) {
   const si_model_config& c = m->cfg;
   cudaStream_t s = m->c->stream;
-  const int h = c.hidden, inter = c.intermediate, qd = c.n_heads * c.head_dim;
+  const int h = c.hidden, inter = c.intermediate;
   const QmvBuffers qb = m->c->qmv();
   {
     cudaLaunchAttribute attr[1];
@@ -358,8 +359,7 @@ int enqueue_step(si_model* m, int B) {
     SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
                        nullptr, m->xprep, true));
     SI_TRY(launch_qmv(s, m->wqkv[l], m->xprep, B, m->qkv, SI_EPI_STORE, qb, true));
-    SI_TRY(enqueue_attention(m, l, m->qkv, m->attn, B, true));
-    SI_TRY(launch_prep(s, m->attn, qd, nullptr, nullptr, 0.f, SI_PREP_PLAIN, qd, B, nullptr, m->xprep, true));
+    SI_TRY(enqueue_attention(m, l, m->qkv, nullptr, B, true));
     SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
     SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
                        nullptr, m->xprep, true));
@@ -528,18 +528,15 @@ SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model*
   ALLOC(rope, (size_t)c.max_seq * c.head_dim * 4);
   ALLOC(x, (size_t)B * h * 4);
   ALLOC(qkv, (size_t)B * m->qkv_rows * 4);
-  ALLOC(attn, (size_t)B * qd * 4);
   ALLOC(gu, (size_t)B * 2 * c.intermediate * 4);
   ALLOC(logits, (size_t)B * c.vocab * 4);
   ALLOC(argmax, (size_t)SI_MAX_BATCH * 4);
   ALLOC(xprep, xprep_bytes(m->Kmax, B));
   ALLOC(part_o, (size_t)B * c.n_heads * m->splits_max * c.head_dim * 4);
   ALLOC(part_ml, (size_t)B * c.n_heads * m->splits_max * 2 * 4);
-  ALLOC(attn_cnt, (size_t)B * c.n_kv_heads * 4);
   ALLOC(dparams, sizeof(StepParams));
 #undef ALLOC
-  cudaError_t e = cudaMemset(m->attn_cnt, 0, (size_t)B * c.n_kv_heads * 4);
-  if (e == cudaSuccess) e = cudaMemset(m->kcache, 0, kv_elems * 2);
+  cudaError_t e = cudaMemset(m->kcache, 0, kv_elems * 2);
   if (e == cudaSuccess) e = cudaMemset(m->vcache, 0, kv_elems * 2);
   if (e == cudaSuccess) e = cudaMallocHost(&m->hparams, sizeof(StepParams));
   if (e == cudaSuccess) e = cudaMallocHost(&m->hargmax, sizeof(int) * SI_MAX_BATCH);

@@ -27,11 +27,14 @@ struct AttnArgs {
   int chunk_max;      // positions per split at the longest context
   float* part_o;      // [batch][nh][splits][head_dim]
   float* part_ml;     // [batch][nh][splits][2]
-  int* counters;      // [batch][nkv], zero between launches
-  float* out;
-  int64_t out_ld;
   int* err;
 };
+
+// KV cache rows are 128 f16 (256 B).  The 16-byte chunk c (dims 8c..8c+7) of
+// position p is stored at chunk c ^ (p & 7), so that eight consecutive
+// positions read at one chunk index hit eight different bank groups
+// (ldmatrix without conflicts).  Offset in halves of dim d of position p:
+__host__ __device__ __forceinline__ int kv_swz(int d, int p) { return (((d >> 3) ^ (p & 7)) << 3) | (d & 7); }
 
 size_t attn_smem_bytes(int G, int chunk_max);
 int launch_attn(cudaStream_t s, const AttnArgs& a, int G, int splits, int batch, int nkv, bool pdl);

@@ -65,7 +65,13 @@ __device__ __forceinline__ int64_t xprep_off(int mg, int nunit, int u, int LW) {
 //   mode 1: v = RmsNorm(x) * w   (TensorOps.cs:135-145); every CTA of a row
 //           computes the row's sum of squares in the same order
 //   mode 2: v = SiLU(x) * x2     (TensorOps.cs:191-195 then :169-185)
-// x row b starts at x + b*ldx (x2 likewise).  The unit's values are scaled by
+//   mode 3: v = attention output merged from split-KV partials: x is
+//           o [B][K/128 heads][S][128] (unnormalised), x2 is (max, sum)
+//           [B][heads][S][2], ldx = S.  For head h: M = max_s m_s,
+//           w_s = exp(m_s - M), v = sum_s w_s o_s / sum_s w_s l_s -- the
+//           softmax of Transformer.cs:99-129 over all positions, assembled
+//           from the splits.
+// x row b starts at x + b*ldx (x2 likewise; modes 0-2).  The unit's values are scaled by
 // 2^e (max |v * 2^e| in [2^13, 2^14)), split into f16 hi/lo fragments for
 // the lanes 8(b%4) .. 8(b%4)+7 of MMA group b/4, and 2^-e is stored with them.
 // ---------------------------------------------------------------------------
@@ -76,13 +82,55 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
                                               uint8_t* __restrict__ xprep) {
   __shared__ float sv[256];
   __shared__ float red[8];
+  __shared__ float mw[2][SI_ATTN_MAX_SPLITS + 1];  // mode 3: merge weights of the unit's two heads
   const int u = blockIdx.x, b = blockIdx.y, mg = b >> 2, cb = b & 3;
   const int Bm = min(4, B - 4 * mg), LW = 8 * Bm;
   const int nunit = gridDim.x;
   const int tid = threadIdx.x, k = 256 * u + tid;
+  pdl_launch();  // dependents may start their independent prologue now
   pdl_wait();
   const float* xb = x + (int64_t)b * ldx;
   float scale = 1.f;
+  float v = 0.f;
+  if (mode == 3) {
+    const int S = ldx, nhd = K / 128;
+    const int warp = tid >> 5, lane = tid & 31;
+    if (warp < 2 && 2 * u + warp < nhd) {  // statistics of head 2u + warp
+      const float2* ml = (const float2*)x2 + ((int64_t)b * nhd + 2 * u + warp) * S;
+      float M = -INFINITY;
+      for (int s = lane; s < S; s += 32) M = fmaxf(M, ml[s].x);
+      M = warp_max(M);
+      float den = 0.f;
+      for (int s = lane; s < S; s += 32) {
+        const float2 p = ml[s];
+        const float w = p.x == -INFINITY ? 0.f : expf(p.x - M);
+        mw[warp][s] = w;
+        den = fmaf(w, p.y, den);
+      }
+      den = warp_sum(den);
+      if (lane == 0) mw[warp][SI_ATTN_MAX_SPLITS] = 1.0f / den;
+    }
+    __syncthreads();
+    if (k < K) {
+      const int hl = tid >> 7, h = 2 * u + hl, d = tid & 127;
+      const float* po = x + ((int64_t)b * nhd + h) * S * 128 + d;
+      const float* wh = mw[hl];
+      float n0 = 0.f, n1 = 0.f;
+      for (int s0 = 0; s0 < S; s0 += 16) {
+        float o[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+          if (s0 + j < S) o[j] = po[(int64_t)(s0 + j) * 128];
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          if (s0 + j < S) n0 = fmaf(wh[s0 + j], o[j], n0);
+          if (s0 + j + 1 < S) n1 = fmaf(wh[s0 + j + 1], o[j + 1], n1);
+        }
+      }
+      v = (n0 + n1) * wh[SI_ATTN_MAX_SPLITS];
+      if (xout) xout[(int64_t)b * K + k] = v;
+    }
+  }
   if (mode == 1) {
     float ss = 0.f;
     for (int i = tid; i < K; i += 256) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
@@ -93,8 +141,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
     for (int i = 0; i < 8; i++) t += red[i];
     scale = 1.0f / sqrtf(t / (float)K + eps);
   }
-  float v = 0.f;
-  if (k < K) {
+  if (k < K && mode != 3) {
     if (mode == 1) {
       v = __fmul_rn(__fmul_rn(xb[k], scale), nw[k]);
     } else if (mode == 2) {
@@ -146,7 +193,6 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
     *(float*)(unit + 132 * LW + 4 * cb) = ldexpf(1.0f, -e);
   }
   __syncthreads();
-  pdl_launch();
 }
 
 // ---------------------------------------------------------------------------
@@ -449,7 +495,7 @@ __device__ __forceinline__ void store_tile(float* __restrict__ y, int64_t rows, 
 }
 
 template <int QT, int EPI, int B, int NW, int NS>
-__global__ void __launch_bounds__(NW * 32, 1)
+__global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
     k_qmv_warp(const uint8_t* __restrict__ W, int nblk, int64_t rows, int tiles,
                const uint8_t* __restrict__ xprep, float* __restrict__ y, QmvScratch scr) {
   using Cfg = WarpCfg<QT, B, NW, NS>;
@@ -492,6 +538,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       if (++u == nunit) u = 0;
     }
   }
+  pdl_launch();  // dependents may start their independent prologue now
   pdl_wait();
   if (lane == 0) {
     int u = c0U;
@@ -510,6 +557,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
   const bool on = lane < LW, oni = 8 * t < LW;
   const int xf_off = on ? WB + lane * 16 : -1;  // -1: read the zero region
   float tg[1] = {0.f}, tg8[1] = {0.f};
+  float p0a = 0.f, p0b = 0.f, p1a = 0.f, p1b = 0.f;  // partials of the shared first / last tile
+  bool has0 = false, has1 = false;
   bool ok = true;
   uint32_t ph = 0;
   int cT = (int)c0T, cU = c0U;
@@ -553,29 +602,14 @@ __global__ void __launch_bounds__(NW * 32, 1)
         const int64_t t0 = tile_first, t1 = tile_first + nunit;  // tile's unit range
         if (t0 >= ub && t1 <= ue) {
           store_tile<EPI, B>(y, rows, cT, lane, tg[0], tg8[0]);
-        } else {
-          // contributors: the warps owning units t0 .. t1-1 (owner(x) = the last
-          // warp whose range starts at or before x; every range is non-empty)
-          const int64_t wf = ((t0 + 1) * GW - 1) / U, wl = (t1 * GW - 1) / U;
-          const int ncon = (int)(wl - wf + 1), slot = (int)(gw - wf);
-          float* base = scr.split + (int64_t)cT * scr.maxc * 64;
-          base[slot * 64 + lane] = tg[0];
-          base[slot * 64 + 32 + lane] = tg8[0];
-          __threadfence();
-          __syncwarp();
-          int prev = 0;
-          if (lane == 0) prev = atomicAdd(scr.count + cT, 1);
-          prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
-          if (prev == ncon - 1) {  // last contributor: add the slots in warp order
-            __threadfence();
-            float a = 0.f, b8 = 0.f;
-            for (int j = 0; j < ncon; j++) {
-              a += *(volatile float*)(base + j * 64 + lane);
-              b8 += *(volatile float*)(base + j * 64 + 32 + lane);
-            }
-            store_tile<EPI, B>(y, rows, cT, lane, a, b8);
-            if (lane == 0) scr.count[cT] = 0;
-          }
+        } else if (cT == (int)c0T) {  // first tile of the range, shared with other warps
+          p0a = tg[0];
+          p0b = tg8[0];
+          has0 = true;
+        } else {  // last tile of the range, shared
+          p1a = tg[0];
+          p1b = tg8[0];
+          has1 = true;
         }
         tg[0] = tg8[0] = 0.f;
         cU = 0;
@@ -586,7 +620,322 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
     ph ^= 1u;
   }
-  pdl_launch();
+  // ---- tiles shared between warps ----
+  // Every warp has drained its ring; the ring memory now holds each warp's (at
+  // most two) shared-tile partials.  The first contributor of a tile inside
+  // this CTA adds the CTA's partials in warp order.  A tile that also spans
+  // other CTAs goes through global scratch: one slot per CTA, and the last
+  // CTA to arrive (per-tile counter) adds the slots in CTA order.  The result
+  // does not depend on timing.
+  __syncthreads();
+  float* part = (float*)smem;  // [NW][2][64]
+  part[(warp * 2 + 0) * 64 + lane] = p0a;
+  part[(warp * 2 + 0) * 64 + 32 + lane] = p0b;
+  part[(warp * 2 + 1) * 64 + lane] = p1a;
+  part[(warp * 2 + 1) * 64 + 32 + lane] = p1b;
+  __syncthreads();
+  const int64_t cw0 = (int64_t)blockIdx.x * NW;  // global id of this CTA's warp 0
+#pragma unroll 1
+  for (int sl = 0; sl < 2; sl++) {
+    if (!(sl == 0 ? has0 : has1) || !ok) continue;
+    const int64_t T = sl == 0 ? c0T : (int64_t)cT - 1;
+    const int64_t t0 = T * nunit, t1 = t0 + nunit;
+    // owner(x) = the last warp whose range starts at or before unit x
+    const int64_t wf = ((t0 + 1) * GW - 1) / U, wl = (t1 * GW - 1) / U;
+    const int64_t jf = wf > cw0 ? wf : cw0, jl = wl < cw0 + NW - 1 ? wl : cw0 + NW - 1;
+    if (gw != jf) continue;  // another warp of this CTA combines this tile
+    float a = 0.f, b8 = 0.f;
+    for (int64_t j = jf; j <= jl; j++) {
+      const int slot = (U * j / GW) / nunit == T ? 0 : 1;  // T is warp j's first tile?
+      a += part[((j - cw0) * 2 + slot) * 64 + lane];
+      b8 += part[((j - cw0) * 2 + slot) * 64 + 32 + lane];
+    }
+    if (wf >= cw0 && wl < cw0 + NW) {
+      store_tile<EPI, B>(y, rows, (int)T, lane, a, b8);
+      continue;
+    }
+    const int64_t cf = wf / NW, cl = wl / NW;
+    const int ncon = (int)(cl - cf + 1), cslot = (int)(blockIdx.x - cf);
+    float* base = scr.split + T * scr.maxc * 64;
+    base[cslot * 64 + lane] = a;
+    base[cslot * 64 + 32 + lane] = b8;
+    __threadfence();
+    __syncwarp();
+    int prev = 0;
+    if (lane == 0) prev = atomicAdd(scr.count + T, 1);
+    prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
+    if (prev == ncon - 1) {  // last CTA: add the slots in CTA order
+      __threadfence();
+      float va[8], vb[8];
+      float sa = 0.f, sb = 0.f;
+      for (int j0 = 0; j0 < ncon; j0 += 8) {
+        const int nj = ncon - j0 < 8 ? ncon - j0 : 8;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          if (j < nj) {
+            va[j] = __ldcg(base + (j0 + j) * 64 + lane);
+            vb[j] = __ldcg(base + (j0 + j) * 64 + 32 + lane);
+          }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          if (j < nj) {
+            sa += va[j];
+            sb += vb[j];
+          }
+      }
+      store_tile<EPI, B>(y, rows, (int)T, lane, sa, sb);
+      if (lane == 0) scr.count[T] = 0;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Batch-1 Q4_K kernel.  Same persistent layout as k_qmv_warp (148 CTAs, per-
+// warp contiguous ranges, deterministic split-tile combine), with three
+// changes that cut the instructions per unit roughly in half:
+//  * the whole prepared activation vector is copied into shared memory once
+//    per CTA, so the ring carries only weights, two units per stage in one
+//    bulk copy;
+//  * the sub-block scales are applied after the MMA: k-tiles of sub-block s
+//    accumulate into MMA column 2(s%4) (hi) / 2(s%4)+1 (lo) -- the lanes of
+//    that column class supply the activation fragment, the others zeros --
+//    and sub-blocks 0-3 and 4-7 use two accumulators, so lane (g, t) ends a
+//    unit holding the partial sums of sub-blocks t and t+4 of rows g and g+8
+//    and scales them by sc * d once (the nibbles go to the MMA unscaled);
+//  * shared-memory offsets are 32-bit.
+// Rows g+8 read their nibbles from bits 4-7 (16 q), compensated in d.
+// ---------------------------------------------------------------------------
+struct Q1Cfg {
+  static constexpr int US = 2, TBB = 2304, SB = US * TBB;  // bytes per ring stage
+  static constexpr int XB = 132 * 8 + 16;                   // prepared bytes per column unit
+  static constexpr int ZERO = 1024;                         // zero fragments: 8 groups x 128 B
+  static size_t smem(int NW, int NS, int nunit) {
+    return (size_t)NW * NS * SB + ZERO + (size_t)nunit * XB + (size_t)(NW * NS + 1) * 8;
+  }
+};
+
+__device__ __forceinline__ float red4(float v) {
+  v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+  return v + __shfl_xor_sync(0xFFFFFFFFu, v, 2);
+}
+
+// exact small integer -> f32: 2^23 + v as bits, minus 2^23
+__device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float(bits) - 8388608.f; }
+
+template <int EPI, int NW, int NS>
+__global__ void __launch_bounds__(NW * 32, 1)
+    k_qmv1(const uint8_t* __restrict__ W, int nunit, int64_t rows, int tiles, const uint8_t* __restrict__ xprep,
+           float* __restrict__ y, QmvScratch scr) {
+  constexpr int SB = Q1Cfg::SB, TBB = Q1Cfg::TBB, XB = Q1Cfg::XB;
+  constexpr int RING = NW * NS * SB;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  uint8_t* const ring = smem + warp * NS * SB;
+  const uint8_t* const zero = smem + RING;
+  const uint8_t* const xs = zero + Q1Cfg::ZERO;
+  const uint32_t bar_x = smem_u32(xs + nunit * XB);
+  const uint32_t bar0 = bar_x + 8 + warp * NS * 8;
+
+  const int64_t P = (int64_t)tiles * nunit / 2;  // unit pairs
+  const int64_t GW = (int64_t)gridDim.x * NW, gw = (int64_t)blockIdx.x * NW + warp;
+  const int64_t pb = P * gw / GW, pe = P * (gw + 1) / GW;
+  const int npair = (int)(pe - pb);
+  const int64_t ub = 2 * pb;
+
+  for (int i = threadIdx.x; i < Q1Cfg::ZERO / 16; i += blockDim.x) ((uint4*)(smem + RING))[i] = make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) mbar_init(bar_x, 1);
+  if (lane == 0)
+    for (int s = 0; s < NS; s++) mbar_init(bar0 + 8 * s, 1);
+  mbar_fence_init();
+  __syncthreads();
+  const uint8_t* wsrc = W + ub * TBB;  // units are contiguous in range order
+  const int pre = npair < NS ? npair : NS;
+  if (lane == 0)
+    for (int s = 0; s < pre; s++) {
+      mbar_arrive_expect_tx(bar0 + 8 * s, SB);
+      bulk_g2s(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s);
+    }
+  pdl_launch();  // dependents may start their independent prologue now
+  pdl_wait();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(bar_x, (uint32_t)(nunit * XB));
+    bulk_g2s(smem_u32(xs), xprep, (uint32_t)(nunit * XB), bar_x);
+  }
+  bool ok = mbar_wait_bounded(bar_x, 0);
+  if (!ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
+
+  // per-lane constants
+  const int cls = lane >> 3;                                   // MMA column class
+  const int xl = (lane & 7) * 16;                              // fragment slot in a group
+  const int sh = 8 * t;                                        // byte of sub-blocks t, t+4
+  const uint32_t msel = (t & 1) ? 0x5342u : 0x5140u;
+  const uint8_t* const xsum0 = lane < 8 ? xs + 1024 + lane * 4 : zero;
+  const int xsum_step = lane < 8 ? XB : 0;
+
+  float tg = 0.f, tg8 = 0.f;
+  float p0a = 0.f, p0b = 0.f, p1a = 0.f, p1b = 0.f;
+  bool has0 = false, has1 = false;
+  const int64_t c0T = ub / nunit;
+  int64_t cT = c0T;
+  int cU = (int)(ub - c0T * nunit);  // even
+  const bool first_partial = cU != 0;
+  uint32_t ph = 0;
+
+  auto unit = [&](const uint8_t* st, int cu) {
+    const uint8_t* xu = xs + cu * XB;
+    const uint4 h0 = *(const uint4*)(st + 16 * g), h1 = *(const uint4*)(st + 16 * (g + 8));
+    const uint8_t* xb[4];
+#pragma unroll
+    for (int c = 0; c < 4; c++) xb[c] = c == cls ? xu + xl : zero;
+    // mins: A[row][k] = m_k(row) (k < 8), B[k][col] = X_k(col) * 2^-5 in columns 0 (hi), 1 (lo)
+    const uint32_t mnl0 = h0.z & 0x3F3F3F3Fu, mnh0 = ((h0.w >> 4) & 0x0F0F0F0Fu) | ((h0.z >> 2) & 0x30303030u);
+    const uint32_t mnl1 = h1.z & 0x3F3F3F3Fu, mnh1 = ((h1.w >> 4) & 0x0F0F0F0Fu) | ((h1.z >> 2) & 0x30303030u);
+    const uint32_t am0 = hsub2_u32(prmt(t < 2 ? mnl0 : mnh0, 0x64646464u, msel), 0x64006400u);
+    const uint32_t am1 = hsub2_u32(prmt(t < 2 ? mnl1 : mnh1, 0x64646464u, msel), 0x64006400u);
+    float Cm[4] = {0.f, 0.f, 0.f, 0.f}, C0[4] = {0.f, 0.f, 0.f, 0.f}, C1[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816(Cm, am0, am1, 0u, 0u, *(const uint32_t*)(xsum0 + cu * xsum_step), 0u);
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      const uint4 q = *(const uint4*)(st + 256 + c * 512 + lane * 16);
+#pragma unroll
+      for (int hs = 0; hs < 2; hs++) {
+        const int jj = 2 * c + hs;  // sub-block
+        const uint4 xv = *(const uint4*)(xb[jj & 3] + jj * 128);
+#pragma unroll
+        for (int kk = 0; kk < 2; kk++) {
+          const int i = 2 * hs + kk;
+          const uint32_t w = i == 0 ? q.x : i == 1 ? q.y : i == 2 ? q.z : q.w;
+          const uint32_t w8 = w >> 8;
+          float* acc = jj < 4 ? C0 : C1;
+          mma16816(acc, w & 0x000F000Fu, w & 0x00F000F0u, w8 & 0x000F000Fu, w8 & 0x00F000F0u,
+                   kk ? xv.z : xv.x, kk ? xv.w : xv.y);
+        }
+      }
+    }
+    // scales of sub-blocks t and t+4 (GetScaleMinK4), rows g and g+8
+    const uint32_t ys0 = h0.y >> sh, ws0 = h0.w >> sh, ys1 = h1.y >> sh, ws1 = h1.w >> sh;
+    const float sa0 = magic_f(lop3_and_or(ys0, 0x3Fu, 0x4B000000u));
+    const float sb0 = magic_f(lop3_and_or(ws0, 0x0Fu, lop3_and_or(ys0 >> 2, 0x30u, 0x4B000000u)));
+    const float sa1 = magic_f(lop3_and_or(ys1, 0x3Fu, 0x4B000000u));
+    const float sb1 = magic_f(lop3_and_or(ws1, 0x0Fu, lop3_and_or(ys1 >> 2, 0x30u, 0x4B000000u)));
+    const float inv = *(const float*)(xu + 1056);
+    const float d0 = h2f_lo(h0.x) * (16777216.f * inv), dm0 = h2f_hi(h0.x) * (32.f * inv);
+    const float d1 = h2f_lo(h1.x) * (1048576.f * inv), dm1 = h2f_hi(h1.x) * (32.f * inv);
+    tg += d0 * (sa0 * (C0[0] + C0[1]) + sb0 * (C1[0] + C1[1])) - dm0 * (Cm[0] + Cm[1]);
+    tg8 += d1 * (sa1 * (C0[2] + C0[3]) + sb1 * (C1[2] + C1[3])) - dm1 * (Cm[2] + Cm[3]);
+  };
+
+  for (int k0 = 0; k0 < npair; k0 += NS) {
+#pragma unroll
+    for (int s = 0; s < NS; s++) {
+      const int k = k0 + s;
+      if (k >= npair) break;
+      if (!mbar_wait_bounded(bar0 + 8 * s, ph)) {  // waited even after a failure
+        if (ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
+        ok = false;
+      }
+      uint8_t* st = ring + s * SB;
+      if (ok) {
+        unit(st, cU);
+        unit(st + TBB, cU + 1);
+      }
+      __syncwarp();
+      if (k + NS < npair && lane == 0) {  // refill this stage with pair k + NS
+        mbar_arrive_expect_tx(bar0 + 8 * s, SB);
+        bulk_g2s(smem_u32(st), wsrc + (int64_t)(k + NS) * SB, SB, bar0 + 8 * s);
+      }
+      cU += 2;
+      if (cU == nunit) {  // this warp's part of tile cT is done
+        const float a = red4(tg), b8 = red4(tg8);
+        if (cT == c0T && first_partial) {
+          p0a = a;
+          p0b = b8;
+          has0 = true;
+        } else {
+          store_tile<EPI, 1>(y, rows, (int)cT, lane, a, b8);
+        }
+        tg = tg8 = 0.f;
+        cU = 0;
+        cT++;
+      }
+    }
+    ph ^= 1u;
+  }
+  int64_t T1 = cT;
+  if (cU != 0) {  // the range ends inside tile cT
+    const float a = red4(tg), b8 = red4(tg8);
+    if (cT == c0T && first_partial) {
+      p0a = a;
+      p0b = b8;
+      has0 = true;
+    } else {
+      p1a = a;
+      p1b = b8;
+      has1 = true;
+    }
+  }
+  // ---- tiles shared between warps (same scheme as k_qmv_warp, in pairs) ----
+  __syncthreads();
+  float* part = (float*)smem;  // [NW][2][64]
+  part[(warp * 2 + 0) * 64 + lane] = p0a;
+  part[(warp * 2 + 0) * 64 + 32 + lane] = p0b;
+  part[(warp * 2 + 1) * 64 + lane] = p1a;
+  part[(warp * 2 + 1) * 64 + 32 + lane] = p1b;
+  __syncthreads();
+  const int64_t cw0 = (int64_t)blockIdx.x * NW;
+  const int64_t npt = nunit / 2;  // pairs per tile
+#pragma unroll 1
+  for (int sl = 0; sl < 2; sl++) {
+    if (!(sl == 0 ? has0 : has1) || !ok) continue;
+    const int64_t T = sl == 0 ? c0T : T1;
+    const int64_t q0 = T * npt, q1 = q0 + npt;  // tile's pair range
+    const int64_t wf = ((q0 + 1) * GW - 1) / P, wl = (q1 * GW - 1) / P;
+    const int64_t jf = wf > cw0 ? wf : cw0, jl = wl < cw0 + NW - 1 ? wl : cw0 + NW - 1;
+    if (gw != jf) continue;
+    float a = 0.f, b8 = 0.f;
+    for (int64_t j = jf; j <= jl; j++) {
+      const int64_t fj = 2 * (P * j / GW);  // first unit of warp j
+      const int slot = (fj / nunit == T && fj % nunit != 0) ? 0 : 1;
+      a += part[((j - cw0) * 2 + slot) * 64 + lane];
+      b8 += part[((j - cw0) * 2 + slot) * 64 + 32 + lane];
+    }
+    if (wf >= cw0 && wl < cw0 + NW) {
+      store_tile<EPI, 1>(y, rows, (int)T, lane, a, b8);
+      continue;
+    }
+    const int64_t cf = wf / NW, cl = wl / NW;
+    const int ncon = (int)(cl - cf + 1), cslot = (int)(blockIdx.x - cf);
+    float* base = scr.split + T * scr.maxc * 64;
+    base[cslot * 64 + lane] = a;
+    base[cslot * 64 + 32 + lane] = b8;
+    __threadfence();
+    __syncwarp();
+    int prev = 0;
+    if (lane == 0) prev = atomicAdd(scr.count + T, 1);
+    prev = __shfl_sync(0xFFFFFFFFu, prev, 0);
+    if (prev == ncon - 1) {
+      __threadfence();
+      float sa = 0.f, sb = 0.f;
+      for (int j0 = 0; j0 < ncon; j0 += 8) {
+        float va[8], vb[8];
+        const int nj = ncon - j0 < 8 ? ncon - j0 : 8;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          if (j < nj) {
+            va[j] = __ldcg(base + (j0 + j) * 64 + lane);
+            vb[j] = __ldcg(base + (j0 + j) * 64 + 32 + lane);
+          }
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          if (j < nj) {
+            sa += va[j];
+            sb += vb[j];
+          }
+      }
+      store_tile<EPI, 1>(y, rows, (int)T, lane, sa, sb);
+      if (lane == 0) scr.count[T] = 0;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -607,6 +956,7 @@ __global__ void __launch_bounds__(256) k_qmv_reg(const uint8_t* __restrict__ W, 
   float tg[NMG], tg8[NMG];
 #pragma unroll
   for (int mg = 0; mg < NMG; mg++) tg[mg] = tg8[mg] = 0.f;
+  pdl_launch();  // dependents may start their independent prologue now
   pdl_wait();
   for (int u = warp; u < nunit; u += QMV_WARPS) {
     GlobLd ld[NMG];
@@ -625,7 +975,6 @@ __global__ void __launch_bounds__(256) k_qmv_reg(const uint8_t* __restrict__ W, 
     else if (QT == SI_Q6_K) unit_q6k<NMG>(ld, lane, tg, tg8);
     else unit_q80<NMG>(ld, lane, min(QPU, nblk - u * QPU), tg, tg8);
   }
-  pdl_launch();
   qmv_epilogue<NMG, EPI>(tg, tg8, B, rows, y, (int)blockIdx.x);
 }
 
@@ -683,9 +1032,41 @@ int launch_warp_cfg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, fl
 }
 
 // 16 warps with the deepest ring (<= 4) that fits, else 8 warps.
+// Largest ring (NS <= NS0 stages) of NW warps within `SMALL_MAX` bytes of
+// shared memory, so that two CTAs -- this launch's and the next one's -- fit
+// on one SM; -1 if none does.
+constexpr int SMALL_MAX = 112 * 1024;
+template <int QT, int EPI, int B, int NW, int NS>
+int launch_fit(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y, const ScratchCap& scr,
+               int gridcap, bool pdl) {
+  if constexpr (NS < 2) {
+    return -1;
+  } else if constexpr (WarpCfg<QT, B, NW, NS>::SMEM <= SMALL_MAX) {
+    return launch_warp_cfg<QT, EPI, B, NW, NS>(s, w, xprep, y, scr, gridcap, pdl);
+  } else {
+    return launch_fit<QT, EPI, B, NW, NS - 1>(s, w, xprep, y, scr, gridcap, pdl);
+  }
+}
+
+inline int qmv_cfg() {
+  static int c = getenv("SI_QMV_CFG") ? atoi(getenv("SI_QMV_CFG")) : 0;
+  return c;
+}
+
 template <int QT, int EPI, int B>
 int launch_warp(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y,
                 const ScratchCap& scr, int sms, bool pdl) {
+  {
+    int r = -1;
+    switch (qmv_cfg()) {
+      case 1: r = launch_fit<QT, EPI, B, 8, 6>(s, w, xprep, y, scr, sms, pdl); break;
+      case 2: r = launch_fit<QT, EPI, B, 8, 6>(s, w, xprep, y, scr, 2 * sms, pdl); break;
+      case 3: r = launch_fit<QT, EPI, B, 4, 8>(s, w, xprep, y, scr, 2 * sms, pdl); break;
+      case 4: r = launch_fit<QT, EPI, B, 4, 8>(s, w, xprep, y, scr, sms, pdl); break;
+      default: break;
+    }
+    if (r >= 0) return r;
+  }
   if constexpr (WarpCfg<QT, B, 16, 4>::SMEM <= WARP_SMEM_MAX)
     return launch_warp_cfg<QT, EPI, B, 16, 4>(s, w, xprep, y, scr, sms, pdl);
   else if constexpr (WarpCfg<QT, B, 16, 3>::SMEM <= WARP_SMEM_MAX)
@@ -705,11 +1086,48 @@ int launch_reg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
   return SI_OK;
 }
 
+// Batch-1 Q4_K launch; returns -1 when the shape does not suit k_qmv1 (odd
+// number of column units, too few unit pairs, or activations too large to
+// keep resident in shared memory).
+template <int EPI>
+int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y, const ScratchCap& scr, int sms,
+              bool pdl) {
+  constexpr int NW = 16, NS = 2;
+  const int64_t nunit = w->nblk;
+  const int64_t P = w->tiles * nunit / 2;
+  const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit);
+  if ((nunit & 1) || P < NW || smem > 227 * 1024) return -1;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  SI_CUDA(cudaGetDevice(&dev));
+  if (dev < 64 && !(attr_set & (1ull << dev))) {
+    SI_CUDA(cudaFuncSetAttribute(k_qmv1<EPI, NW, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_set |= 1ull << dev;
+  }
+  const int64_t grid = std::min<int64_t>(P / NW, sms);
+  const int64_t minr = P / (grid * NW), npt = nunit / 2;
+  const int maxc = (int)((npt - 1 + minr - 1) / minr + 1);
+  if ((size_t)w->tiles * maxc * 64 * 4 > scr.split_bytes || w->tiles > scr.count_n) return -1;
+  QmvScratch q = scr.scr;
+  q.maxc = maxc;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)grid), dim3(NW * 32), smem, pdl, attr);
+  SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv1<EPI, NW, NS>, (const uint8_t*)w->dev, (int)nunit, w->rows, (int)w->tiles,
+                             xprep, y, q));
+  return SI_OK;
+}
+
 template <int QT, int EPI>
 int dispatch_b(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y,
                const ScratchCap& scr, int sms, bool pdl) {
   const int64_t units = w->tiles * ((w->nblk + QtInfo<QT>::QPU - 1) / QtInfo<QT>::QPU);
   if (units < 16) B = B <= 4 ? -B : B;  // too small to stream: one CTA per tile
+  if constexpr (QT == SI_Q4_K) {
+    if (B == 1) {
+      const int r = launch_q1<EPI>(s, w, xprep, y, scr, sms, pdl);
+      if (r >= 0) return r;
+    }
+  }
   switch (B) {
     case 1: return launch_warp<QT, EPI, 1>(s, w, xprep, y, scr, sms, pdl);
     case 2: return launch_warp<QT, EPI, 2>(s, w, xprep, y, scr, sms, pdl);
@@ -744,6 +1162,8 @@ int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const 
   if (K <= 0 || (K & 31)) SI_FAIL(SI_ERR_INVALID, "prep: K=%d must be a positive multiple of 32", K);
   if (K > SI_MAX_K) SI_FAIL(SI_ERR_INVALID, "prep: K=%d above the supported maximum %d", K, SI_MAX_K);
   if (B < 1 || B > SI_MAX_BATCH) SI_FAIL(SI_ERR_INVALID, "prep: batch %d outside 1..%d", B, SI_MAX_BATCH);
+  if (mode == SI_PREP_ATTN_MERGE && (ldx < 1 || ldx > SI_ATTN_MAX_SPLITS || K % 128))
+    SI_FAIL(SI_ERR_INVALID, "prep: %d attention splits / K=%d", ldx, K);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(s, dim3(xprep_units(K), B), dim3(256), 0, pdl, attr);
   SI_CUDA(cudaLaunchKernelEx(&cfg, k_prep, x, ldx, x2, norm_w, eps, mode, K, B, xout, xprep));

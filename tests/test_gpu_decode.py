@@ -102,7 +102,8 @@ def test_decode_batch5_uses_two_mma_groups(ctx):
 
 
 def test_batch_rows_are_independent(ctx):
-    """Sequence b of a batch equals the same sequence decoded alone."""
+    """Sequence b of a batch equals the same sequence decoded alone (batch 1
+    runs its own matvec kernel, so the summation order differs slightly)."""
     cfg = small_cfg(4, max_batch=2)
     m = DecodeModel(ctx, cfg)
     m.synth(SEED)
@@ -110,7 +111,7 @@ def test_batch_rows_are_independent(ctx):
     _, lg2 = m.step([9, 9], 50, logits=True)
     m.kv_synth(50, SEED)
     _, lg1 = m.step([9], 50, logits=True)
-    assert rel_l2(lg2[0], lg1[0]) < 1e-6
+    assert rel_l2(lg2[0], lg1[0]) < 1e-5
     m.free()
 
 
