@@ -253,6 +253,7 @@ def run_ours(args, world, rank, local):
         tok = int(m.step([tok], pos)[0])
         pos += 1
     e2e_ms = (time.perf_counter() - w0) * 1e3 / args.steps
+    kernels_per_step = m.step_kernels(1)
     kern_ms, kern_bytes = matvec_roofline(ctx, torch, dev)
     t = torch.tensor([ms, e2e_ms, kern_ms], device=dev)
     if world > 1:
@@ -283,7 +284,7 @@ def run_ours(args, world, rank, local):
                                 "frac": round(tb / (ms * 1e-3) / 1e9 / peak, 4)},
             "e2e": {"value": round(world * 1e3 / e2e_ms, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4},
-            "gpu_launches": (9 * cfg.n_layers + 5) * args.steps,
+            "gpu_launches": kernels_per_step * args.steps,
             "clocks": clk,
             "tokens_head": [int(v) for v in gen[:8, 0]],
         }

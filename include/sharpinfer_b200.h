@@ -255,6 +255,11 @@ SI_EXPORT int si_decode_step(si_model* m, const int* tokens_host, int batch, int
 SI_EXPORT int si_decode_generate(si_model* m, const int* tokens_host, int batch, int pos0,
                                  int nsteps, int* out_tokens_host);
 
+/* Kernel launches of one captured decode step at this batch size (captures
+ * the step if needed): the device work behind one Transformer.Forward call
+ * (Transformer.cs:67-162).  For measurement. */
+SI_EXPORT int si_decode_step_kernels(si_model* m, int batch, int* kernels);
+
 /* Attention of one layer alone (RoPE, KV append at pos, attention) for
  * qkv_dev [batch][(n_heads + 2 n_kv_heads) * head_dim] -> out_dev
  * [batch][n_heads * head_dim] (test hook for the attention kernel). */

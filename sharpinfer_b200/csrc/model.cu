@@ -224,6 +224,7 @@ struct si_model {
   int* hist = nullptr;            // device token history of si_decode_generate
   int64_t hist_cap = 0;           // ints
   std::map<int, cudaGraphExec_t> graphs;
+  std::map<int, int> graph_kernels;  // kernel launches per captured step
   std::vector<void*> allocs;
 };
 
@@ -400,6 +401,17 @@ int get_graph(si_model* m, int B, cudaGraphExec_t* out) {
     return st;
   }
   if (e != cudaSuccess) SI_FAIL(SI_ERR_CUDA, "decode-step capture failed: %s", cudaGetErrorString(e));
+  size_t nn = 0;
+  int kernels = 0;
+  if (cudaGraphGetNodes(g, nullptr, &nn) == cudaSuccess && nn) {
+    std::vector<cudaGraphNode_t> nodes(nn);
+    if (cudaGraphGetNodes(g, nodes.data(), &nn) == cudaSuccess)
+      for (auto nd : nodes) {
+        cudaGraphNodeType ty;
+        if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) kernels++;
+      }
+  }
+  m->graph_kernels[B] = kernels;
   cudaGraphExec_t ge = nullptr;
   e = cudaGraphInstantiate(&ge, g, 0);
   cudaGraphDestroy(g);
@@ -757,6 +769,17 @@ SI_EXPORT int si_decode_generate(si_model* m, const int* tokens, int batch, int 
   SI_CUDA(cudaMemcpyAsync(out_tokens, m->hist, (size_t)need * 4, cudaMemcpyDeviceToHost, s));
   SI_CUDA(cudaStreamSynchronize(s));
   return check_device_errors(m->c);
+}
+
+SI_EXPORT int si_decode_step_kernels(si_model* m, int batch, int* kernels) {
+  clear_error();
+  if (!m || !kernels) SI_FAIL(SI_ERR_INVALID, "si_decode_step_kernels: NULL argument");
+  if (batch < 1 || batch > m->cfg.max_batch) SI_FAIL(SI_ERR_INVALID, "si_decode_step_kernels: batch %d", batch);
+  SI_TRY(bind_device(m->c));
+  cudaGraphExec_t ge;
+  SI_TRY(get_graph(m, batch, &ge));
+  *kernels = m->graph_kernels[batch];
+  return SI_OK;
 }
 
 SI_EXPORT int si_model_attention(si_model* m, int layer, const float* qkv, float* out, int batch, int pos) {

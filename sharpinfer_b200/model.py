@@ -106,6 +106,12 @@ class DecodeModel:
         N.call("si_decode_generate", self.handle, N.ptr(tok), tok.size, pos0, nsteps, N.ptr(out))
         return out
 
+    def step_kernels(self, batch=1):
+        """Kernel launches in one captured decode step at this batch size."""
+        n = ctypes.c_int()
+        N.call("si_decode_step_kernels", self.handle, batch, ctypes.byref(n))
+        return n.value
+
     def attention(self, layer, qkv, pos, out=None):
         """Attention of one layer for qkv [batch][(nh + 2 nkv) * hd] (CUDA f32 tensor)."""
         import torch
