@@ -266,6 +266,46 @@ SI_EXPORT int si_decode_step_kernels(si_model* m, int batch, int* kernels);
 SI_EXPORT int si_model_attention(si_model* m, int layer, const float* qkv_dev, float* out_dev,
                                  int batch, int pos);
 
+/* --------------------------------------------- f32 interface of CudaBackend
+ * The functions SharpInfer's managed backend binds from `sharpinfer_cuda`
+ * (src/SharpInfer.Gpu/CudaBackend.cs:141-163), with the same signatures and
+ * conventions: void returns (failures go to si_last_error() only), host
+ * pointers valid for the call (device pointers also accepted), synchronous.
+ * Operators follow TensorOps.cs. */
+
+/* CudaBackend.cs:143 -- a handle (si_ctx*) or NULL when no B200 is usable. */
+SI_EXPORT void* cuda_init(int device_id);
+/* CudaBackend.cs:144 */
+SI_EXPORT void cuda_cleanup(void* handle);
+/* CudaBackend.cs:145 -- NUL-terminated device name into buffer[buf_len]. */
+SI_EXPORT void cuda_device_name(void* handle, char* buffer, int buf_len);
+/* HardwareBackends.cs:440 (CudaProbe.cuda_is_available): 1 if a CUDA device exists. */
+SI_EXPORT int cuda_is_available(void);
+/* HardwareBackends.cs:441 binds a zero-argument `cuda_device_name`, which
+ * cannot share its name with the three-argument export above; this is that
+ * probe under its own name (device 0; a per-thread buffer). */
+SI_EXPORT const char* cuda_device_name_str(void);
+/* CudaBackend.cs:147-148 -- result[r] = Dot(mat[r, :], vec) (TensorOps.cs:63-72). */
+SI_EXPORT void cuda_mat_vec_mul(void* handle, const float* mat, const float* vec, float* result, int rows,
+                                int cols);
+/* CudaBackend.cs:150-151 -- C[M][N] = A[M][K] B[K][N] (TensorOps.cs:79-112). */
+SI_EXPORT void cuda_mat_mul(void* handle, const float* a, const float* b, float* c, int M, int K, int N);
+/* CudaBackend.cs:153-154 -- softmax in place (TensorOps.cs:115-132). */
+SI_EXPORT void cuda_softmax(void* handle, float* x, int len);
+/* CudaBackend.cs:156-157 -- output = RmsNorm(x) * weight (TensorOps.cs:135-145). */
+SI_EXPORT void cuda_rms_norm(void* handle, float* output, const float* x, const float* weight, int size,
+                             float eps);
+/* CudaBackend.cs:159-160 -- x = SiLU(x) (TensorOps.cs:191-195). */
+SI_EXPORT void cuda_silu(void* handle, float* x, int len);
+/* CudaBackend.cs:162-163 -- a += b (TensorOps.cs:149-165). */
+SI_EXPORT void cuda_add_inplace(void* handle, float* a, const float* b, int len);
+/* Layers/FlashAttention.cs:380-384 (NativeFlashAttn, Cdecl): f32 Q, O [batch][heads][seq][head_dim],
+ * K, V [batch][heads][kv][head_dim]; causal masking lets query i see keys
+ * j <= i + (kv - seq); head_dim <= 256.  Semantics of FlashAttention.Forward
+ * (FlashAttention.cs:59-167). */
+SI_EXPORT void flash_attention_forward(void* Q, void* K, void* V, void* O, int batch, int heads, int seq, int kv,
+                                       int head_dim, float scale, int causal);
+
 #ifdef __cplusplus
 }
 #endif

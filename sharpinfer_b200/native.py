@@ -69,6 +69,18 @@ _SIGS = {
     "si_qmatvec_host": (_i32, [_c_p, _c_p, _c_p, _c_p, _i32]),
     "si_qmatvec_noalloc": (_i32, [_c_p, _c_p, _c_p, _i32, _c_p]),
     "si_decode_step_kernels": (_i32, [_c_p, _i32, ctypes.POINTER(_i32)]),
+    "cuda_init": (_c_p, [_i32]),
+    "cuda_cleanup": (None, [_c_p]),
+    "cuda_device_name": (None, [_c_p, _c_p, _i32]),
+    "cuda_is_available": (_i32, []),
+    "cuda_device_name_str": (ctypes.c_char_p, []),
+    "cuda_mat_vec_mul": (None, [_c_p, _c_p, _c_p, _c_p, _i32, _i32]),
+    "cuda_mat_mul": (None, [_c_p, _c_p, _c_p, _c_p, _i32, _i32, _i32]),
+    "cuda_softmax": (None, [_c_p, _c_p, _i32]),
+    "cuda_rms_norm": (None, [_c_p, _c_p, _c_p, _c_p, _i32, ctypes.c_float]),
+    "cuda_silu": (None, [_c_p, _c_p, _i32]),
+    "cuda_add_inplace": (None, [_c_p, _c_p, _c_p, _i32]),
+    "flash_attention_forward": (None, [_c_p, _c_p, _c_p, _c_p] + [_i32] * 5 + [ctypes.c_float, _i32]),
     "si_model_create": (_i32, [_c_p, ctypes.POINTER(ModelConfig), ctypes.POINTER(_c_p)]),
     "si_model_free": (_i32, [_c_p]),
     "si_model_set_tensor": (_i32, [_c_p, _i32, _i32, _c_p]),
