@@ -155,6 +155,14 @@ SI_EXPORT int si_act_prepare(si_ctx* ctx, const float* x_dev, int64_t cols, int 
 SI_EXPORT int si_qmatvec_prepared(si_ctx* ctx, const si_weight* w, float* y_dev, int batch,
                                   int accumulate);
 
+/* Prefill GEMM: y[m][r] = sum_c W[r][c] * x[m][c] for m < M (any M >= 1),
+ * x [M][cols] bf16 and y [M][rows] f32, both device pointers -- the batched
+ * counterpart of IComputeBackend.MatMul (TensorOps.cs:244, :79-112) that
+ * replaces the per-token prefill loop (InferenceEngine.cs:82-85).  W is
+ * dequantised to f16 into context scratch, then multiplied on the tensor
+ * cores (tcgen05, f32 accumulation); cols must be a multiple of 64. */
+SI_EXPORT int si_qgemm(si_ctx* ctx, const si_weight* w, const uint16_t* x_bf16_dev, float* y_dev, int M);
+
 /* Same with host buffers (copied in, computed, copied out, synchronised),
  * the calling convention of cuda_mat_vec_mul (kernels.cu:67-87). */
 SI_EXPORT int si_qmatvec_host(si_ctx* ctx, const si_weight* w, const float* x_host,

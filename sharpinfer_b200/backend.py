@@ -162,6 +162,20 @@ class B200Context:
         self._leave(cur)
         return out
 
+    def qgemm(self, w, x, out=None):
+        """y = x W^T for bf16 x [M, cols] (CUDA tensor) on the tensor cores; y f32 [M, rows]."""
+        torch = _torch()
+        assert x.dtype == torch.bfloat16 and x.shape[-1] == w.cols
+        x2 = x.reshape(-1, w.cols).contiguous()
+        M = x2.shape[0]
+        cur = self._enter()
+        with torch.cuda.stream(self.torch_stream):
+            if out is None:
+                out = torch.empty((M, w.rows), dtype=torch.float32, device=x.device)
+            N.call("si_qgemm", self.handle, w.handle, N.ptr(x2), N.ptr(out), M)
+        self._leave(cur)
+        return out
+
     def qmatvec_host(self, w, x):
         """Same with host numpy arrays; synchronous (the cuda_mat_vec_mul convention)."""
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, w.cols)

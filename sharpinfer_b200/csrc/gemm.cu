@@ -1,0 +1,316 @@
+// Prefill GEMM on the 5th-generation tensor cores: Y[M][N] = X[M][K] W[N][K]^T
+// for a K-quant weight W and bf16 activations X -- the batched form of the
+// quantised MatVecMul that prefill needs (TensorOps.MatMul semantics,
+// src/SharpInfer.Core/Tensors/TensorOps.cs:79-112, over the weights
+// DequantizeTensor produces, Quantization.cs:415-469).
+//
+// Pipeline (one call):
+//  1. k_dequant_f16: the weight's blocks -> f16 [N][K] in a context scratch
+//     buffer (element = the reference's f32 value d*sc*q - dmin*m, rounded to
+//     f16 once).  Dequantising inside the GEMM mainloop would cost each weight
+//     ~1 CUDA-core instruction per 128-256 MACs, several times the issue
+//     budget the tensor cores leave free, so it is a bandwidth-bound pre-pass.
+//  2. k_bf16_to_f16: X -> f16 (exact for |x| < 65504; kind::f16 needs A and
+//     B of one type, and f16 keeps 3 more mantissa bits of W than bf16).
+//  3. k_gemm_tc: 128 x 256 output tile per CTA, K in steps of 64.  Warp 0
+//     issues TMA loads (128B-swizzled, 4-stage mbarrier ring), warp 1 issues
+//     tcgen05.mma (kind::f16, f32 accumulator in TMEM, 4 MMAs of K = 16 per
+//     stage) and tcgen05.commit to free stages, warps 2-5 read the
+//     accumulator back with tcgen05.ld and store Y.
+// Accuracy: the only rounding beyond f32 is W's f16 rounding (2^-12
+// relative), ~1e-4 relative L2 on Y.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "quantfmt.cuh"
+
+namespace si {
+namespace {
+
+constexpr int GM = 128, GN = 256, GK = 64, GST = 4;
+constexpr int A_BYTES = GM * GK * 2;  // 16 KB
+constexpr int B_BYTES = GN * GK * 2;  // 32 KB
+constexpr int GEMM_SMEM = GST * (A_BYTES + B_BYTES) + 1024 + 256;
+
+// f16 of one (row, block) in the reference's f32 arithmetic.
+__global__ void k_dequant_f16(int qt, const uint8_t* __restrict__ W, int64_t rows, int64_t nblk,
+                              __half* __restrict__ out) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= rows * nblk) return;
+  const int64_t r = idx / nblk, b = idx % nblk;
+  const int64_t T = r >> 4;
+  const int ri = (int)(r & 15);
+  const int be = qt == SI_Q8_0 ? 32 : 256;
+  __half* o = out + r * nblk * be + b * be;
+  if (qt == SI_Q4_K) {
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 2304);
+    const uint8_t* hdr = (const uint8_t*)(tbw + 4 * ri);
+    const float d = h2f(hdr[0] | (hdr[1] << 8)), dmin = h2f(hdr[2] | (hdr[3] << 8));
+    const uint8_t* q = hdr + 4;
+    for (int j = 0; j < 8; j++) {  // GetScaleMinK4 (Quantization.cs:302-314)
+      uint32_t sc, mn;
+      if (j < 4) {
+        sc = q[j] & 63;
+        mn = q[j + 4] & 63;
+      } else {
+        sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+      }
+      const float d1 = __fmul_rn(d, (float)sc), m1f = __fmul_rn(dmin, (float)mn);
+      for (int l0 = 0; l0 < 32; l0 += 8) {
+        __align__(16) __half v[8];
+#pragma unroll
+        for (int l = 0; l < 8; l++)
+          v[l] = __float2half_rn(__fsub_rn(__fmul_rn(d1, (float)dev_q4k_code(tbw, ri, 32 * j + l0 + l)), m1f));
+        *(uint4*)(o + 32 * j + l0) = *(const uint4*)v;
+      }
+    }
+  } else if (qt == SI_Q6_K) {
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 3360);
+    const int8_t* scales = (const int8_t*)(tbw + 768) + 16 * ri;
+    const uint32_t dw = tbw[832 + (ri & 7)];
+    const float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
+    for (int e0 = 0; e0 < 256; e0 += 8) {
+      __align__(16) __half v[8];
+#pragma unroll
+      for (int l = 0; l < 8; l++) {
+        const int e = e0 + l;
+        const float ds = __fmul_rn(d, (float)scales[e >> 4]);
+        v[l] = __float2half_rn(__fmul_rn(ds, (float)((int)dev_q6k_code(tbw, ri, e) - 32)));
+      }
+      *(uint4*)(o + e0) = *(const uint4*)v;
+    }
+  } else {
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 544);
+    const uint32_t dw = tbw[128 + (ri & 7)];
+    const float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
+    for (int e0 = 0; e0 < 32; e0 += 8) {
+      __align__(16) __half v[8];
+#pragma unroll
+      for (int l = 0; l < 8; l++) v[l] = __float2half_rn(__fmul_rn((float)dev_q80_code(tbw, ri, e0 + l), d));
+      *(uint4*)(o + e0) = *(const uint4*)v;
+    }
+  }
+}
+
+__global__ void k_bf16_to_f16(const uint16_t* __restrict__ x, __half* __restrict__ y, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_launch();
+  pdl_wait();
+  if (i < n) y[i] = __float2half_rn(__uint_as_float((uint32_t)x[i] << 16));
+}
+
+// ---- tcgen05 / TMA helpers ----
+// K-major operand, 128-byte swizzle: rows of 64 f16 (128 B), 8-row atoms of
+// 1024 B (SBO), LBO 16 B, descriptor version 1.
+__device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// kind::f16 instruction descriptor: D f32, A and B f16, both K-major, N = GN, M = GM.
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(GN >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int c0, int c1, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(tm), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
+                                                    const __grid_constant__ CUtensorMap tmB, float* __restrict__ Y,
+                                                    int M, int N, int K, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sA = base, sB = base + GST * A_BYTES, bars = sB + GST * B_BYTES;
+  const uint32_t done = bars + 64, tslot = bars + 72;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * GM, n0 = blockIdx.x * GN, nk = K / GK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GST; s++) {
+      mbar_init(bars + 8 * s, 1);       // full: TMA bytes landed
+      mbar_init(bars + 32 + 8 * s, 1);  // empty: MMAs reading the stage are done
+    }
+    mbar_init(done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tslot), "r"(GN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = lds_u32(tslot);
+  pdl_launch();  // dependents may start their independent prologue now
+  pdl_wait();    // A and B are written by the preceding conversion kernels
+
+  bool ok = true;
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer
+      for (int kt = 0; kt < nk && ok; kt++) {
+        const int s = kt % GST;
+        if (kt >= GST && !mbar_wait_bounded(bars + 32 + 8 * s, (uint32_t)((kt / GST - 1) & 1))) ok = false;
+        mbar_arrive_expect_tx(bars + 8 * s, A_BYTES + B_BYTES);
+        tma_load_2d(sA + s * A_BYTES, &tmA, kt * GK, m0, bars + 8 * s);
+        tma_load_2d(sB + s * B_BYTES, &tmB, kt * GK, n0, bars + 8 * s);
+      }
+      if (!ok) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      for (int kt = 0; kt < nk; kt++) {
+        const int s = kt % GST;
+        if (!mbar_wait_bounded(bars + 8 * s, (uint32_t)((kt / GST) & 1))) ok = false;
+        tc_fence_after();
+        if (ok) {
+          const uint64_t da = sdesc_k128(sA + s * A_BYTES), db = sdesc_k128(sB + s * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < GK / 16; kk++)  // +32 B along K per MMA inside the swizzle atom
+            umma_f16(tmem, da + 2 * kk, db + 2 * kk, IDESC, (kt | kk) != 0);
+        }
+        umma_commit(bars + 32 + 8 * s);
+      }
+      umma_commit(done);
+      if (!ok) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
+    }
+  } else {  // epilogue: TMEM lanes 32 (warp % 4) .. +31 = tile rows
+    if (!mbar_wait_bounded(done, 0)) {
+      ok = false;
+      if (lane == 0) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
+    }
+    tc_fence_after();
+    const int q = warp & 3;
+    const int row = m0 + 32 * q + lane;
+    float* yr = Y + (int64_t)row * N;
+    for (int c0 = 0; c0 < GN; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
+      if (!ok || row >= M) continue;
+      const int col0 = n0 + c0;
+      if (col0 + 32 <= N && (N & 3) == 0) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+          *(float4*)(yr + col0 + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                  __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; j++)
+          if (col0 + j < N) yr[col0 + j] = __uint_as_float(r[j]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GN) : "memory");
+  }
+}
+
+// cuTensorMapEncodeTiled from the driver, resolved once.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, []() {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+  });
+  return fn;
+}
+
+// 2D f16 tensor [rows][cols] (row-major), box [box_rows][64], 128-byte swizzle.
+int make_tmap(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) SI_FAIL(SI_ERR_CUDA, "qgemm: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)GK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) SI_FAIL(SI_ERR_CUDA, "qgemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return SI_OK;
+}
+
+}  // namespace
+
+int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int M) {
+  const int64_t N = w->rows, K = w->cols;
+  if (K % GK) SI_FAIL(SI_ERR_UNSUPPORTED, "qgemm: cols %lld not a multiple of %d", (long long)K, GK);
+  SI_TRY(ensure(c->stage[0], (size_t)N * K * 2));
+  SI_TRY(ensure(c->stage[1], (size_t)M * K * 2));
+  __half* wf = (__half*)c->stage[0].ptr;
+  __half* xf = (__half*)c->stage[1].ptr;
+  const int64_t nb = N * w->nblk;
+  k_dequant_f16<<<(unsigned)((nb + 127) / 128), 128, 0, c->stream>>>(w->qtype, (const uint8_t*)w->dev, N, w->nblk,
+                                                                      wf);
+  SI_CUDA(cudaGetLastError());
+  const int64_t nx = (int64_t)M * K;
+  k_bf16_to_f16<<<(unsigned)((nx + 255) / 256), 256, 0, c->stream>>>(x, xf, nx);
+  SI_CUDA(cudaGetLastError());
+  CUtensorMap ta, tb;
+  SI_TRY(make_tmap(&ta, xf, M, K, GM));
+  SI_TRY(make_tmap(&tb, wf, N, K, GN));
+  static uint64_t attr_set = 0;
+  if (c->device < 64 && !(attr_set & (1ull << c->device))) {
+    SI_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM));
+    attr_set |= 1ull << c->device;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((N + GN - 1) / GN), (unsigned)((M + GM - 1) / GM));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = GEMM_SMEM;
+  cfg.stream = c->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc, ta, tb, y, M, (int)N, (int)K, c->dev_err));
+  return SI_OK;
+}
+
+}  // namespace si
+
+using namespace si;
+
+extern "C" SI_EXPORT int si_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x_bf16, float* y, int M) {
+  clear_error();
+  if (!c || !w || !x_bf16 || !y) SI_FAIL(SI_ERR_INVALID, "si_qgemm: NULL argument");
+  if (M < 1) SI_FAIL(SI_ERR_INVALID, "si_qgemm: M = %d", M);
+  if (w->device != c->device) SI_FAIL(SI_ERR_INVALID, "si_qgemm: weight on device %d, context on %d", w->device, c->device);
+  SI_TRY(bind_device(c));
+  return launch_qgemm(c, w, x_bf16, y, M);
+}

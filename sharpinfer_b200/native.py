@@ -68,6 +68,7 @@ _SIGS = {
     "si_qmatvec_prepared": (_i32, [_c_p, _c_p, _c_p, _i32, _i32]),
     "si_qmatvec_host": (_i32, [_c_p, _c_p, _c_p, _c_p, _i32]),
     "si_qmatvec_noalloc": (_i32, [_c_p, _c_p, _c_p, _i32, _c_p]),
+    "si_qgemm": (_i32, [_c_p, _c_p, _c_p, _c_p, _i32]),
     "si_decode_step_kernels": (_i32, [_c_p, _i32, ctypes.POINTER(_i32)]),
     "cuda_init": (_c_p, [_i32]),
     "cuda_cleanup": (None, [_c_p]),
