@@ -96,11 +96,79 @@ __global__ void k_dequant_f16(int qt, const uint8_t* __restrict__ W, int64_t row
   }
 }
 
+// Q4_K: one warp per 16-row tile-block, reading the fragment-ordered words
+// directly (lane (g, t), word i of chunk c = k-tile 4c + i, rows g and g+8).
+__global__ void __launch_bounds__(256) k_dequant_q4k_f16(const uint8_t* __restrict__ W, int64_t rows, int64_t nblk,
+                                                         int64_t ntb, __half* __restrict__ out) {
+  const int64_t tb = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (tb >= ntb) return;
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int64_t T = tb / nblk, b = tb % nblk;
+  const uint32_t* tbw = (const uint32_t*)(W + tb * 2304);
+  const int64_t K = nblk * 256;
+  float d1[2][8], m1[2][8];
+#pragma unroll
+  for (int h = 0; h < 2; h++) {  // rows g, g+8: GetScaleMinK4 (Quantization.cs:302-314)
+    const uint4 hd = *(const uint4*)(tbw + 4 * (g + 8 * h));
+    const float d = h2f(hd.x & 0xFFFF), dmin = h2f(hd.x >> 16);
+    const uint32_t qw[3] = {hd.y, hd.z, hd.w};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      auto qb = [&](int k) { return (qw[k >> 2] >> (8 * (k & 3))) & 0xFF; };
+      uint32_t sc, mn;
+      if (j < 4) {
+        sc = qb(j) & 63;
+        mn = qb(j + 4) & 63;
+      } else {
+        sc = (qb(j + 4) & 0xF) | ((qb(j - 4) >> 6) << 4);
+        mn = (qb(j + 4) >> 4) | ((qb(j) >> 6) << 4);
+      }
+      d1[h][j] = __fmul_rn(d, (float)sc);
+      m1[h][j] = __fmul_rn(dmin, (float)mn);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+    const uint4 q = *(const uint4*)(tbw + 64 + c * 128 + lane * 4);
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const uint32_t w = i == 0 ? q.x : i == 1 ? q.y : i == 2 ? q.z : q.w;
+      const int kt = 4 * c + i, s = kt >> 1;
+      const int64_t col = b * 256 + 16 * kt + 2 * t;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int64_t r = T * 16 + g + 8 * h;
+        if (r >= rows) continue;
+        const int sh = 4 * h;
+        auto v = [&](int bit) {
+          return __float2half_rn(__fsub_rn(__fmul_rn(d1[h][s], (float)((w >> (bit + sh)) & 0xF)), m1[h][s]));
+        };
+        __half* o = out + r * K + col;
+        *(__half2*)o = __halves2half2(v(0), v(16));
+        *(__half2*)(o + 8) = __halves2half2(v(8), v(24));
+      }
+    }
+  }
+}
+
 __global__ void k_bf16_to_f16(const uint16_t* __restrict__ x, __half* __restrict__ y, int64_t n) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
   pdl_launch();
   pdl_wait();
-  if (i < n) y[i] = __float2half_rn(__uint_as_float((uint32_t)x[i] << 16));
+  if (i + 8 <= n) {
+    const uint4 v = *(const uint4*)(x + i);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const __half lo = __float2half_rn(__uint_as_float(w[k] << 16));
+      const __half hi = __float2half_rn(__uint_as_float(w[k] & 0xFFFF0000u));
+      o[k] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+    }
+    *(uint4*)(y + i) = make_uint4(o[0], o[1], o[2], o[3]);
+  } else {
+    for (int64_t j = i; j < n; j++) y[j] = __float2half_rn(__uint_as_float((uint32_t)x[j] << 16));
+  }
 }
 
 // ---- tcgen05 / TMA helpers ----
@@ -273,12 +341,18 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
   SI_TRY(ensure(c->stage[1], (size_t)M * K * 2));
   __half* wf = (__half*)c->stage[0].ptr;
   __half* xf = (__half*)c->stage[1].ptr;
-  const int64_t nb = N * w->nblk;
-  k_dequant_f16<<<(unsigned)((nb + 127) / 128), 128, 0, c->stream>>>(w->qtype, (const uint8_t*)w->dev, N, w->nblk,
-                                                                      wf);
+  if (w->qtype == SI_Q4_K) {
+    const int64_t ntb = w->tiles * w->nblk;
+    k_dequant_q4k_f16<<<(unsigned)((ntb + 7) / 8), 256, 0, c->stream>>>((const uint8_t*)w->dev, N, w->nblk, ntb, wf);
+  } else {
+    const int64_t nb = N * w->nblk;
+    k_dequant_f16<<<(unsigned)((nb + 127) / 128), 128, 0, c->stream>>>(w->qtype, (const uint8_t*)w->dev, N, w->nblk,
+                                                                        wf);
+  }
   SI_CUDA(cudaGetLastError());
   const int64_t nx = (int64_t)M * K;
-  k_bf16_to_f16<<<(unsigned)((nx + 255) / 256), 256, 0, c->stream>>>(x, xf, nx);
+  if (((uintptr_t)x & 15) != 0) SI_FAIL(SI_ERR_INVALID, "si_qgemm: x must be 16-byte aligned");
+  k_bf16_to_f16<<<(unsigned)((nx / 8 + 256) / 256), 256, 0, c->stream>>>(x, xf, nx);
   SI_CUDA(cudaGetLastError());
   CUtensorMap ta, tb;
   SI_TRY(make_tmap(&ta, xf, M, K, GM));
