@@ -220,6 +220,30 @@ typedef enum {
 /* Allocate the model (weights, f16 KV cache, activations) on the context's
  * GPU.  Weights are undefined until set or synthesised. */
 SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model** out);
+
+/* ------------------------------------------------- tensor parallelism (TP)
+ * The tensor-parallel path of InferenceCluster (src/SharpInfer.Core/Engine/
+ * DistributedInference.cs:143-160) with the partial-sum exchange of its
+ * AllReduce (:623-705) done on the GPUs, one rank per GPU: rank
+ * `rank` of `tp` (1, 2, 4, 8) holds q/k/v heads, gate/up rows and lm_head
+ * vocabulary rows 1/tp each (column-parallel), Wo / Wdown columns 1/tp each
+ * (row-parallel), and its kv heads of the cache; the embedding and norms are
+ * replicated.  After Wo and Wdown the ranks exchange partial sums directly in
+ * each other's memory (NVLink peer stores, no collective library), and the
+ * greedy token is chosen across the vocabulary slices.  Every rank runs the
+ * same calls (set/synth, kv_synth, decode_step / decode_generate) in the same
+ * order.  Logits returned by si_decode_step are this rank's slice
+ * [batch][vocab / tp]. */
+SI_EXPORT int si_model_create_tp(si_ctx* ctx, const si_model_config* cfg, int tp, int rank, si_model** out);
+/* This rank's communication buffer as an IPC handle (len >= 64 bytes). */
+SI_EXPORT int si_model_tp_handle(si_model* m, void* handle_out, int len);
+/* Map every rank's buffer: handles of ranks 0 .. tp-1, 64 bytes each
+ * (the handles of si_model_tp_handle, gathered by the host). */
+SI_EXPORT int si_model_tp_connect(si_model* m, const void* handles, int len);
+/* The part of a whole tensor a rank holds: global rows grow0 .. grow0 + rows,
+ * and in each row quant blocks gb0 .. gb0 + nblk of gnblk.  No device work. */
+SI_EXPORT int si_tp_slice(const si_model_config* cfg, int tp, int rank, int tensor, int64_t* grow0, int64_t* rows,
+                          int64_t* gb0, int64_t* nblk, int64_t* gnblk);
 SI_EXPORT int si_model_free(si_model* m);
 
 /* Upload one weight tensor as raw GGUF blocks, row-major [rows][cols] of the
@@ -244,7 +268,8 @@ SI_EXPORT int si_model_kv_synth(si_model* m, int len, uint64_t seed);
 SI_EXPORT uint64_t si_model_kv_tag(int layer, int seq, int is_value);
 
 /* Write n cache positions from host f16 arrays in the reference layout
- * [n][kv head][dim] (KVCache.Store, KVCache.cs:46-57). */
+ * [n][kv head][dim] (KVCache.Store, KVCache.cs:46-57), all kv heads of the
+ * model (a tensor-parallel rank keeps its own). */
 SI_EXPORT int si_model_kv_write(si_model* m, int layer, int seq, int pos0, int n,
                                 const uint16_t* k_host, const uint16_t* v_host);
 

@@ -44,6 +44,39 @@ void clear_error();
 // ---------------------------------------------------------------------------
 
 namespace si {
+// Tensor parallelism over peer memory.  Every rank owns a communication
+// buffer mapped into every other rank (CUDA IPC):
+//   [0, 1024)     flags: u32 [2 kinds][8 source ranks] (Wo, Wdown partial
+//                 sums), then u32 [16 batch rows][8 ranks] (argmax)
+//   [1024, 2048)  argmax candidates: [16 batch rows][8 ranks] {f32, i32}
+//   [2048, ...)   partial sums: [2 kinds][tp source ranks][max_batch][hidden] f32
+// A producer stores its partial rows into the slot [kind][own rank] of every
+// rank, then raises flag [kind][own rank] of every rank to the step's value
+// (epoch * 2 * n_layers + 2 * layer + kind + 1, never 0); consumers wait for
+// all tp flags and add the slots in rank order, so every rank computes the
+// same sum.
+constexpr int SI_TP_MAX = 8;
+constexpr int SI_TP_FLAGS = 0, SI_TP_ARGMAX_FLAGS = 64, SI_TP_ARGMAX = 1024, SI_TP_SLOTS = 2048;
+struct TpArgs {
+  uint8_t* const* peers = nullptr;  // device array [tp] of comm buffer bases
+  const unsigned* epoch = nullptr;  // step counter (StepParams::epoch)
+  int* counter = nullptr;           // CTA arrival counter of the producing kernel
+  int tp = 1, rank = 0, kind = 0;
+  int flag_add = 0;                 // 2 * layer + kind + 1
+  int nlayers2 = 0;                 // 2 * n_layers
+  int64_t slot_off = 0;             // byte offset of [kind][rank] slots in a comm buffer
+  int ld = 0;                       // floats per batch row (hidden)
+};
+// Consumer side of the tensor-parallel sum (k_prep, SI_PREP_RMSNORM_TP).
+struct PrepTp {
+  const uint8_t* comm = nullptr;    // this rank's comm buffer
+  const unsigned* epoch = nullptr;  // step counter
+  int* err = nullptr;
+  int tp = 1, kind = 0, flag_add = 0, nlayers2 = 0;
+  int64_t slots_off = 0;            // byte offset of slots [kind][source 0]
+  int64_t src_stride = 0;           // bytes between source ranks' slots
+  int ld = 0;                       // floats per batch row
+};
 // Device scratch of the streaming matvec: partial sums of row tiles split
 // between warps ([tiles][slots][64] f32) and per-tile arrival counters
 // ([tiles] int, zero between launches).
@@ -54,6 +87,7 @@ struct QmvBuffers {
   int64_t count_n;
   int* err;
   int sms;
+  TpArgs tp;  // used by the SI_EPI_TP epilogue
 };
 // CTAs (of nw warps) of the streaming matvec for `units` 16x256 units.
 inline int64_t qmv_warp_grid(int64_t units, int nw, int sms) {
@@ -98,7 +132,7 @@ struct si_ctx {
   si_devbuf qmv_count;                // and their counters (zero between launches)
   si::QmvBuffers qmv() const {
     return si::QmvBuffers{(float*)qmv_split.ptr, qmv_split.bytes, (int*)qmv_count.ptr,
-                          (int64_t)(qmv_count.bytes / 4), dev_err, sm_count};
+                          (int64_t)(qmv_count.bytes / 4), dev_err, sm_count, si::TpArgs{}};
   }
   // Host-pointer entry points: device staging and pinned host staging.
   si_devbuf stage[4];
@@ -150,7 +184,10 @@ int launch_dequant(si_ctx* c, const si_weight* w, float* out);
 // Activation preparation modes and matvec epilogues.
 enum { SI_PREP_PLAIN = 0, SI_PREP_RMSNORM = 1, SI_PREP_SILU_MUL = 2, SI_PREP_ATTN_MERGE = 3 };
 constexpr int SI_ATTN_MAX_SPLITS = 511;
-enum { SI_EPI_STORE = 0, SI_EPI_ADD = 1 };
+enum { SI_EPI_STORE = 0, SI_EPI_ADD = 1, SI_EPI_TP = 2 };
+// mode 4: v = RmsNorm(x + sum of the tp partial-sum slots) * w; the summed
+// residual is also written to xout (the next residual buffer)
+enum { SI_PREP_RMSNORM_TP = 4 };
 constexpr int SI_MAX_K = 49152;  // activation length limit of the prep kernel (smem)
 constexpr int SI_MAX_BATCH = 16;
 
@@ -166,11 +203,14 @@ inline size_t xprep_bytes(int K, int B) {
 }
 
 int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const float* norm_w,
-                float eps, int mode, int K, int B, float* xout, uint8_t* xprep, bool pdl);
+                float eps, int mode, int K, int B, float* xout, uint8_t* xprep, bool pdl,
+                const PrepTp* tpp = nullptr);
 int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
                const QmvBuffers& qb, bool pdl);
 int launch_synth_blocks(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma,
                         int64_t blk0, int64_t nblocks, uint8_t* dst);
+int launch_synth_blocks_2d(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma, int64_t grow0,
+                           int64_t nrows, int64_t gnblk, int64_t gb0, int64_t nblk, uint8_t* dst);
 
 }  // namespace si
 
@@ -309,7 +349,46 @@ __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
 }
 
 // Device error bits written by kernels whose bounded waits give up.
-enum { SI_DEVERR_WAIT_TIMEOUT = 1 };
+enum { SI_DEVERR_WAIT_TIMEOUT = 1, SI_DEVERR_PEER_TIMEOUT = 2 };
+
+// ---- system-scope flags between GPUs (peer memory over NVLink) ----
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait until flag p reaches `want` (flags only grow); gives up after ~1 s.
+__device__ __forceinline__ bool flag_wait(const unsigned* p, unsigned want) {
+  if ((int)(ld_acquire_sys(p) - want) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 26); i++) {
+    if ((int)(ld_acquire_sys(p) - want) >= 0) return true;
+    if ((i & 63u) == 63u) {
+      if (globaltimer_ns() - t0 > 1000000000ull) return false;
+      __nanosleep(64);
+    }
+  }
+  return false;
+}
+// End of a kernel that stored tp partial sums into peer slots: the last CTA
+// to finish raises flag [kind][rank] in every rank's buffer.
+__device__ __forceinline__ void tp_signal(const TpArgs& a) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const int n = (int)(gridDim.x * gridDim.y * gridDim.z);
+    if (atomicAdd(a.counter, 1) == n - 1) {
+      *a.counter = 0;
+      __threadfence_system();
+      const unsigned v = *a.epoch * (unsigned)a.nlayers2 + (unsigned)a.flag_add;
+      for (int p = 0; p < a.tp; p++)
+        st_release_sys((unsigned*)(a.peers[p] + SI_TP_FLAGS) + a.kind * SI_TP_MAX + a.rank, v);
+    }
+  }
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -82,8 +82,20 @@ __global__ void k_embed(const StepParams* __restrict__ p, int qt, const uint8_t*
 // Greedy selection (SamplingPipeline.ArgMax, SamplingPipeline.cs:83-89):
 // first index of the maximum under strict '>'; NaNs never win, and a NaN at
 // index 0 makes the answer 0.
+// Tensor parallelism: each rank holds the vocabulary slice [rank * vocab, (rank +
+// 1) * vocab); its candidate (value, global index) goes to every rank, and
+// every rank takes the largest value, ties to the lowest index.  A NaN at
+// global index 0 still makes the answer 0 (it is sent as +inf at index 0).
+struct ArgmaxTp {
+  uint8_t* const* peers = nullptr;
+  const uint8_t* comm = nullptr;
+  const unsigned* epoch = nullptr;
+  int* err = nullptr;
+  int tp = 1, rank = 0;
+};
+
 __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logits, int64_t vocab,
-                                                 int* __restrict__ out) {
+                                                 int* __restrict__ out, ArgmaxTp tp) {
   __shared__ float sv[32];
   __shared__ int si[32];
   pdl_launch();  // dependents may start their independent prologue now
@@ -124,7 +136,39 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
         bi = oi;
       }
     }
-    if (l == 0) out[b] = (isnan(x[0]) || bi < 0) ? 0 : bi;
+    if (l == 0) {
+      if (tp.tp == 1) {
+        out[b] = (isnan(x[0]) || bi < 0) ? 0 : bi;
+      } else {
+        float cv = bi < 0 ? -INFINITY : bv;
+        int ci = bi < 0 ? 0 : bi + tp.rank * (int)vocab;
+        if (tp.rank == 0 && isnan(x[0])) {
+          cv = INFINITY;
+          ci = 0;
+        }
+        const unsigned want = *tp.epoch + 1u;
+        for (int p = 0; p < tp.tp; p++) {
+          float2* slot = (float2*)(tp.peers[p] + SI_TP_ARGMAX) + b * SI_TP_MAX + tp.rank;
+          *slot = make_float2(cv, __int_as_float(ci));
+        }
+        __threadfence_system();
+        for (int p = 0; p < tp.tp; p++)
+          st_release_sys((unsigned*)(tp.peers[p] + SI_TP_ARGMAX_FLAGS) + b * SI_TP_MAX + tp.rank, want);
+        float gv = -INFINITY;
+        int gi = -1;
+        for (int r = 0; r < tp.tp; r++) {
+          if (!flag_wait((const unsigned*)(tp.comm + SI_TP_ARGMAX_FLAGS) + b * SI_TP_MAX + r, want))
+            atomicOr(tp.err, SI_DEVERR_PEER_TIMEOUT);
+          const float2 c = ((const float2*)(tp.comm + SI_TP_ARGMAX))[b * SI_TP_MAX + r];
+          const int idx = __float_as_int(c.y);
+          if (gi < 0 || c.x > gv || (c.x == gv && idx < gi)) {
+            gv = c.x;
+            gi = idx;
+          }
+        }
+        out[b] = gi < 0 ? 0 : gi;
+      }
+    }
   }
 }
 
@@ -147,19 +191,23 @@ __global__ void k_advance(StepParams* __restrict__ p, const int* __restrict__ ar
   if (b == 0) {
     p->pos += 1;
     p->step += 1;
+    p->epoch += 1;
   }
 }
 
 // Seeded f16 N(0,1) for positions [0, len) of one (layer, seq) cache; the
 // generator index follows the reference layout [pos][kv head][dim].
-__global__ void k_kv_synth(__half* __restrict__ cache, uint64_t key, int len, int nkv, int max_seq) {
+// (With tensor parallelism this rank holds kv heads kvh0 .. kvh0 + nkv - 1 of nkv_g.)
+__global__ void k_kv_synth(__half* __restrict__ cache, uint64_t key, int len, int nkv, int max_seq, int nkv_g,
+                           int kvh0) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t n = (int64_t)len * nkv * 128;
   if (i >= n) return;
   const int d = (int)(i % 128), kvh = (int)((i / 128) % nkv);
   const int64_t pos = i / (128 * nkv);
+  const int64_t gi = (pos * nkv_g + kvh0 + kvh) * 128 + d;
   cache[((int64_t)kvh * max_seq + pos) * 128 + kv_swz(d, (int)pos)] =
-      __ushort_as_half(si_synth_f16(key, (uint64_t)i, 1.0f));
+      __ushort_as_half(si_synth_f16(key, (uint64_t)gi, 1.0f));
 }
 
 __global__ void k_f32_synth(float* __restrict__ out, uint64_t key, int64_t n, float mean, float sigma) {
@@ -169,12 +217,13 @@ __global__ void k_f32_synth(float* __restrict__ out, uint64_t key, int64_t n, fl
 
 // [n][nkv][128] (reference layout) -> [nkv][max_seq][128] at pos0.
 __global__ void k_kv_scatter(__half* __restrict__ cache, const uint16_t* __restrict__ src, int pos0,
-                             int n, int nkv, int max_seq) {
+                             int n, int nkv, int max_seq, int nkv_g, int kvh0) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)n * nkv * 128) return;
   const int d = (int)(i % 128), kvh = (int)((i / 128) % nkv);
   const int64_t t = i / (128 * nkv);
-  cache[((int64_t)kvh * max_seq + pos0 + t) * 128 + kv_swz(d, (int)(pos0 + t))] = __ushort_as_half(src[i]);
+  cache[((int64_t)kvh * max_seq + pos0 + t) * 128 + kv_swz(d, (int)(pos0 + t))] =
+      __ushort_as_half(src[(t * nkv_g + kvh0 + kvh) * 128 + d]);
 }
 
 cudaLaunchConfig_t cfg_of(cudaStream_t s, dim3 g, dim3 b, size_t smem, bool pdl, cudaLaunchAttribute* attr) {
@@ -204,7 +253,15 @@ using namespace si;
 
 struct si_model {
   si_ctx* c = nullptr;
-  si_model_config cfg{};
+  si_model_config cfg{};   // this rank's shapes (heads, kv heads, FFN rows, vocabulary slice)
+  si_model_config gcfg{};  // the whole model's shapes
+  int tp = 1, rank = 0;    // tensor parallelism
+  uint8_t* comm = nullptr;                 // this rank's communication buffer (tp > 1)
+  uint8_t* peer_base[SI_TP_MAX] = {};      // every rank's buffer mapped here
+  uint8_t** peers_dev = nullptr;           // the same table on the device
+  bool connected = false;
+  int* tp_counter = nullptr;               // arrival counters of the two producing kernels
+  unsigned epoch = 0;                      // steps taken (mirrors StepParams::epoch)
   int G = 0, qkv_rows = 0, Kmax = 0;
   int splits_max = 0, chunk_max = 0;
   std::vector<si_weight*> wqkv, wo, wgu, wdown;
@@ -214,7 +271,7 @@ struct si_model {
   __half* kcache = nullptr;
   __half* vcache = nullptr;
   float* rope = nullptr;
-  float *x = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr;
+  float *x = nullptr, *x2 = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr;
   int* argmax = nullptr;
   uint8_t* xprep = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
@@ -258,27 +315,80 @@ int make_weight(si_model* m, int qt, int64_t rows, int64_t cols, si_weight** out
   return SI_OK;
 }
 
-// (weight, first row) of a projection tensor inside its fused weight.
-int tensor_slot(si_model* m, int layer, int t, si_weight** w, int64_t* row0, int64_t* rows,
-                int64_t* cols) {
-  const si_model_config& c = m->cfg;
-  const int64_t hd = c.head_dim, qr = (int64_t)c.n_heads * hd, kr = (int64_t)c.n_kv_heads * hd;
-  if (layer < 0) {
-    if (t == SI_T_EMB) { *w = m->emb; *row0 = 0; *rows = c.vocab; *cols = c.hidden; return SI_OK; }
-    if (t == SI_T_LM_HEAD) { *w = m->lm_head; *row0 = 0; *rows = c.vocab; *cols = c.hidden; return SI_OK; }
-    SI_FAIL(SI_ERR_INVALID, "tensor %d is not a global quantised tensor", t);
-  }
-  if (layer >= c.n_layers) SI_FAIL(SI_ERR_INVALID, "layer %d out of range", layer);
+// Which part of a whole tensor rank `rank` of `tp` holds: global rows grow0 ..
+// grow0 + rows and, in each, quant blocks gb0 .. gb0 + nblk of gnblk.
+// Column-parallel tensors (q, k, v, gate, up, lm_head) take a slice of rows,
+// row-parallel ones (o, down) a slice of every row (Megatron layout); the
+// embedding is replicated.
+int tp_slice(const si_model_config& g, int tp, int rank, int t, int64_t* grow0, int64_t* rows, int64_t* gb0,
+             int64_t* nblk, int64_t* gnblk) {
+  const int64_t hd = g.head_dim;
+  auto be = [](int qt) -> int64_t { return qt == SI_Q8_0 ? 32 : 256; };
+  const int64_t bw = be(g.weight_qtype);
+  auto colpar = [&](int64_t grows, int64_t cols, int qt) {
+    *rows = grows / tp;
+    *grow0 = (int64_t)rank * *rows;
+    *gnblk = *nblk = cols / be(qt);
+    *gb0 = 0;
+  };
+  auto rowpar = [&](int64_t grows, int64_t gcols) {
+    *rows = grows;
+    *grow0 = 0;
+    *gnblk = gcols / bw;
+    *nblk = *gnblk / tp;
+    *gb0 = (int64_t)rank * *nblk;
+  };
   switch (t) {
-    case SI_T_Q: *w = m->wqkv[layer]; *row0 = 0; *rows = qr; *cols = c.hidden; return SI_OK;
-    case SI_T_K: *w = m->wqkv[layer]; *row0 = qr; *rows = kr; *cols = c.hidden; return SI_OK;
-    case SI_T_V: *w = m->wqkv[layer]; *row0 = qr + kr; *rows = kr; *cols = c.hidden; return SI_OK;
-    case SI_T_O: *w = m->wo[layer]; *row0 = 0; *rows = c.hidden; *cols = qr; return SI_OK;
-    case SI_T_GATE: *w = m->wgu[layer]; *row0 = 0; *rows = c.intermediate; *cols = c.hidden; return SI_OK;
-    case SI_T_UP: *w = m->wgu[layer]; *row0 = c.intermediate; *rows = c.intermediate; *cols = c.hidden; return SI_OK;
-    case SI_T_DOWN: *w = m->wdown[layer]; *row0 = 0; *rows = c.hidden; *cols = c.intermediate; return SI_OK;
-    default: SI_FAIL(SI_ERR_INVALID, "tensor %d is not a quantised layer tensor", t);
+    case SI_T_Q: colpar((int64_t)g.n_heads * hd, g.hidden, g.weight_qtype); return SI_OK;
+    case SI_T_K:
+    case SI_T_V: colpar((int64_t)g.n_kv_heads * hd, g.hidden, g.weight_qtype); return SI_OK;
+    case SI_T_GATE:
+    case SI_T_UP: colpar(g.intermediate, g.hidden, g.weight_qtype); return SI_OK;
+    case SI_T_O: rowpar(g.hidden, (int64_t)g.n_heads * hd); return SI_OK;
+    case SI_T_DOWN: rowpar(g.hidden, g.intermediate); return SI_OK;
+    case SI_T_LM_HEAD: colpar(g.vocab, g.hidden, g.lm_head_qtype); return SI_OK;
+    case SI_T_EMB:
+      *rows = g.vocab;
+      *grow0 = *gb0 = 0;
+      *gnblk = *nblk = g.hidden / be(g.emb_qtype);
+      return SI_OK;
+    default: SI_FAIL(SI_ERR_INVALID, "tensor %d is not a quantised tensor", t);
   }
+}
+
+// Where a tensor lives on this rank: the fused weight, the first local row
+// inside it, and the part of the whole tensor (tp_slice) it holds.
+struct Slot {
+  si_weight* w;
+  int64_t row0, rows;
+  int64_t grow0, gnblk, gb0;
+};
+
+int tensor_slot(si_model* m, int layer, int t, Slot* sl) {
+  const si_model_config& c = m->cfg;
+  if ((layer < 0) != (t == SI_T_EMB || t == SI_T_LM_HEAD))
+    SI_FAIL(SI_ERR_INVALID, "tensor %d with layer %d", t, layer);
+  if (layer >= c.n_layers) SI_FAIL(SI_ERR_INVALID, "layer %d out of range", layer);
+  int64_t grow0, rows, gb0, nblk, gnblk;
+  SI_TRY(tp_slice(m->gcfg, m->tp, m->rank, t, &grow0, &rows, &gb0, &nblk, &gnblk));
+  const int64_t qr = (int64_t)c.n_heads * c.head_dim, kr = (int64_t)c.n_kv_heads * c.head_dim;
+  si_weight* w = nullptr;
+  int64_t row0 = 0;
+  switch (t) {
+    case SI_T_Q: w = m->wqkv[layer]; break;
+    case SI_T_K: w = m->wqkv[layer]; row0 = qr; break;
+    case SI_T_V: w = m->wqkv[layer]; row0 = qr + kr; break;
+    case SI_T_O: w = m->wo[layer]; break;
+    case SI_T_GATE: w = m->wgu[layer]; break;
+    case SI_T_UP: w = m->wgu[layer]; row0 = c.intermediate; break;
+    case SI_T_DOWN: w = m->wdown[layer]; break;
+    case SI_T_EMB: w = m->emb; break;
+    case SI_T_LM_HEAD: w = m->lm_head; break;
+    default: SI_FAIL(SI_ERR_INVALID, "tensor %d is not a quantised tensor", t);
+  }
+  if (w->nblk != nblk) SI_FAIL(SI_ERR_INVALID, "tensor %d: shard shape mismatch", t);
+  *sl = Slot{w, row0, rows, grow0, gnblk, gb0};
+  return SI_OK;
 }
 
 float* norm_ptr(si_model* m, int layer, int t) {
@@ -345,37 +455,97 @@ int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int 
 }
 
 // The whole decode step on the context stream (eager or under capture).
+// Tensor-parallel arguments of the producer (kind 0: Wo, 1: Wdown of `layer`)
+// and of its consumer, the RmsNorm prep that adds the partial sums.
+QmvBuffers tp_producer(si_model* m, int layer, int kind) {
+  QmvBuffers qb = m->c->qmv();
+  const int64_t slot = (int64_t)m->cfg.max_batch * m->cfg.hidden * 4;
+  qb.tp = TpArgs{m->peers_dev, &m->dparams->epoch, m->tp_counter + kind, m->tp, m->rank, kind,
+                 2 * layer + kind + 1, 2 * m->cfg.n_layers,
+                 SI_TP_SLOTS + (int64_t)kind * m->tp * slot + (int64_t)m->rank * slot, m->cfg.hidden};
+  return qb;
+}
+PrepTp tp_consumer(si_model* m, int layer, int kind) {
+  const int64_t slot = (int64_t)m->cfg.max_batch * m->cfg.hidden * 4;
+  PrepTp p;
+  p.comm = m->comm;
+  p.epoch = &m->dparams->epoch;
+  p.err = m->c->dev_err;
+  p.tp = m->tp;
+  p.kind = kind;
+  p.flag_add = 2 * layer + kind + 1;
+  p.nlayers2 = 2 * m->cfg.n_layers;
+  p.slots_off = SI_TP_SLOTS + (int64_t)kind * m->tp * slot;
+  p.src_stride = slot;
+  p.ld = m->cfg.hidden;
+  return p;
+}
+
+// The whole decode step on the context stream (eager or under capture).  With
+// tensor parallelism the Wo / Wdown matvecs store partial sums into every
+// rank's slots and the following RmsNorm prep adds them to the residual,
+// which alternates between x (before attention) and x2 (before the FFN).
 int enqueue_step(si_model* m, int B) {
   const si_model_config& c = m->cfg;
   cudaStream_t s = m->c->stream;
   const int h = c.hidden, inter = c.intermediate;
+  const bool tp = m->tp > 1;
   const QmvBuffers qb = m->c->qmv();
   {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cfg_of(s, dim3((h + 255) / 256, B), dim3(256), 0, false, attr);
     SI_CUDA(cudaLaunchKernelEx(&cfg, k_embed, (const StepParams*)m->dparams, m->emb->qtype,
-                               (const uint8_t*)m->emb->dev, m->emb->nblk, (int64_t)c.vocab, h, m->x));
+                               (const uint8_t*)m->emb->dev, m->emb->nblk, (int64_t)m->emb->rows, h, m->x));
   }
   for (int l = 0; l < c.n_layers; l++) {
-    SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
-                       nullptr, m->xprep, true));
+    if (tp && l > 0) {
+      const PrepTp pt = tp_consumer(m, l - 1, 1);
+      SI_TRY(launch_prep(s, m->x2, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
+                         m->x, m->xprep, true, &pt));
+    } else {
+      SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
+                         nullptr, m->xprep, true));
+    }
     SI_TRY(launch_qmv(s, m->wqkv[l], m->xprep, B, m->qkv, SI_EPI_STORE, qb, true));
     SI_TRY(enqueue_attention(m, l, m->qkv, nullptr, B, true));
-    SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
-    SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
-                       nullptr, m->xprep, true));
+    if (tp) {
+      SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, nullptr, SI_EPI_TP, tp_producer(m, l, 0), true));
+      const PrepTp pt = tp_consumer(m, l, 0);
+      SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
+                         m->x2, m->xprep, true, &pt));
+    } else {
+      SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
+      SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
+                         nullptr, m->xprep, true));
+    }
     SI_TRY(launch_qmv(s, m->wgu[l], m->xprep, B, m->gu, SI_EPI_STORE, qb, true));
     SI_TRY(launch_prep(s, m->gu, 2 * inter, m->gu + inter, nullptr, 0.f, SI_PREP_SILU_MUL, inter, B, nullptr,
                        m->xprep, true));
-    SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
+    if (tp) SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, nullptr, SI_EPI_TP, tp_producer(m, l, 1), true));
+    else SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
   }
-  SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, -1, SI_T_FINAL_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
-                     nullptr, m->xprep, true));
+  if (tp) {
+    const PrepTp pt = tp_consumer(m, c.n_layers - 1, 1);
+    SI_TRY(launch_prep(s, m->x2, h, nullptr, norm_ptr(m, -1, SI_T_FINAL_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
+                       m->x, m->xprep, true, &pt));
+  } else {
+    SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, -1, SI_T_FINAL_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
+                       nullptr, m->xprep, true));
+  }
   SI_TRY(launch_qmv(s, m->lm_head, m->xprep, B, m->logits, SI_EPI_STORE, qb, true));
   {
+    ArgmaxTp at;
+    if (tp) {
+      at.peers = m->peers_dev;
+      at.comm = m->comm;
+      at.epoch = &m->dparams->epoch;
+      at.err = m->c->dev_err;
+      at.tp = m->tp;
+      at.rank = m->rank;
+    }
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cfg_of(s, dim3(B), dim3(1024), 0, true, attr);
-    SI_CUDA(cudaLaunchKernelEx(&cfg, k_argmax, (const float*)m->logits, (int64_t)c.vocab, m->argmax));
+    SI_CUDA(cudaLaunchKernelEx(&cfg, k_argmax, (const float*)m->logits, (int64_t)c.vocab, m->argmax, at));
   }
   {
     cudaLaunchAttribute attr[1];
@@ -491,15 +661,30 @@ SI_EXPORT uint64_t si_model_kv_tag(int layer, int seq, int is_value) {
   return 0x4B560000ull + ((uint64_t)layer * 64 + (uint64_t)seq) * 2 + (uint64_t)(is_value != 0);
 }
 
-SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model** out) {
+SI_EXPORT int si_model_create_tp(si_ctx* ctx, const si_model_config* cfg, int tp, int rank, si_model** out) {
   clear_error();
   if (!ctx || !out) SI_FAIL(SI_ERR_INVALID, "si_model_create: NULL argument");
   *out = nullptr;
   SI_TRY(check_config(cfg));
+  if (tp != 1 && tp != 2 && tp != 4 && tp != 8) SI_FAIL(SI_ERR_UNSUPPORTED, "tensor parallel size %d (1, 2, 4 or 8)", tp);
+  if (rank < 0 || rank >= tp) SI_FAIL(SI_ERR_INVALID, "rank %d outside [0, %d)", rank, tp);
+  {
+    const int be = cfg->weight_qtype == SI_Q8_0 ? 32 : 256;
+    if (cfg->n_kv_heads % tp || cfg->vocab % tp || (cfg->intermediate / tp) % be || (cfg->intermediate / tp) % 16 ||
+        cfg->intermediate % tp || ((cfg->n_heads / tp) * cfg->head_dim) % be)
+      SI_FAIL(SI_ERR_INVALID, "model shapes do not split over %d ranks on quant-block boundaries", tp);
+  }
   SI_TRY(bind_device(ctx));
   si_model* m = new si_model();
   m->c = ctx;
+  m->gcfg = *cfg;
   m->cfg = *cfg;
+  m->tp = tp;
+  m->rank = rank;
+  m->cfg.n_heads /= tp;
+  m->cfg.n_kv_heads /= tp;
+  m->cfg.intermediate /= tp;
+  m->cfg.vocab /= tp;
   const si_model_config& c = m->cfg;
   m->G = c.n_heads / c.n_kv_heads;
   m->qkv_rows = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
@@ -521,7 +706,7 @@ SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model*
     if (st == SI_OK) st = make_weight(m, c.weight_qtype, 2 * (int64_t)c.intermediate, c.hidden, &m->wgu[l]);
     if (st == SI_OK) st = make_weight(m, c.weight_qtype, c.hidden, c.intermediate, &m->wdown[l]);
   }
-  if (st == SI_OK) st = make_weight(m, c.emb_qtype, c.vocab, c.hidden, &m->emb);
+  if (st == SI_OK) st = make_weight(m, c.emb_qtype, m->gcfg.vocab, c.hidden, &m->emb);
   if (st == SI_OK) st = make_weight(m, c.lm_head_qtype, c.vocab, c.hidden, &m->lm_head);
   if (st != SI_OK) return fail(st);
   const int64_t h = c.hidden;
@@ -539,6 +724,12 @@ SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model*
   ALLOC(vcache, kv_elems * 2);
   ALLOC(rope, (size_t)c.max_seq * c.head_dim * 4);
   ALLOC(x, (size_t)B * h * 4);
+  ALLOC(x2, (size_t)B * h * 4);
+  if (tp > 1) {
+    ALLOC(comm, SI_TP_SLOTS + (size_t)2 * tp * B * h * 4);
+    ALLOC(tp_counter, 2 * sizeof(int));
+    ALLOC(peers_dev, SI_TP_MAX * sizeof(uint8_t*));
+  }
   ALLOC(qkv, (size_t)B * m->qkv_rows * 4);
   ALLOC(gu, (size_t)B * 2 * c.intermediate * 4);
   ALLOC(logits, (size_t)B * c.vocab * 4);
@@ -549,6 +740,8 @@ SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model*
   ALLOC(dparams, sizeof(StepParams));
 #undef ALLOC
   cudaError_t e = cudaMemset(m->kcache, 0, kv_elems * 2);
+  if (e == cudaSuccess && m->comm) e = cudaMemset(m->comm, 0, SI_TP_SLOTS + (size_t)2 * tp * B * h * 4);
+  if (e == cudaSuccess && m->tp_counter) e = cudaMemset(m->tp_counter, 0, 2 * sizeof(int));
   if (e == cudaSuccess) e = cudaMemset(m->vcache, 0, kv_elems * 2);
   if (e == cudaSuccess) e = cudaMallocHost(&m->hparams, sizeof(StepParams));
   if (e == cudaSuccess) e = cudaMallocHost(&m->hargmax, sizeof(int) * SI_MAX_BATCH);
@@ -569,12 +762,67 @@ SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model*
   return SI_OK;
 }
 
+SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model** out) {
+  return si_model_create_tp(ctx, cfg, 1, 0, out);
+}
+
+SI_EXPORT int si_tp_slice(const si_model_config* cfg, int tp, int rank, int tensor, int64_t* grow0, int64_t* rows,
+                          int64_t* gb0, int64_t* nblk, int64_t* gnblk) {
+  clear_error();
+  if (!cfg || !grow0 || !rows || !gb0 || !nblk || !gnblk) SI_FAIL(SI_ERR_INVALID, "si_tp_slice: NULL argument");
+  if (tp < 1 || rank < 0 || rank >= tp) SI_FAIL(SI_ERR_INVALID, "si_tp_slice: rank %d of %d", rank, tp);
+  return tp_slice(*cfg, tp, rank, tensor, grow0, rows, gb0, nblk, gnblk);
+}
+
+SI_EXPORT int si_model_tp_handle(si_model* m, void* handle_out, int len) {
+  clear_error();
+  if (!m || !handle_out || len < (int)sizeof(cudaIpcMemHandle_t))
+    SI_FAIL(SI_ERR_INVALID, "si_model_tp_handle: need %d bytes", (int)sizeof(cudaIpcMemHandle_t));
+  if (m->tp == 1) SI_FAIL(SI_ERR_INVALID, "si_model_tp_handle: model is not tensor parallel");
+  SI_TRY(bind_device(m->c));
+  cudaIpcMemHandle_t h;
+  SI_CUDA(cudaIpcGetMemHandle(&h, m->comm));
+  memcpy(handle_out, &h, sizeof(h));
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_tp_connect(si_model* m, const void* handles, int len) {
+  clear_error();
+  if (!m || !handles) SI_FAIL(SI_ERR_INVALID, "si_model_tp_connect: NULL argument");
+  const int hs = (int)sizeof(cudaIpcMemHandle_t);
+  if (m->tp == 1 || len != m->tp * hs) SI_FAIL(SI_ERR_INVALID, "si_model_tp_connect: need %d handles", m->tp);
+  if (m->connected) SI_FAIL(SI_ERR_INVALID, "si_model_tp_connect: already connected");
+  SI_TRY(bind_device(m->c));
+  for (int r = 0; r < m->tp; r++) {
+    if (r == m->rank) {
+      m->peer_base[r] = m->comm;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, (const uint8_t*)handles + r * hs, hs);
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; q++)
+        if (q != m->rank && m->peer_base[q]) cudaIpcCloseMemHandle(m->peer_base[q]);
+      SI_FAIL(SI_ERR_CUDA, "opening rank %d's buffer failed: %s", r, cudaGetErrorString(e));
+    }
+    m->peer_base[r] = (uint8_t*)p;
+  }
+  SI_CUDA(cudaMemcpy(m->peers_dev, m->peer_base, SI_TP_MAX * sizeof(uint8_t*), cudaMemcpyHostToDevice));
+  m->connected = true;
+  return SI_OK;
+}
+
 SI_EXPORT int si_model_free(si_model* m) {
   clear_error();
   if (!m) return SI_OK;
   cudaSetDevice(m->c->device);
   cudaStreamSynchronize(m->c->stream);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+  if (m->connected)
+    for (int r = 0; r < m->tp; r++)
+      if (r != m->rank && m->peer_base[r]) cudaIpcCloseMemHandle(m->peer_base[r]);
   for (auto* v : {&m->wqkv, &m->wo, &m->wgu, &m->wdown})
     for (si_weight* w : *v) si_weight_free(w);
   si_weight_free(m->emb);
@@ -598,17 +846,28 @@ SI_EXPORT int si_model_set_tensor(si_model* m, int layer, int t, const void* hos
     SI_CUDA(cudaMemcpy(norm_ptr(m, layer, t), host, (size_t)m->cfg.hidden * 4, cudaMemcpyHostToDevice));
     return SI_OK;
   }
-  si_weight* w;
-  int64_t row0, rows, cols;
-  SI_TRY(tensor_slot(m, layer, t, &w, &row0, &rows, &cols));
-  const int64_t rb = w->nblk * gguf_block_bytes(w->qtype);
+  Slot sl;
+  SI_TRY(tensor_slot(m, layer, t, &sl));
+  si_weight* w = sl.w;
+  const int64_t bb = gguf_block_bytes(w->qtype);
+  const int64_t rb = w->nblk * bb;                                // local bytes per row
+  const uint8_t* src = (const uint8_t*)host + sl.grow0 * sl.gnblk * bb;
   const int64_t cr = std::max<int64_t>(16, ((64ll << 20) / rb) / 16 * 16);
+  const int64_t rows = sl.rows;
   SI_TRY(ensure(c->stage[0], (size_t)(std::min(cr, rows) * rb)));
+  std::vector<uint8_t> gather;
   for (int64_t r = 0; r < rows; r += cr) {
     const int64_t nr = std::min(cr, rows - r);
-    SI_CUDA(cudaMemcpyAsync(c->stage[0].ptr, (const uint8_t*)host + r * rb, (size_t)(nr * rb),
-                            cudaMemcpyHostToDevice, c->stream));
-    SI_TRY(launch_repack(c, w->qtype, (const uint8_t*)c->stage[0].ptr, row0 + rows, w->cols, row0 + r, nr, w->dev));
+    const uint8_t* chunk = src + r * sl.gnblk * bb;
+    if (sl.gnblk != w->nblk) {  // a slice of every row: gather it on the host
+      gather.resize((size_t)(nr * rb));
+      for (int64_t i = 0; i < nr; i++)
+        memcpy(gather.data() + i * rb, chunk + (i * sl.gnblk + sl.gb0) * bb, (size_t)rb);
+      chunk = gather.data();
+    }
+    SI_CUDA(cudaMemcpyAsync(c->stage[0].ptr, chunk, (size_t)(nr * rb), cudaMemcpyHostToDevice, c->stream));
+    SI_TRY(launch_repack(c, w->qtype, (const uint8_t*)c->stage[0].ptr, sl.row0 + rows, w->cols, sl.row0 + r, nr,
+                         w->dev));
     SI_CUDA(cudaStreamSynchronize(c->stream));
   }
   return SI_OK;
@@ -638,16 +897,19 @@ SI_EXPORT int si_model_synth(si_model* m, uint64_t seed) {
       SI_CUDA(cudaGetLastError());
       continue;
     }
-    si_weight* w;
-    int64_t row0, r2, c2;
-    SI_TRY(tensor_slot(m, layer, t, &w, &row0, &r2, &c2));
+    Slot sl;
+    SI_TRY(tensor_slot(m, layer, t, &sl));
+    si_weight* w = sl.w;
+    const int64_t rl = sl.rows;
     const int64_t rb = w->nblk * gguf_block_bytes(qt);
     const int64_t cr = std::max<int64_t>(16, ((64ll << 20) / rb) / 16 * 16);
-    SI_TRY(ensure(c->stage[0], (size_t)(std::min(cr, rows) * rb)));
-    for (int64_t r = 0; r < rows; r += cr) {
-      const int64_t nr = std::min(cr, rows - r);
-      SI_TRY(launch_synth_blocks(c, qt, seed, tag, rc, sg, r * w->nblk, nr * w->nblk, (uint8_t*)c->stage[0].ptr));
-      SI_TRY(launch_repack(c, qt, (const uint8_t*)c->stage[0].ptr, row0 + rows, w->cols, row0 + r, nr, w->dev));
+    SI_TRY(ensure(c->stage[0], (size_t)(std::min(cr, rl) * rb)));
+    for (int64_t r = 0; r < rl; r += cr) {
+      const int64_t nr = std::min(cr, rl - r);
+      // global blocks (grow0 + r + i) * gnblk + gb0 + j, j < nblk, in local row-major order
+      SI_TRY(launch_synth_blocks_2d(c, qt, seed, tag, rc, sg, sl.grow0 + r, nr, sl.gnblk, sl.gb0, w->nblk,
+                                    (uint8_t*)c->stage[0].ptr));
+      SI_TRY(launch_repack(c, qt, (const uint8_t*)c->stage[0].ptr, sl.row0 + rl, w->cols, sl.row0 + r, nr, w->dev));
       SI_CUDA(cudaStreamSynchronize(c->stream));
     }
   }
@@ -670,7 +932,8 @@ SI_EXPORT int si_model_kv_synth(si_model* m, int len, uint64_t seed) {
       for (int v = 0; v < 2; v++) {
         __half* base = (v ? m->vcache : m->kcache) + off;
         k_kv_synth<<<(unsigned)((n + 255) / 256), 256, 0, m->c->stream>>>(
-            base, si_key(seed, si_model_kv_tag(l, b, v)), len, c.n_kv_heads, c.max_seq);
+            base, si_key(seed, si_model_kv_tag(l, b, v)), len, c.n_kv_heads, c.max_seq, m->gcfg.n_kv_heads,
+            m->rank * c.n_kv_heads);
       }
     }
   SI_CUDA(cudaGetLastError());
@@ -688,7 +951,7 @@ SI_EXPORT int si_model_kv_write(si_model* m, int layer, int seq, int pos0, int n
     SI_FAIL(SI_ERR_INVALID, "si_model_kv_write: range outside the cache");
   si_ctx* ctx = m->c;
   SI_TRY(bind_device(ctx));
-  const size_t bytes = (size_t)n * c.n_kv_heads * c.head_dim * 2;
+  const size_t bytes = (size_t)n * m->gcfg.n_kv_heads * c.head_dim * 2;  // all kv heads, [n][heads][dim]
   if (!bytes) return SI_OK;
   SI_TRY(ensure(ctx->stage[3], bytes));
   const int64_t per = (int64_t)c.n_kv_heads * c.max_seq * c.head_dim;
@@ -697,7 +960,8 @@ SI_EXPORT int si_model_kv_write(si_model* m, int layer, int seq, int pos0, int n
   for (int which = 0; which < 2; which++) {
     SI_CUDA(cudaMemcpyAsync(ctx->stage[3].ptr, which ? v : k, bytes, cudaMemcpyHostToDevice, ctx->stream));
     k_kv_scatter<<<(unsigned)((cnt + 255) / 256), 256, 0, ctx->stream>>>(
-        (which ? m->vcache : m->kcache) + off, (const uint16_t*)ctx->stage[3].ptr, pos0, n, c.n_kv_heads, c.max_seq);
+        (which ? m->vcache : m->kcache) + off, (const uint16_t*)ctx->stage[3].ptr, pos0, n, c.n_kv_heads, c.max_seq,
+        m->gcfg.n_kv_heads, m->rank * c.n_kv_heads);
     SI_CUDA(cudaGetLastError());
     SI_CUDA(cudaStreamSynchronize(ctx->stream));
   }
@@ -713,10 +977,13 @@ SI_EXPORT int si_decode_step(si_model* m, const int* tokens, int batch, int pos,
   if (pos < 0 || pos >= c.max_seq)
     SI_FAIL(SI_ERR_INVALID, "position %d exceeds max sequence length %d", pos, c.max_seq);  // KVCache.cs:48-49
   for (int b = 0; b < batch; b++)
-    if (tokens[b] < 0 || tokens[b] >= c.vocab) SI_FAIL(SI_ERR_INVALID, "token id %d outside the vocabulary", tokens[b]);
+    if (tokens[b] < 0 || tokens[b] >= m->gcfg.vocab)
+      SI_FAIL(SI_ERR_INVALID, "token id %d outside the vocabulary", tokens[b]);
+  if (m->tp > 1 && !m->connected) SI_FAIL(SI_ERR_INVALID, "tensor-parallel model not connected to its peers");
   SI_TRY(bind_device(m->c));
   cudaGraphExec_t ge;
   SI_TRY(get_graph(m, batch, &ge));
+  m->hparams->epoch = m->epoch++;
   m->hparams->pos = pos;
   m->hparams->batch = batch;
   for (int b = 0; b < batch; b++) m->hparams->tokens[b] = tokens[b];
@@ -744,7 +1011,9 @@ SI_EXPORT int si_decode_generate(si_model* m, const int* tokens, int batch, int 
   if (nsteps < 0 || pos0 < 0 || (int64_t)pos0 + nsteps > c.max_seq)
     SI_FAIL(SI_ERR_INVALID, "positions %d..%d exceed max sequence length %d", pos0, pos0 + nsteps, c.max_seq);
   for (int b = 0; b < batch; b++)
-    if (tokens[b] < 0 || tokens[b] >= c.vocab) SI_FAIL(SI_ERR_INVALID, "token id %d outside the vocabulary", tokens[b]);
+    if (tokens[b] < 0 || tokens[b] >= m->gcfg.vocab)
+      SI_FAIL(SI_ERR_INVALID, "token id %d outside the vocabulary", tokens[b]);
+  if (m->tp > 1 && !m->connected) SI_FAIL(SI_ERR_INVALID, "tensor-parallel model not connected to its peers");
   if (nsteps == 0) return SI_OK;
   SI_TRY(bind_device(m->c));
   cudaGraphExec_t ge;
@@ -757,6 +1026,8 @@ SI_EXPORT int si_decode_generate(si_model* m, const int* tokens, int batch, int 
     SI_CUDA(cudaMalloc(&m->hist, (size_t)need * 4));
     m->hist_cap = need;
   }
+  m->hparams->epoch = m->epoch;
+  m->epoch += (unsigned)nsteps;
   m->hparams->pos = pos0;
   m->hparams->batch = batch;
   for (int b = 0; b < batch; b++) m->hparams->tokens[b] = tokens[b];

@@ -13,6 +13,7 @@ struct StepParams {
   int step;      // steps taken since the parameters were last written by the host
   int hist_cap;  // steps the history buffer holds
   int* hist;     // [hist_cap][batch] greedy tokens of consecutive steps
+  unsigned epoch;  // steps since the model was created (tensor-parallel flag values)
 };
 
 struct AttnArgs {

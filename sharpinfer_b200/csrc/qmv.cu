@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
                                               const float* __restrict__ x2,
                                               const float* __restrict__ nw, float eps, int mode,
                                               int K, int B, float* __restrict__ xout,
-                                              uint8_t* __restrict__ xprep) {
+                                              uint8_t* __restrict__ xprep, PrepTp tpp) {
   __shared__ float sv[256];
   __shared__ float red[8];
   __shared__ float mw[2][SI_ATTN_MAX_SPLITS + 1];  // mode 3: merge weights of the unit's two heads
@@ -131,6 +131,39 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
       if (xout) xout[(int64_t)b * K + k] = v;
     }
   }
+  if (mode == SI_PREP_RMSNORM_TP) {
+    // residual + the tp partial sums, added in rank order (identical on every rank)
+    if (tid == 0) {
+      const unsigned want = *tpp.epoch * (unsigned)tpp.nlayers2 + (unsigned)tpp.flag_add;
+      const unsigned* fl = (const unsigned*)(tpp.comm + SI_TP_FLAGS) + tpp.kind * SI_TP_MAX;
+      for (int r = 0; r < tpp.tp; r++)
+        if (!flag_wait(fl + r, want)) atomicOr(tpp.err, SI_DEVERR_PEER_TIMEOUT);
+    }
+    __syncthreads();
+    auto res = [&](int i) {
+      float a = xb[i];
+      for (int r = 0; r < tpp.tp; r++)
+        a = __fadd_rn(a, ((const float*)(tpp.comm + tpp.slots_off + r * tpp.src_stride))[(int64_t)b * tpp.ld + i]);
+      return a;
+    };
+    float ss = 0.f;
+    for (int i = tid; i < K; i += 256) {
+      const float a = res(i);
+      ss = __fadd_rn(ss, __fmul_rn(a, a));
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int i = 0; i < 8; i++) t += red[i];
+    scale = 1.0f / sqrtf(t / (float)K + eps);
+    if (k < K) {
+      const float a = res(k);
+      xout[(int64_t)b * K + k] = a;
+      v = __fmul_rn(__fmul_rn(a, scale), nw[k]);
+    }
+    __syncthreads();  // red is reused below
+  }
   if (mode == 1) {
     float ss = 0.f;
     for (int i = tid; i < K; i += 256) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
@@ -141,7 +174,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
     for (int i = 0; i < 8; i++) t += red[i];
     scale = 1.0f / sqrtf(t / (float)K + eps);
   }
-  if (k < K && mode != 3) {
+  if (k < K && mode != 3 && mode != SI_PREP_RMSNORM_TP) {
     if (mode == 1) {
       v = __fmul_rn(__fmul_rn(xb[k], scale), nw[k]);
     } else if (mode == 2) {
@@ -201,7 +234,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
 // ---------------------------------------------------------------------------
 template <int NMG, int EPI>
 __device__ __forceinline__ void qmv_epilogue(const float (&tg)[NMG], const float (&tg8)[NMG], int B,
-                                             int64_t rows, float* __restrict__ y, int tile) {
+                                             int64_t rows, float* __restrict__ y, int tile, const TpArgs& tpa) {
   __shared__ float red[QMV_WARPS][NMG][2][32];
   __syncthreads();  // the previous tile's reduction has been read
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -221,9 +254,13 @@ __device__ __forceinline__ void qmv_epilogue(const float (&tg)[NMG], const float
     const int bt = 4 * mg + tt;
     const int64_t row = (int64_t)tile * 16 + gg + 8 * half;
     if (bt < B && row < rows) {
-      float* dst = y + (int64_t)bt * rows + row;
-      if (EPI == SI_EPI_ADD) *dst += v;
-      else *dst = v;
+      if (EPI == SI_EPI_TP) {
+        for (int p = 0; p < tpa.tp; p++) ((float*)(tpa.peers[p] + tpa.slot_off))[(int64_t)bt * tpa.ld + row] = v;
+      } else {
+        float* dst = y + (int64_t)bt * rows + row;
+        if (EPI == SI_EPI_ADD) *dst += v;
+        else *dst = v;
+      }
     }
   }
 }
@@ -466,6 +503,7 @@ struct QmvScratch {
   int* count;    // [tiles] arrivals (zero between launches; reset by the last)
   int* err;      // device error word
   int maxc;      // contributor slots per tile
+  TpArgs tp;     // SI_EPI_TP: peer slots and flags
 };
 
 template <int QT, int B, int NW, int NS>
@@ -478,8 +516,19 @@ struct WarpCfg {
 
 template <int EPI, int B>
 __device__ __forceinline__ void store_tile(float* __restrict__ y, int64_t rows, int T, int lane,
-                                           float v0, float v8) {
+                                           float v0, float v8, const TpArgs& tpa) {
   const int g = lane >> 2, t = lane & 3;
+  if (EPI == SI_EPI_TP) {  // partial rows into slot [kind][rank] of every rank
+    if (t < B) {
+      const int64_t r0 = (int64_t)T * 16 + g, r1 = r0 + 8;
+      for (int p = 0; p < tpa.tp; p++) {
+        float* yb = (float*)(tpa.peers[p] + tpa.slot_off) + (int64_t)t * tpa.ld;
+        if (r0 < rows) yb[r0] = v0;
+        if (r1 < rows) yb[r1] = v8;
+      }
+    }
+    return;
+  }
   if (t < B) {
     const int64_t r0 = (int64_t)T * 16 + g, r1 = r0 + 8;
     float* yb = y + (int64_t)t * rows;
@@ -601,7 +650,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
         // ---- this warp's part of tile cT is done ----
         const int64_t t0 = tile_first, t1 = tile_first + nunit;  // tile's unit range
         if (t0 >= ub && t1 <= ue) {
-          store_tile<EPI, B>(y, rows, cT, lane, tg[0], tg8[0]);
+          store_tile<EPI, B>(y, rows, cT, lane, tg[0], tg8[0], scr.tp);
         } else if (cT == (int)c0T) {  // first tile of the range, shared with other warps
           p0a = tg[0];
           p0b = tg8[0];
@@ -651,7 +700,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
       b8 += part[((j - cw0) * 2 + slot) * 64 + 32 + lane];
     }
     if (wf >= cw0 && wl < cw0 + NW) {
-      store_tile<EPI, B>(y, rows, (int)T, lane, a, b8);
+      store_tile<EPI, B>(y, rows, (int)T, lane, a, b8, scr.tp);
       continue;
     }
     const int64_t cf = wf / NW, cl = wl / NW;
@@ -683,10 +732,11 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
             sb += vb[j];
           }
       }
-      store_tile<EPI, B>(y, rows, (int)T, lane, sa, sb);
+      store_tile<EPI, B>(y, rows, (int)T, lane, sa, sb, scr.tp);
       if (lane == 0) scr.count[T] = 0;
     }
   }
+  if (EPI == SI_EPI_TP) tp_signal(scr.tp);
 }
 
 // ---------------------------------------------------------------------------
@@ -852,7 +902,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
           p0b = b8;
           has0 = true;
         } else {
-          store_tile<EPI, 1>(y, rows, (int)cT, lane, a, b8);
+          store_tile<EPI, 1>(y, rows, (int)cT, lane, a, b8, scr.tp);
         }
         tg = tg8 = 0.f;
         cU = 0;
@@ -900,7 +950,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       b8 += part[((j - cw0) * 2 + slot) * 64 + 32 + lane];
     }
     if (wf >= cw0 && wl < cw0 + NW) {
-      store_tile<EPI, 1>(y, rows, (int)T, lane, a, b8);
+      store_tile<EPI, 1>(y, rows, (int)T, lane, a, b8, scr.tp);
       continue;
     }
     const int64_t cf = wf / NW, cl = wl / NW;
@@ -932,10 +982,11 @@ __global__ void __launch_bounds__(NW * 32, 1)
             sb += vb[j];
           }
       }
-      store_tile<EPI, 1>(y, rows, (int)T, lane, sa, sb);
+      store_tile<EPI, 1>(y, rows, (int)T, lane, sa, sb, scr.tp);
       if (lane == 0) scr.count[T] = 0;
     }
   }
+  if (EPI == SI_EPI_TP) tp_signal(scr.tp);
 }
 
 // ---------------------------------------------------------------------------
@@ -945,7 +996,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
 template <int QT, int NMG, int EPI>
 __global__ void __launch_bounds__(256) k_qmv_reg(const uint8_t* __restrict__ W, int nblk,
                                                  int64_t rows, const uint8_t* __restrict__ xprep,
-                                                 int B, float* __restrict__ y) {
+                                                 int B, float* __restrict__ y, TpArgs tpa) {
   constexpr int TBB = QtInfo<QT>::TBB, QPU = QtInfo<QT>::QPU;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, t = lane & 3;
   const int nunit = (nblk + QPU - 1) / QPU;
@@ -975,7 +1026,8 @@ __global__ void __launch_bounds__(256) k_qmv_reg(const uint8_t* __restrict__ W, 
     else if (QT == SI_Q6_K) unit_q6k<NMG>(ld, lane, tg, tg8);
     else unit_q80<NMG>(ld, lane, min(QPU, nblk - u * QPU), tg, tg8);
   }
-  qmv_epilogue<NMG, EPI>(tg, tg8, B, rows, y, (int)blockIdx.x);
+  qmv_epilogue<NMG, EPI>(tg, tg8, B, rows, y, (int)blockIdx.x, tpa);
+  if (EPI == SI_EPI_TP) tp_signal(tpa);
 }
 
 cudaLaunchConfig_t make_cfg(cudaStream_t s, dim3 grid, dim3 block, size_t smem, bool pdl,
@@ -1078,11 +1130,12 @@ int launch_warp(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float*
 }
 
 template <int QT, int NMG, int EPI>
-int launch_reg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, bool pdl) {
+int launch_reg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, const TpArgs& tpa,
+               bool pdl) {
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)w->tiles), dim3(256), 0, pdl, attr);
   SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv_reg<QT, NMG, EPI>, (const uint8_t*)w->dev, (int)w->nblk,
-                             w->rows, xprep, B, y));
+                             w->rows, xprep, B, y, tpa));
   return SI_OK;
 }
 
@@ -1135,11 +1188,11 @@ int dispatch_b(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
     case 4: return launch_warp<QT, EPI, 4>(s, w, xprep, y, scr, sms, pdl);
     default: break;
   }
-  if (B < 0) return launch_reg<QT, 1, EPI>(s, w, xprep, -B, y, pdl);
+  if (B < 0) return launch_reg<QT, 1, EPI>(s, w, xprep, -B, y, scr.scr.tp, pdl);
   switch ((B + 3) / 4) {
-    case 2: return launch_reg<QT, 2, EPI>(s, w, xprep, B, y, pdl);
-    case 3: return launch_reg<QT, 3, EPI>(s, w, xprep, B, y, pdl);
-    case 4: return launch_reg<QT, 4, EPI>(s, w, xprep, B, y, pdl);
+    case 2: return launch_reg<QT, 2, EPI>(s, w, xprep, B, y, scr.scr.tp, pdl);
+    case 3: return launch_reg<QT, 3, EPI>(s, w, xprep, B, y, scr.scr.tp, pdl);
+    case 4: return launch_reg<QT, 4, EPI>(s, w, xprep, B, y, scr.scr.tp, pdl);
     default: SI_FAIL(SI_ERR_INVALID, "qmatvec: batch %d outside 1..16", B);
   }
 }
@@ -1158,7 +1211,7 @@ int dispatch_qt(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B,
 }  // namespace
 
 int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const float* norm_w,
-                float eps, int mode, int K, int B, float* xout, uint8_t* xprep, bool pdl) {
+                float eps, int mode, int K, int B, float* xout, uint8_t* xprep, bool pdl, const PrepTp* tpp) {
   if (K <= 0 || (K & 31)) SI_FAIL(SI_ERR_INVALID, "prep: K=%d must be a positive multiple of 32", K);
   if (K > SI_MAX_K) SI_FAIL(SI_ERR_INVALID, "prep: K=%d above the supported maximum %d", K, SI_MAX_K);
   if (B < 1 || B > SI_MAX_BATCH) SI_FAIL(SI_ERR_INVALID, "prep: batch %d outside 1..%d", B, SI_MAX_BATCH);
@@ -1166,14 +1219,20 @@ int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const 
     SI_FAIL(SI_ERR_INVALID, "prep: %d attention splits / K=%d", ldx, K);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(s, dim3(xprep_units(K), B), dim3(256), 0, pdl, attr);
-  SI_CUDA(cudaLaunchKernelEx(&cfg, k_prep, x, ldx, x2, norm_w, eps, mode, K, B, xout, xprep));
+  if (mode == SI_PREP_RMSNORM_TP && (!tpp || !xout)) SI_FAIL(SI_ERR_INVALID, "prep: tensor-parallel mode without peers");
+  SI_CUDA(cudaLaunchKernelEx(&cfg, k_prep, x, ldx, x2, norm_w, eps, mode, K, B, xout, xprep,
+                             tpp ? *tpp : PrepTp{}));
   return SI_OK;
 }
 
 int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
                const QmvBuffers& qb, bool pdl) {
-  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0}, qb.split_bytes, qb.count_n};
+  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp}, qb.split_bytes, qb.count_n};
   if (epi == SI_EPI_ADD) return dispatch_qt<SI_EPI_ADD>(s, w, xprep, B, y, scr, qb.sms, pdl);
+  if (epi == SI_EPI_TP) {
+    if (qb.tp.tp < 1 || !qb.tp.peers || !qb.tp.counter) SI_FAIL(SI_ERR_INVALID, "qmatvec: tensor-parallel epilogue without peers");
+    return dispatch_qt<SI_EPI_TP>(s, w, xprep, B, y, scr, qb.sms, pdl);
+  }
   return dispatch_qt<SI_EPI_STORE>(s, w, xprep, B, y, scr, qb.sms, pdl);
 }
 

@@ -171,11 +171,15 @@ __global__ void k_dequant(int qt, const uint8_t* __restrict__ W, int64_t rows, i
   dequant_block(qt, W, nblk, r, b, out + r * nblk * be + b * be);
 }
 
+// Blocks blk0 + i (i < nblocks) of a tensor, or -- when nblk > 0 -- the
+// blocks of rows grow0 .. grow0 + nblocks / nblk, columns gb0 .. gb0 + nblk of
+// a tensor with gnblk blocks per row (a slice of every row), row-major.
 __global__ void k_synth_blocks(int qt, uint64_t key, int recipe, float sigma, int64_t blk0,
-                               int64_t nblocks, uint8_t* __restrict__ dst) {
+                               int64_t nblocks, uint8_t* __restrict__ dst, int64_t gnblk, int64_t gb0,
+                               int64_t nblk) {
   int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nblocks) return;
-  uint64_t gb = (uint64_t)(blk0 + i);
+  uint64_t gb = nblk > 0 ? (uint64_t)((blk0 + i / nblk) * gnblk + gb0 + i % nblk) : (uint64_t)(blk0 + i);
   uint8_t buf[210];
   int bb;
   if (qt == SI_Q4_K) {
@@ -224,7 +228,18 @@ int launch_synth_blocks(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int reci
   if (nblocks == 0) return SI_OK;
   int threads = 128;
   k_synth_blocks<<<(unsigned)((nblocks + threads - 1) / threads), threads, 0, c->stream>>>(
-      qt, si_key(seed, tag), recipe, sigma, blk0, nblocks, dst);
+      qt, si_key(seed, tag), recipe, sigma, blk0, nblocks, dst, 0, 0, 0);
+  SI_CUDA(cudaGetLastError());
+  return SI_OK;
+}
+
+int launch_synth_blocks_2d(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma, int64_t grow0,
+                           int64_t nrows, int64_t gnblk, int64_t gb0, int64_t nblk, uint8_t* dst) {
+  const int64_t nblocks = nrows * nblk;
+  if (nblocks == 0) return SI_OK;
+  int threads = 128;
+  k_synth_blocks<<<(unsigned)((nblocks + threads - 1) / threads), threads, 0, c->stream>>>(
+      qt, si_key(seed, tag), recipe, sigma, grow0, nblocks, dst, gnblk, gb0, nblk);
   SI_CUDA(cudaGetLastError());
   return SI_OK;
 }

@@ -55,14 +55,43 @@ def host_kv(cfg, seed, layer, seq, length):
     return k, v
 
 
-class DecodeModel:
-    """si_model*: weights, f16 KV cache and the graph-captured decode step."""
+def tp_slice(cfg, tp, rank, tensor):
+    """(grow0, rows, gb0, nblk, gnblk): the part of a whole tensor rank `rank` of `tp` holds."""
+    out = [ctypes.c_int64() for _ in range(5)]
+    N.call("si_tp_slice", ctypes.byref(cfg), tp, rank, tensor, *[ctypes.byref(o) for o in out])
+    return tuple(o.value for o in out)
 
-    def __init__(self, ctx, cfg):
-        self.ctx, self.cfg = ctx, cfg
+
+def exchange_handles(handle, group=None):
+    """Every rank's 64-byte buffer handle, in rank order, over torch.distributed."""
+    import torch.distributed as dist
+    got = [None] * dist.get_world_size(group)
+    dist.all_gather_object(got, bytes(handle), group=group)
+    return b"".join(got)
+
+
+class DecodeModel:
+    """si_model*: weights, f16 KV cache and the graph-captured decode step.
+    With tp > 1 this is rank `rank` of a tensor-parallel model; connect it to
+    the other ranks with tp_connect(exchange_handles(model.tp_handle()))."""
+
+    def __init__(self, ctx, cfg, tp=1, rank=0):
+        self.ctx, self.cfg, self.tp, self.rank = ctx, cfg, tp, rank
         h = ctypes.c_void_p()
-        N.call("si_model_create", ctx.handle, ctypes.byref(cfg), ctypes.byref(h))
+        N.call("si_model_create_tp", ctx.handle, ctypes.byref(cfg), tp, rank, ctypes.byref(h))
         self.handle = h
+
+    @property
+    def local_vocab(self):
+        return self.cfg.vocab // self.tp
+
+    def tp_handle(self):
+        buf = ctypes.create_string_buffer(64)
+        N.call("si_model_tp_handle", self.handle, buf, 64)
+        return buf.raw
+
+    def tp_connect(self, handles):
+        N.call("si_model_tp_connect", self.handle, handles, len(handles))
 
     def free(self):
         if self.handle:
@@ -95,7 +124,7 @@ class DecodeModel:
         """Greedy next token of each sequence (and optionally the logits)."""
         tok = np.ascontiguousarray(tokens, np.int32).ravel()
         out = np.empty(tok.size, np.int32)
-        lg = np.empty((tok.size, self.cfg.vocab), np.float32) if logits else None
+        lg = np.empty((tok.size, self.local_vocab), np.float32) if logits else None
         N.call("si_decode_step", self.handle, N.ptr(tok), tok.size, pos, N.ptr(out), N.ptr(lg))
         return (out, lg) if logits else out
 
