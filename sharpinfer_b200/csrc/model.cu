@@ -878,7 +878,7 @@ SI_EXPORT int si_model_synth(si_model* m, uint64_t seed) {
   if (!m) SI_FAIL(SI_ERR_INVALID, "si_model_synth: NULL model");
   si_ctx* c = m->c;
   SI_TRY(bind_device(c));
-  const si_model_config& cfg = m->cfg;
+  const si_model_config& cfg = m->gcfg;  // recipes (tags, scales) are those of the whole tensors
   std::vector<std::pair<int, int>> items;
   for (int l = 0; l < cfg.n_layers; l++)
     for (int t = SI_T_Q; t <= SI_T_FFN_NORM; t++) items.push_back({l, t});
