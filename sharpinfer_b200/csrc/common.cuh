@@ -46,26 +46,27 @@ void clear_error();
 namespace si {
 // Tensor parallelism over peer memory.  Every rank owns a communication
 // buffer mapped into every other rank (CUDA IPC):
-//   [0, 1024)     flags: u32 [2 kinds][8 source ranks] (Wo, Wdown partial
-//                 sums), then u32 [16 batch rows][8 ranks] (argmax)
-//   [1024, 2048)  argmax candidates: [16 batch rows][8 ranks] {f32, i32}
-//   [2048, ...)   partial sums: [2 kinds][tp source ranks][max_batch][hidden] f32
-// A producer stores its partial rows into the slot [kind][own rank] of every
-// rank, then raises flag [kind][own rank] of every rank to the step's value
-// (epoch * 2 * n_layers + 2 * layer + kind + 1, never 0); consumers wait for
-// all tp flags and add the slots in rank order, so every rank computes the
-// same sum.
+//   [0, 2048)     argmax candidates: [16 batch rows][8 ranks] x two 8-byte
+//                 words {value bits, tag}, {index, tag}
+//   [2048, ...)   partial sums: [2 kinds][tp source ranks][max_batch][hidden]
+//                 8-byte words {f32 bits, tag}
+// A producer stores each partial-sum element into slot [kind][own rank] of
+// every rank as ONE 8-byte store carrying the value and the step's tag
+// (epoch * 2 * n_layers + 2 * layer + kind + 1, never 0).  A consumer polls
+// each element it needs until the tag matches -- the 8-byte store is seen
+// whole or not at all -- so no fence, counter or flag is needed; it adds the
+// tp slots in rank order, so every rank computes the same sum.
 constexpr int SI_TP_MAX = 8;
-constexpr int SI_TP_FLAGS = 0, SI_TP_ARGMAX_FLAGS = 64, SI_TP_ARGMAX = 1024, SI_TP_SLOTS = 2048;
+constexpr int SI_TP_ARGMAX = 0, SI_TP_SLOTS = 2048;
 struct TpArgs {
   uint8_t* const* peers = nullptr;  // device array [tp] of comm buffer bases
   const unsigned* epoch = nullptr;  // step counter (StepParams::epoch)
-  int* counter = nullptr;           // CTA arrival counter of the producing kernel
   int tp = 1, rank = 0, kind = 0;
   int flag_add = 0;                 // 2 * layer + kind + 1
   int nlayers2 = 0;                 // 2 * n_layers
   int64_t slot_off = 0;             // byte offset of [kind][rank] slots in a comm buffer
-  int ld = 0;                       // floats per batch row (hidden)
+  int ld = 0;                       // elements per batch row (hidden)
+  __device__ __forceinline__ unsigned tag() const { return *epoch * (unsigned)nlayers2 + (unsigned)flag_add; }
 };
 // Consumer side of the tensor-parallel sum (k_prep, SI_PREP_RMSNORM_TP).
 struct PrepTp {
@@ -75,7 +76,7 @@ struct PrepTp {
   int tp = 1, kind = 0, flag_add = 0, nlayers2 = 0;
   int64_t slots_off = 0;            // byte offset of slots [kind][source 0]
   int64_t src_stride = 0;           // bytes between source ranks' slots
-  int ld = 0;                       // floats per batch row
+  int ld = 0;                       // elements per batch row
 };
 // Device scratch of the streaming matvec: partial sums of row tiles split
 // between warps ([tiles][slots][64] f32) and per-tile arrival counters
@@ -351,43 +352,31 @@ __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
 // Device error bits written by kernels whose bounded waits give up.
 enum { SI_DEVERR_WAIT_TIMEOUT = 1, SI_DEVERR_PEER_TIMEOUT = 2 };
 
-// ---- system-scope flags between GPUs (peer memory over NVLink) ----
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// ---- tagged 8-byte words between GPUs (peer memory over NVLink) ----
+// One 64-bit scalar access (single-copy atomic when 8-byte aligned): value in
+// the low word, tag in the high word.
+__device__ __forceinline__ void st_tagged(void* p, uint32_t bits, unsigned tag) {
+  const uint64_t w = (uint64_t)bits | ((uint64_t)tag << 32);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ uint2 ld_tagged(const void* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return make_uint2((uint32_t)w, (uint32_t)(w >> 32));
 }
-// Wait until flag p reaches `want` (flags only grow); gives up after ~1 s.
-__device__ __forceinline__ bool flag_wait(const unsigned* p, unsigned want) {
-  if ((int)(ld_acquire_sys(p) - want) >= 0) return true;
+// The word at p once its tag is `want` (tags only grow); after ~1 s gives up,
+// sets *err and returns what is there.
+__device__ __forceinline__ uint32_t wait_tagged(const void* p, unsigned want, int* err) {
+  uint2 v = ld_tagged(p);
+  if ((int)(v.y - want) >= 0) return v.x;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < (1u << 26); i++) {
-    if ((int)(ld_acquire_sys(p) - want) >= 0) return true;
-    if ((i & 63u) == 63u) {
-      if (globaltimer_ns() - t0 > 1000000000ull) return false;
-      __nanosleep(64);
-    }
+    v = ld_tagged(p);
+    if ((int)(v.y - want) >= 0) return v.x;
+    if ((i & 63u) == 63u && globaltimer_ns() - t0 > 1000000000ull) break;
   }
-  return false;
-}
-// End of a kernel that stored tp partial sums into peer slots: the last CTA
-// to finish raises flag [kind][rank] in every rank's buffer.
-__device__ __forceinline__ void tp_signal(const TpArgs& a) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const int n = (int)(gridDim.x * gridDim.y * gridDim.z);
-    if (atomicAdd(a.counter, 1) == n - 1) {
-      *a.counter = 0;
-      __threadfence_system();
-      const unsigned v = *a.epoch * (unsigned)a.nlayers2 + (unsigned)a.flag_add;
-      for (int p = 0; p < a.tp; p++)
-        st_release_sys((unsigned*)(a.peers[p] + SI_TP_FLAGS) + a.kind * SI_TP_MAX + a.rank, v);
-    }
-  }
+  atomicOr(err, SI_DEVERR_PEER_TIMEOUT);
+  return v.x;
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

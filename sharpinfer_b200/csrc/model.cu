@@ -148,21 +148,18 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
         }
         const unsigned want = *tp.epoch + 1u;
         for (int p = 0; p < tp.tp; p++) {
-          float2* slot = (float2*)(tp.peers[p] + SI_TP_ARGMAX) + b * SI_TP_MAX + tp.rank;
-          *slot = make_float2(cv, __int_as_float(ci));
+          uint2* slot = (uint2*)(tp.peers[p] + SI_TP_ARGMAX) + (b * SI_TP_MAX + tp.rank) * 2;
+          st_tagged(slot, __float_as_uint(cv), want);
+          st_tagged(slot + 1, (uint32_t)ci, want);
         }
-        __threadfence_system();
-        for (int p = 0; p < tp.tp; p++)
-          st_release_sys((unsigned*)(tp.peers[p] + SI_TP_ARGMAX_FLAGS) + b * SI_TP_MAX + tp.rank, want);
         float gv = -INFINITY;
         int gi = -1;
         for (int r = 0; r < tp.tp; r++) {
-          if (!flag_wait((const unsigned*)(tp.comm + SI_TP_ARGMAX_FLAGS) + b * SI_TP_MAX + r, want))
-            atomicOr(tp.err, SI_DEVERR_PEER_TIMEOUT);
-          const float2 c = ((const float2*)(tp.comm + SI_TP_ARGMAX))[b * SI_TP_MAX + r];
-          const int idx = __float_as_int(c.y);
-          if (gi < 0 || c.x > gv || (c.x == gv && idx < gi)) {
-            gv = c.x;
+          const uint2* c = (const uint2*)(tp.comm + SI_TP_ARGMAX) + (b * SI_TP_MAX + r) * 2;
+          const float v = __uint_as_float(wait_tagged(c, want, tp.err));
+          const int idx = (int)wait_tagged(c + 1, want, tp.err);
+          if (gi < 0 || v > gv || (v == gv && idx < gi)) {
+            gv = v;
             gi = idx;
           }
         }
@@ -260,7 +257,6 @@ struct si_model {
   uint8_t* peer_base[SI_TP_MAX] = {};      // every rank's buffer mapped here
   uint8_t** peers_dev = nullptr;           // the same table on the device
   bool connected = false;
-  int* tp_counter = nullptr;               // arrival counters of the two producing kernels
   unsigned epoch = 0;                      // steps taken (mirrors StepParams::epoch)
   int G = 0, qkv_rows = 0, Kmax = 0;
   int splits_max = 0, chunk_max = 0;
@@ -459,14 +455,14 @@ int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int 
 // and of its consumer, the RmsNorm prep that adds the partial sums.
 QmvBuffers tp_producer(si_model* m, int layer, int kind) {
   QmvBuffers qb = m->c->qmv();
-  const int64_t slot = (int64_t)m->cfg.max_batch * m->cfg.hidden * 4;
-  qb.tp = TpArgs{m->peers_dev, &m->dparams->epoch, m->tp_counter + kind, m->tp, m->rank, kind,
-                 2 * layer + kind + 1, 2 * m->cfg.n_layers,
-                 SI_TP_SLOTS + (int64_t)kind * m->tp * slot + (int64_t)m->rank * slot, m->cfg.hidden};
+  const int64_t slot = (int64_t)m->cfg.max_batch * m->cfg.hidden * 8;
+  qb.tp = TpArgs{m->peers_dev, &m->dparams->epoch, m->tp, m->rank, kind, 2 * layer + kind + 1,
+                 2 * m->cfg.n_layers, SI_TP_SLOTS + (int64_t)kind * m->tp * slot + (int64_t)m->rank * slot,
+                 m->cfg.hidden};
   return qb;
 }
 PrepTp tp_consumer(si_model* m, int layer, int kind) {
-  const int64_t slot = (int64_t)m->cfg.max_batch * m->cfg.hidden * 4;
+  const int64_t slot = (int64_t)m->cfg.max_batch * m->cfg.hidden * 8;
   PrepTp p;
   p.comm = m->comm;
   p.epoch = &m->dparams->epoch;
@@ -726,8 +722,7 @@ SI_EXPORT int si_model_create_tp(si_ctx* ctx, const si_model_config* cfg, int tp
   ALLOC(x, (size_t)B * h * 4);
   ALLOC(x2, (size_t)B * h * 4);
   if (tp > 1) {
-    ALLOC(comm, SI_TP_SLOTS + (size_t)2 * tp * B * h * 4);
-    ALLOC(tp_counter, 2 * sizeof(int));
+    ALLOC(comm, SI_TP_SLOTS + (size_t)2 * tp * B * h * 8);
     ALLOC(peers_dev, SI_TP_MAX * sizeof(uint8_t*));
   }
   ALLOC(qkv, (size_t)B * m->qkv_rows * 4);
@@ -740,8 +735,7 @@ SI_EXPORT int si_model_create_tp(si_ctx* ctx, const si_model_config* cfg, int tp
   ALLOC(dparams, sizeof(StepParams));
 #undef ALLOC
   cudaError_t e = cudaMemset(m->kcache, 0, kv_elems * 2);
-  if (e == cudaSuccess && m->comm) e = cudaMemset(m->comm, 0, SI_TP_SLOTS + (size_t)2 * tp * B * h * 4);
-  if (e == cudaSuccess && m->tp_counter) e = cudaMemset(m->tp_counter, 0, 2 * sizeof(int));
+  if (e == cudaSuccess && m->comm) e = cudaMemset(m->comm, 0, SI_TP_SLOTS + (size_t)2 * tp * B * h * 8);
   if (e == cudaSuccess) e = cudaMemset(m->vcache, 0, kv_elems * 2);
   if (e == cudaSuccess) e = cudaMallocHost(&m->hparams, sizeof(StepParams));
   if (e == cudaSuccess) e = cudaMallocHost(&m->hargmax, sizeof(int) * SI_MAX_BATCH);

@@ -132,18 +132,15 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
     }
   }
   if (mode == SI_PREP_RMSNORM_TP) {
-    // residual + the tp partial sums, added in rank order (identical on every rank)
-    if (tid == 0) {
-      const unsigned want = *tpp.epoch * (unsigned)tpp.nlayers2 + (unsigned)tpp.flag_add;
-      const unsigned* fl = (const unsigned*)(tpp.comm + SI_TP_FLAGS) + tpp.kind * SI_TP_MAX;
-      for (int r = 0; r < tpp.tp; r++)
-        if (!flag_wait(fl + r, want)) atomicOr(tpp.err, SI_DEVERR_PEER_TIMEOUT);
-    }
-    __syncthreads();
+    // residual + the tp partial sums, added in rank order (identical on every
+    // rank); each partial-sum element is awaited through its tag
+    const unsigned want = *tpp.epoch * (unsigned)tpp.nlayers2 + (unsigned)tpp.flag_add;
     auto res = [&](int i) {
       float a = xb[i];
-      for (int r = 0; r < tpp.tp; r++)
-        a = __fadd_rn(a, ((const float*)(tpp.comm + tpp.slots_off + r * tpp.src_stride))[(int64_t)b * tpp.ld + i]);
+      for (int r = 0; r < tpp.tp; r++) {
+        const uint2* sl = (const uint2*)(tpp.comm + tpp.slots_off + r * tpp.src_stride) + (int64_t)b * tpp.ld + i;
+        a = __fadd_rn(a, __uint_as_float(wait_tagged(sl, want, tpp.err)));
+      }
       return a;
     };
     float ss = 0.f;
@@ -255,7 +252,9 @@ __device__ __forceinline__ void qmv_epilogue(const float (&tg)[NMG], const float
     const int64_t row = (int64_t)tile * 16 + gg + 8 * half;
     if (bt < B && row < rows) {
       if (EPI == SI_EPI_TP) {
-        for (int p = 0; p < tpa.tp; p++) ((float*)(tpa.peers[p] + tpa.slot_off))[(int64_t)bt * tpa.ld + row] = v;
+        const unsigned tag = tpa.tag();
+        for (int p = 0; p < tpa.tp; p++)
+          st_tagged((uint2*)(tpa.peers[p] + tpa.slot_off) + (int64_t)bt * tpa.ld + row, __float_as_uint(v), tag);
       } else {
         float* dst = y + (int64_t)bt * rows + row;
         if (EPI == SI_EPI_ADD) *dst += v;
@@ -518,13 +517,14 @@ template <int EPI, int B>
 __device__ __forceinline__ void store_tile(float* __restrict__ y, int64_t rows, int T, int lane,
                                            float v0, float v8, const TpArgs& tpa) {
   const int g = lane >> 2, t = lane & 3;
-  if (EPI == SI_EPI_TP) {  // partial rows into slot [kind][rank] of every rank
+  if (EPI == SI_EPI_TP) {  // partial rows into slot [kind][rank] of every rank, tagged
     if (t < B) {
       const int64_t r0 = (int64_t)T * 16 + g, r1 = r0 + 8;
+      const unsigned tag = tpa.tag();
       for (int p = 0; p < tpa.tp; p++) {
-        float* yb = (float*)(tpa.peers[p] + tpa.slot_off) + (int64_t)t * tpa.ld;
-        if (r0 < rows) yb[r0] = v0;
-        if (r1 < rows) yb[r1] = v8;
+        uint2* yb = (uint2*)(tpa.peers[p] + tpa.slot_off) + (int64_t)t * tpa.ld;
+        if (r0 < rows) st_tagged(yb + r0, __float_as_uint(v0), tag);
+        if (r1 < rows) st_tagged(yb + r1, __float_as_uint(v8), tag);
       }
     }
     return;
@@ -736,7 +736,6 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
       if (lane == 0) scr.count[T] = 0;
     }
   }
-  if (EPI == SI_EPI_TP) tp_signal(scr.tp);
 }
 
 // ---------------------------------------------------------------------------
@@ -986,7 +985,6 @@ __global__ void __launch_bounds__(NW * 32, 1)
       if (lane == 0) scr.count[T] = 0;
     }
   }
-  if (EPI == SI_EPI_TP) tp_signal(scr.tp);
 }
 
 // ---------------------------------------------------------------------------
@@ -1027,7 +1025,6 @@ __global__ void __launch_bounds__(256) k_qmv_reg(const uint8_t* __restrict__ W, 
     else unit_q80<NMG>(ld, lane, min(QPU, nblk - u * QPU), tg, tg8);
   }
   qmv_epilogue<NMG, EPI>(tg, tg8, B, rows, y, (int)blockIdx.x, tpa);
-  if (EPI == SI_EPI_TP) tp_signal(tpa);
 }
 
 cudaLaunchConfig_t make_cfg(cudaStream_t s, dim3 grid, dim3 block, size_t smem, bool pdl,
@@ -1230,7 +1227,7 @@ int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
   const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp}, qb.split_bytes, qb.count_n};
   if (epi == SI_EPI_ADD) return dispatch_qt<SI_EPI_ADD>(s, w, xprep, B, y, scr, qb.sms, pdl);
   if (epi == SI_EPI_TP) {
-    if (qb.tp.tp < 1 || !qb.tp.peers || !qb.tp.counter) SI_FAIL(SI_ERR_INVALID, "qmatvec: tensor-parallel epilogue without peers");
+    if (qb.tp.tp < 1 || !qb.tp.peers || !qb.tp.epoch) SI_FAIL(SI_ERR_INVALID, "qmatvec: tensor-parallel epilogue without peers");
     return dispatch_qt<SI_EPI_TP>(s, w, xprep, B, y, scr, qb.sms, pdl);
   }
   return dispatch_qt<SI_EPI_STORE>(s, w, xprep, B, y, scr, qb.sms, pdl);
