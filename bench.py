@@ -205,6 +205,105 @@ def matvec_roofline(ctx, torch, dev, reps=40):
     return ms, q4k_bytes(rows, cols) + 4 * (cols + rows)
 
 
+PREFILL_SHAPES = ((4096, 4096), (14336, 4096), (4096, 14336))  # (N rows, K cols): q/o, gate/up, down
+
+
+def run_prefill(args, world, rank, local):
+    """Prefill GEMM (si_qgemm, tcgen05) on the 8B projection shapes at M tokens:
+    y = x W^T, W Q4_K, x bf16.  value: whole-call TFLOP/s over the three shapes
+    (dequantising pass + conversion + GEMM, weights in HBM, x resident);
+    roofline: the gate/up shape with the f16 weight cached (conversion + GEMM)."""
+    import torch
+    from sharpinfer_b200 import B200Context, native as N
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ctx = B200Context(local)
+    torch.cuda.set_stream(ctx.torch_stream)
+    s = ctx.torch_stream
+    M = args.prefill_m
+
+    def timed(fn, reps):
+        for _ in range(args.warmup):
+            fn()
+        ctx.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(reps):
+                fn()
+        g.replay()
+        ctx.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+        ctx.synchronize()
+        del g
+        return e0.elapsed_time(e1) / reps
+
+    flops = tot_ms = 0.0
+    rows = []
+    roof = None
+    host_ms = 0.0
+    clocks = ClockSampler(local)
+    clocks.start()
+    for n, k in PREFILL_SHAPES:
+        w = ctx.synth_weight(N.SI_Q4_K, n, k, SEED, 91, N.SYNTH_MODEL, 1.0 / (23.3 * 64.0))
+        x = torch.randn(M, k, device=dev).to(torch.bfloat16)
+        y = torch.empty(M, n, device=dev)
+        ms = timed(lambda: ctx.qgemm(w, x, out=y), args.steps)
+        fl = 2.0 * M * n * k
+        flops += fl
+        tot_ms += ms
+        rows.append({"N": n, "K": k, "us": round(ms * 1e3, 1), "tflops": round(fl / ms / 1e9, 1)})
+        # e2e: x from pinned host memory, y back to host, every call
+        xh = x.cpu().pin_memory()
+        yh = torch.empty(M, n, pin_memory=True)
+        for _ in range(2):
+            x.copy_(xh, non_blocking=True)
+            ctx.qgemm(w, x, out=y)
+            yh.copy_(y, non_blocking=True)
+        ctx.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            x.copy_(xh, non_blocking=True)
+            ctx.qgemm(w, x, out=y)
+            yh.copy_(y, non_blocking=True)
+        ctx.synchronize()
+        host_ms += (time.perf_counter() - t0) * 1e3 / args.steps
+        if n == 14336:
+            ctx.qgemm_cache_weight(w)
+            roof = (fl, timed(lambda: ctx.qgemm(w, x, out=y), args.steps))
+        w.free()
+    clk = clocks.stop()
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peak = peaks.get("bf16_tflops", 1590.0)
+    ach = roof[0] / roof[1] / 1e9
+    line = {"metric": "prefill GEMM TFLOP/s (Llama-3-8B Q4_K projections, bf16 activations)",
+            "value": round(flops / tot_ms / 1e9, 1), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(tot_ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 x f16 -> f32 (tcgen05 kind::f16)", "data": "synthetic",
+            "config": {"workload": "prefill%d: M=%d x (N,K) in %s, Q4_K weights" % (M, M, list(PREFILL_SHAPES)),
+                       "l2": "weights and activations per shape > L2 (HBM-resident)"},
+            "shapes": rows,
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(ach / peak, 4), "traffic": None,
+                         "kernel": "k_gemm_tc (+ bf16->f16 conversion), N=14336 K=4096, f16 weight cached",
+                         "peak_source": "measured" if peaks else "fallback"},
+            "e2e": {"value": round(flops / host_ms / 1e9, 1), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": sum(M * k * 2 for n, k in PREFILL_SHAPES),
+                    "d2h_bytes_per_step": sum(M * n * 4 for n, k in PREFILL_SHAPES)},
+            "gpu_launches": 3 * 3 * args.steps, "clocks": clk}
+    print(json.dumps(line), flush=True)
+    # release tensors that live on the context's stream before it goes away
+    del x, y, xh, yh
+    ctx.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream(dev))
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    ctx.close()
+
+
 def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -321,11 +420,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=32, help="transformer layers (32 = the full 8B model)")
     ap.add_argument("--ctx", type=int, default=KV_LEN, help="prefilled KV positions")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--prefill-m", type=int, default=2048, help="tokens of the prefill GEMM workload")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
     if args.impl == "reference":
         run_reference(args, world, rank)
+    elif args.workload == "prefill":
+        if rank == 0:
+            run_prefill(args, world, rank, local)
     else:
         run_ours(args, world, rank, local)
 

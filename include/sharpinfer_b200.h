@@ -162,6 +162,11 @@ SI_EXPORT int si_qmatvec_prepared(si_ctx* ctx, const si_weight* w, float* y_dev,
  * dequantised to f16 into context scratch, then multiplied on the tensor
  * cores (tcgen05, f32 accumulation); cols must be a multiple of 64. */
 SI_EXPORT int si_qgemm(si_ctx* ctx, const si_weight* w, const uint16_t* x_bf16_dev, float* y_dev, int M);
+/* Keep a dequantised f16 copy of W (rows * cols * 2 bytes of device memory,
+ * freed with the weight) so that later si_qgemm calls skip the dequantising
+ * pass -- for prefill in several chunks over the same weights.  The copy is
+ * what DequantizeTensor (Quantization.cs:415-469) produces, rounded to f16. */
+SI_EXPORT int si_qgemm_cache_weight(si_ctx* ctx, si_weight* w);
 
 /* Same with host buffers (copied in, computed, copied out, synchronised),
  * the calling convention of cuda_mat_vec_mul (kernels.cu:67-87). */

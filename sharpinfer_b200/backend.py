@@ -176,6 +176,10 @@ class B200Context:
         self._leave(cur)
         return out
 
+    def qgemm_cache_weight(self, w):
+        """Keep a dequantised f16 copy of w for later qgemm calls."""
+        N.call("si_qgemm_cache_weight", self.handle, w.handle)
+
     def qmatvec_host(self, w, x):
         """Same with host numpy arrays; synchronous (the cuda_mat_vec_mul convention)."""
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, w.cols)

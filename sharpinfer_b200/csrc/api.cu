@@ -293,6 +293,7 @@ SI_EXPORT int si_weight_free(si_weight* w) {
   if (!w) return SI_OK;
   cudaSetDevice(w->device);
   if (w->dev) cudaFree(w->dev);
+  if (w->f16) cudaFree(w->f16);
   delete w;
   return SI_OK;
 }

@@ -149,6 +149,7 @@ struct si_weight {
   void* dev = nullptr;
   size_t bytes = 0;
   int device = 0;
+  void* f16 = nullptr;  // optional dequantised [rows][cols] f16 copy for prefill (si_qgemm_cache_weight)
 };
 
 namespace si {

@@ -30,10 +30,15 @@
 namespace si {
 namespace {
 
-constexpr int GM = 128, GN = 256, GK = 64, GST = 4;
+constexpr int GM = 128, GK = 64, GST = 4;
 constexpr int A_BYTES = GM * GK * 2;  // 16 KB
-constexpr int B_BYTES = GN * GK * 2;  // 32 KB
-constexpr int GEMM_SMEM = GST * (A_BYTES + B_BYTES) + 1024 + 256;
+template <int BN>
+struct GemmCfg {
+  static constexpr int B_BYTES = BN * GK * 2;  // 32 KB at BN = 256
+  static constexpr int SMEM = GST * (A_BYTES + B_BYTES) + 1024 + 256;
+  // kind::f16 instruction descriptor: D f32, A and B f16, both K-major, N = BN, M = GM.
+  static constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
+};
 
 // f16 of one (row, block) in the reference's f32 arithmetic.
 __global__ void k_dequant_f16(int qt, const uint8_t* __restrict__ W, int64_t rows, int64_t nblk,
@@ -178,8 +183,6 @@ __device__ __forceinline__ uint64_t sdesc_k128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// kind::f16 instruction descriptor: D f32, A and B f16, both K-major, N = GN, M = GM.
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(GN >> 3) << 17) | ((uint32_t)(GM >> 4) << 24);
 
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int c0, int c1, uint32_t bar) {
   asm volatile(
@@ -211,9 +214,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+template <int GN>
 __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                     const __grid_constant__ CUtensorMap tmB, float* __restrict__ Y,
                                                     int M, int N, int K, int* err) {
+  constexpr int B_BYTES = GemmCfg<GN>::B_BYTES;
+  constexpr uint32_t IDESC = GemmCfg<GN>::IDESC;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sA = base, sB = base + GST * A_BYTES, bars = sB + GST * B_BYTES;
@@ -334,51 +340,90 @@ int make_tmap(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t cols, int 
 
 }  // namespace
 
-int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int M) {
-  const int64_t N = w->rows, K = w->cols;
-  if (K % GK) SI_FAIL(SI_ERR_UNSUPPORTED, "qgemm: cols %lld not a multiple of %d", (long long)K, GK);
-  SI_TRY(ensure(c->stage[0], (size_t)N * K * 2));
-  SI_TRY(ensure(c->stage[1], (size_t)M * K * 2));
-  __half* wf = (__half*)c->stage[0].ptr;
-  __half* xf = (__half*)c->stage[1].ptr;
+// f16 copy of W (rows x cols) at dst on the context stream.
+int dequant_f16(si_ctx* c, const si_weight* w, __half* dst) {
+  const int64_t N = w->rows;
   if (w->qtype == SI_Q4_K) {
     const int64_t ntb = w->tiles * w->nblk;
-    k_dequant_q4k_f16<<<(unsigned)((ntb + 7) / 8), 256, 0, c->stream>>>((const uint8_t*)w->dev, N, w->nblk, ntb, wf);
+    k_dequant_q4k_f16<<<(unsigned)((ntb + 7) / 8), 256, 0, c->stream>>>((const uint8_t*)w->dev, N, w->nblk, ntb, dst);
   } else {
     const int64_t nb = N * w->nblk;
     k_dequant_f16<<<(unsigned)((nb + 127) / 128), 128, 0, c->stream>>>(w->qtype, (const uint8_t*)w->dev, N, w->nblk,
-                                                                        wf);
+                                                                        dst);
   }
   SI_CUDA(cudaGetLastError());
+  return SI_OK;
+}
+
+int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int M) {
+  const int64_t N = w->rows, K = w->cols;
+  if (K % GK) SI_FAIL(SI_ERR_UNSUPPORTED, "qgemm: cols %lld not a multiple of %d", (long long)K, GK);
+  SI_TRY(ensure(c->stage[1], (size_t)M * K * 2));
+  __half* wf = (__half*)w->f16;
+  if (!wf) {  // no cached copy: dequantise into scratch for this call
+    SI_TRY(ensure(c->stage[0], (size_t)N * K * 2));
+    wf = (__half*)c->stage[0].ptr;
+    SI_TRY(dequant_f16(c, w, wf));
+  }
+  __half* xf = (__half*)c->stage[1].ptr;
   const int64_t nx = (int64_t)M * K;
   if (((uintptr_t)x & 15) != 0) SI_FAIL(SI_ERR_INVALID, "si_qgemm: x must be 16-byte aligned");
   k_bf16_to_f16<<<(unsigned)((nx / 8 + 256) / 256), 256, 0, c->stream>>>(x, xf, nx);
   SI_CUDA(cudaGetLastError());
+  // 256-wide tiles, or 128-wide when 256 would leave SMs idle
+  const int64_t tiles256 = ((N + 255) / 256) * (((int64_t)M + GM - 1) / GM);
+  const int GN = tiles256 < c->sm_count ? 128 : 256;
   CUtensorMap ta, tb;
   SI_TRY(make_tmap(&ta, xf, M, K, GM));
   SI_TRY(make_tmap(&tb, wf, N, K, GN));
-  static uint64_t attr_set = 0;
-  if (c->device < 64 && !(attr_set & (1ull << c->device))) {
-    SI_CUDA(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, GEMM_SMEM));
-    attr_set |= 1ull << c->device;
+  static uint64_t attr_set[2] = {0, 0};
+  const int ai = GN == 128 ? 0 : 1;
+  const int smem = GN == 128 ? GemmCfg<128>::SMEM : GemmCfg<256>::SMEM;
+  if (c->device < 64 && !(attr_set[ai] & (1ull << c->device))) {
+    if (GN == 128) SI_CUDA(cudaFuncSetAttribute(k_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    else SI_CUDA(cudaFuncSetAttribute(k_gemm_tc<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set[ai] |= 1ull << c->device;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((N + GN - 1) / GN), (unsigned)((M + GM - 1) / GM));
   cfg.blockDim = dim3(192);
-  cfg.dynamicSmemBytes = GEMM_SMEM;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = c->stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc, ta, tb, y, M, (int)N, (int)K, c->dev_err));
+  if (GN == 128) SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<128>, ta, tb, y, M, (int)N, (int)K, c->dev_err));
+  else SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<256>, ta, tb, y, M, (int)N, (int)K, c->dev_err));
   return SI_OK;
 }
 
 }  // namespace si
 
 using namespace si;
+
+extern "C" SI_EXPORT int si_qgemm_cache_weight(si_ctx* c, si_weight* w) {
+  clear_error();
+  if (!c || !w) SI_FAIL(SI_ERR_INVALID, "si_qgemm_cache_weight: NULL argument");
+  if (w->device != c->device) SI_FAIL(SI_ERR_INVALID, "si_qgemm_cache_weight: weight on device %d, context on %d",
+                                      w->device, c->device);
+  if (w->f16) return SI_OK;
+  SI_TRY(bind_device(c));
+  void* p = nullptr;
+  const size_t bytes = (size_t)w->rows * w->cols * 2;
+  const cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess)
+    SI_FAIL(e == cudaErrorMemoryAllocation ? SI_ERR_OOM : SI_ERR_CUDA, "cudaMalloc(%zu) failed: %s", bytes,
+            cudaGetErrorString(e));
+  const int st = dequant_f16(c, w, (__half*)p);
+  if (st != SI_OK || cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    cudaFree(p);
+    return st != SI_OK ? st : SI_ERR_CUDA;
+  }
+  w->f16 = p;
+  return SI_OK;
+}
 
 extern "C" SI_EXPORT int si_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x_bf16, float* y, int M) {
   clear_error();

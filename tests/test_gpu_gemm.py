@@ -29,6 +29,7 @@ def bf16_round(a):
     (N.SI_Q6_K, 200, 520, 1024),
     (N.SI_Q8_0, 130, 384, 320),     # Q8_0, K not a multiple of 256
     (N.SI_Q4_K, 256, 512, 14336),   # down-projection K
+    (N.SI_Q4_K, 1280, 4096, 256),   # enough 256-wide tiles for every SM: the 256-column variant
 ])
 def test_qgemm_matches_oracle(ctx, qt, M, rows, cols):
     import torch
@@ -54,4 +55,17 @@ def test_qgemm_repeatable_and_rejects_bad_shapes(ctx):
     assert torch.equal(a, b)
     with pytest.raises(N.SIError):
         N.call("si_qgemm", ctx.handle, w.handle, N.ptr(x), N.ptr(a), 0)
+    w.free()
+
+
+def test_cached_f16_weight_gives_the_same_result(ctx):
+    import torch
+    blocks = synth_blocks_host(N.SI_Q4_K, 512, 1024, 8, 2, N.SYNTH_PLAIN, 0.01)
+    w = ctx.upload(N.SI_Q4_K, blocks, 512, 1024)
+    x = torch.randn(200, 1024, device="cuda").to(torch.bfloat16)
+    a = ctx.qgemm(w, x)
+    ctx.qgemm_cache_weight(w)
+    b = ctx.qgemm(w, x)
+    ctx.synchronize()
+    assert torch.equal(a, b)
     w.free()
