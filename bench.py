@@ -39,6 +39,11 @@ SEED = 20261201
 KV_LEN = 4096
 START_TOKEN = 128000
 METRIC = "decode tok/s (Llama-3-8B Q4_K_M, ctx 4096, batch 1)"
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up k_qmv1 launch
+# (28672 x 4096 Q4_K, batch 1) from an ncu --set full capture of
+# `bench.py --layers 2` (summary under profiles/): the algorithmic bytes,
+# no re-reads.
+GATEUP_TRAFFIC = 66131712
 
 
 def measured_peaks():
@@ -366,10 +371,7 @@ def run_ours(args, world, rank, local):
         peak, peak_kind = measured_peaks()
         achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
         tb = token_bytes(cfg, args.ctx + args.warmup + args.steps // 2)
-        traffic = None
-        tp = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tp):
-            traffic = json.load(open(tp)).get("q4k_gateup_bytes_per_launch")
+        traffic = GATEUP_TRAFFIC
         line = {
             "metric": METRIC, "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -381,7 +383,7 @@ def run_ours(args, world, rank, local):
                        "l2": "inputs larger than L2 (%.2f GB streamed per step)" % (tb / 1e9)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "k_qmv_warp Q4_K, fused gate/up 28672x4096 (66 MB), batch 1",
+                         "kernel": "k_qmv1 (batch-1 Q4_K), fused gate/up 28672x4096 (66 MB)",
                          "peak_source": peak_kind + " (burst copy)"},
             "decode_roofline": {"bytes_per_token": tb, "achieved_gbs": round(tb / (ms * 1e-3) / 1e9, 1),
                                 "frac": round(tb / (ms * 1e-3) / 1e9 / (peak * world), 4)},
