@@ -279,6 +279,15 @@ def run_prefill(args, world, rank, local):
             ctx.qgemm_cache_weight(w)
             roof = (fl, timed(lambda: ctx.qgemm(w, x, out=y), args.steps))
         w.free()
+    # flash prefill attention at the same M: 32 q heads over 8 kv heads, d = 128, causal
+    H, Hkv = 32, 8
+    q = torch.randn(1, H, M, 128, device=dev).to(torch.bfloat16)
+    kk = torch.randn(1, Hkv, M, 128, device=dev).to(torch.bfloat16)
+    vv = torch.randn(1, Hkv, M, 128, device=dev).to(torch.bfloat16)
+    ao = torch.empty(1, H, M, 128, device=dev)
+    att_ms = timed(lambda: ctx.attn_prefill(q, kk, vv, 1.0 / 128 ** 0.5, True, out=ao), args.steps)
+    att_flops = 4.0 * M * M * 128 * H / 2
+    del q, kk, vv, ao
     clk = clocks.stop()
     peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
         os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
@@ -291,6 +300,8 @@ def run_prefill(args, world, rank, local):
             "config": {"workload": "prefill%d: M=%d x (N,K) in %s, Q4_K weights" % (M, M, list(PREFILL_SHAPES)),
                        "l2": "weights and activations per shape > L2 (HBM-resident)"},
             "shapes": rows,
+            "attention": {"kernel": "k_attn_prefill (mma.sync bf16, causal, 32/8 heads, d 128)", "seq": M,
+                          "us": round(att_ms * 1e3, 1), "tflops": round(att_flops / att_ms / 1e9, 1)},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(ach / peak, 4), "traffic": None,
                          "kernel": "k_gemm_tc (+ bf16->f16 conversion), N=14336 K=4096, f16 weight cached",

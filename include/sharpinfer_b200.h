@@ -162,6 +162,17 @@ SI_EXPORT int si_qmatvec_prepared(si_ctx* ctx, const si_weight* w, float* y_dev,
  * dequantised to f16 into context scratch, then multiplied on the tensor
  * cores (tcgen05, f32 accumulation); cols must be a multiple of 64. */
 SI_EXPORT int si_qgemm(si_ctx* ctx, const si_weight* w, const uint16_t* x_bf16_dev, float* y_dev, int M);
+/* Prefill attention on the tensor cores: FlashAttention.Forward
+ * (src/SharpInfer.Core/Layers/FlashAttention.cs:59-167) for bf16 q [batch][heads][seq][128],
+ * k, v [batch][kv_heads][kv][128] (grouped-query: head h reads kv head
+ * h / (heads / kv_heads)), f32 o [batch][heads][seq][128], all device
+ * pointers (16-byte aligned).  causal != 0 lets query i see keys
+ * j <= i + start_pos; a query with no visible key gets 0.  Asynchronous on
+ * the context stream. */
+SI_EXPORT int si_attn_prefill(si_ctx* ctx, const uint16_t* q_bf16, const uint16_t* k_bf16, const uint16_t* v_bf16,
+                              float* o, int batch, int heads, int kv_heads, int seq, int kv, int head_dim, float scale,
+                              int causal, int start_pos);
+
 /* Keep a dequantised f16 copy of W (rows * cols * 2 bytes of device memory,
  * freed with the weight) so that later si_qgemm calls skip the dequantising
  * pass -- for prefill in several chunks over the same weights.  The copy is

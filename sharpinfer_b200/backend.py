@@ -176,6 +176,24 @@ class B200Context:
         self._leave(cur)
         return out
 
+    def attn_prefill(self, q, k, v, scale, causal=True, start_pos=None, out=None):
+        """FlashAttention.Forward on the tensor cores: bf16 q [B, H, S, 128], k/v [B, Hkv, KV, 128]
+        (CUDA tensors); returns f32 [B, H, S, 128].  start_pos defaults to KV - S."""
+        torch = _torch()
+        B, H, S, D = q.shape
+        Hkv, KV = k.shape[1], k.shape[2]
+        if start_pos is None:
+            start_pos = KV - S
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        cur = self._enter()
+        with torch.cuda.stream(self.torch_stream):
+            if out is None:
+                out = torch.empty((B, H, S, D), dtype=torch.float32, device=q.device)
+            N.call("si_attn_prefill", self.handle, N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(out), B, H, Hkv, S, KV, D,
+                   float(scale), int(bool(causal)), int(start_pos))
+        self._leave(cur)
+        return out
+
     def qgemm_cache_weight(self, w):
         """Keep a dequantised f16 copy of w for later qgemm calls."""
         N.call("si_qgemm_cache_weight", self.handle, w.handle)

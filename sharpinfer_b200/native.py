@@ -70,6 +70,7 @@ _SIGS = {
     "si_qmatvec_noalloc": (_i32, [_c_p, _c_p, _c_p, _i32, _c_p]),
     "si_qgemm": (_i32, [_c_p, _c_p, _c_p, _c_p, _i32]),
     "si_qgemm_cache_weight": (_i32, [_c_p, _c_p]),
+    "si_attn_prefill": (_i32, [_c_p, _c_p, _c_p, _c_p, _c_p] + [_i32] * 6 + [ctypes.c_float, _i32, _i32]),
     "si_model_create_tp": (_i32, [_c_p, ctypes.POINTER(ModelConfig), _i32, _i32, ctypes.POINTER(_c_p)]),
     "si_model_tp_handle": (_i32, [_c_p, _c_p, _i32]),
     "si_model_tp_connect": (_i32, [_c_p, _c_p, _i32]),
