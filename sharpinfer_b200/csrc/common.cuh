@@ -100,12 +100,16 @@ inline int64_t qmv_warp_grid(int64_t units, int nw, int sms) {
 inline void qmv_scratch_need(int64_t tiles, int64_t nunit, int sms, size_t* split_bytes,
                              int64_t* counts) {
   int64_t worst = 0;
-  const int cfgs[4][2] = {{8, 1}, {16, 1}, {8, 2}, {4, 2}};  // (warps, grid cap in SMs)
-  for (const auto& cf : cfgs) {
-    const int nw = cf[0];
-    const int64_t units = tiles * nunit, grid = qmv_warp_grid(units, nw, cf[1] * sms);
+  for (const int nw : {8, 16}) {  // k_qmv_warp: units split over grid x nw warps
+    const int64_t units = tiles * nunit, grid = qmv_warp_grid(units, nw, sms);
     const int64_t minr = units / (grid * nw);
     const int64_t maxc = minr > 0 ? (nunit - 1 + minr - 1) / minr + 1 : nunit + 1;
+    if (maxc > worst) worst = maxc;
+  }
+  if (nunit % 2 == 0 && tiles * nunit / 2 >= 16) {  // k_qmv1: unit pairs over grid x 16 warps
+    const int64_t P = tiles * nunit / 2, grid = P / 16 < sms ? P / 16 : sms;
+    const int64_t minr = P / (grid * 16), npt = nunit / 2;
+    const int64_t maxc = (npt - 1 + minr - 1) / minr + 1;
     if (maxc > worst) worst = maxc;
   }
   *split_bytes = (size_t)tiles * worst * 64 * 4;

@@ -773,8 +773,8 @@ __device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float
 
 template <int EPI, int NW, int NS>
 __global__ void __launch_bounds__(NW * 32, 1)
-    k_qmv1(const uint8_t* __restrict__ W, int nunit, int64_t rows, int tiles, const uint8_t* __restrict__ xprep,
-           float* __restrict__ y, QmvScratch scr) {
+    k_qmv1(const uint8_t* __restrict__ W, int nunit, int64_t rows, int tiles, int tile_mode,
+           const uint8_t* __restrict__ xprep, float* __restrict__ y, QmvScratch scr) {
   constexpr int SB = Q1Cfg::SB, TBB = Q1Cfg::TBB, XB = Q1Cfg::XB;
   constexpr int RING = NW * NS * SB;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -785,11 +785,21 @@ __global__ void __launch_bounds__(NW * 32, 1)
   const uint32_t bar_x = smem_u32(xs + nunit * XB);
   const uint32_t bar0 = bar_x + 8 + warp * NS * 8;
 
-  const int64_t P = (int64_t)tiles * nunit / 2;  // unit pairs
-  const int64_t GW = (int64_t)gridDim.x * NW, gw = (int64_t)blockIdx.x * NW + warp;
-  const int64_t pb = P * gw / GW, pe = P * (gw + 1) / GW;
-  const int npair = (int)(pe - pb);
-  const int64_t ub = 2 * pb;
+  // Work split: the CTA takes pairs [cb, ce) -- whole row tiles in tile
+  // mode, so no tile is shared between CTAs, else an even share of all
+  // pairs -- and warp w of the CTA the w-th of NW even parts of that range.
+  // Pair and unit indices fit in 32 bits (the host checks tiles * nunit
+  // < 2^24, so products with the grid size stay below 2^31); a 32-bit
+  // division is a short sequence, a 64-bit one a long subroutine.
+  const int P = tiles * nunit / 2;  // unit pairs
+  const int npt = nunit / 2;        // pairs per tile
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int cb = tile_mode ? tiles * cta / G * npt : P * cta / G;
+  const int ce = tile_mode ? tiles * (cta + 1) / G * npt : P * (cta + 1) / G;
+  const int PC = ce - cb;
+  const int pb = cb + PC * warp / NW, pe = cb + PC * (warp + 1) / NW;
+  const int npair = pe - pb;
+  const int ub = 2 * pb;
 
   for (int i = threadIdx.x; i < Q1Cfg::ZERO / 16; i += blockDim.x) ((uint4*)(smem + RING))[i] = make_uint4(0, 0, 0, 0);
   if (threadIdx.x == 0) mbar_init(bar_x, 1);
@@ -797,7 +807,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     for (int s = 0; s < NS; s++) mbar_init(bar0 + 8 * s, 1);
   mbar_fence_init();
   __syncthreads();
-  const uint8_t* wsrc = W + ub * TBB;  // units are contiguous in range order
+  const uint8_t* wsrc = W + (int64_t)ub * TBB;  // units are contiguous in range order
   const int pre = npair < NS ? npair : NS;
   if (lane == 0)
     for (int s = 0; s < pre; s++) {
@@ -824,9 +834,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
   float tg = 0.f, tg8 = 0.f;
   float p0a = 0.f, p0b = 0.f, p1a = 0.f, p1b = 0.f;
   bool has0 = false, has1 = false;
-  const int64_t c0T = ub / nunit;
-  int64_t cT = c0T;
-  int cU = (int)(ub - c0T * nunit);  // even
+  const int c0T = ub / nunit;
+  int cT = c0T;
+  int cU = ub - c0T * nunit;  // even
   const bool first_partial = cU != 0;
   uint32_t ph = 0;
 
@@ -901,7 +911,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
           p0b = b8;
           has0 = true;
         } else {
-          store_tile<EPI, 1>(y, rows, (int)cT, lane, a, b8, scr.tp);
+          store_tile<EPI, 1>(y, rows, cT, lane, a, b8, scr.tp);
         }
         tg = tg8 = 0.f;
         cU = 0;
@@ -910,8 +920,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
     }
     ph ^= 1u;
   }
-  int64_t T1 = cT;
-  if (cU != 0) {  // the range ends inside tile cT
+  const int T1 = cT;
+  if (cU != 0 && npair > 0) {  // the range ends inside tile cT
     const float a = red4(tg), b8 = red4(tg8);
     if (cT == c0T && first_partial) {
       p0a = a;
@@ -923,7 +933,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       has1 = true;
     }
   }
-  // ---- tiles shared between warps (same scheme as k_qmv_warp, in pairs) ----
+  // ---- tiles shared between warps of this CTA, then between CTAs ----
   __syncthreads();
   float* part = (float*)smem;  // [NW][2][64]
   part[(warp * 2 + 0) * 64 + lane] = p0a;
@@ -931,30 +941,31 @@ __global__ void __launch_bounds__(NW * 32, 1)
   part[(warp * 2 + 1) * 64 + lane] = p1a;
   part[(warp * 2 + 1) * 64 + 32 + lane] = p1b;
   __syncthreads();
-  const int64_t cw0 = (int64_t)blockIdx.x * NW;
-  const int64_t npt = nunit / 2;  // pairs per tile
+  auto warp_of = [&](int q) { return ((q - cb + 1) * NW - 1) / PC; };  // warp holding pair q
 #pragma unroll 1
   for (int sl = 0; sl < 2; sl++) {
     if (!(sl == 0 ? has0 : has1) || !ok) continue;
-    const int64_t T = sl == 0 ? c0T : T1;
-    const int64_t q0 = T * npt, q1 = q0 + npt;  // tile's pair range
-    const int64_t wf = ((q0 + 1) * GW - 1) / P, wl = (q1 * GW - 1) / P;
-    const int64_t jf = wf > cw0 ? wf : cw0, jl = wl < cw0 + NW - 1 ? wl : cw0 + NW - 1;
-    if (gw != jf) continue;
+    const int T = sl == 0 ? c0T : T1;
+    const int q0 = T * npt, q1 = q0 + npt;  // tile's pair range
+    const int lo = q0 > cb ? q0 : cb, hi = q1 < ce ? q1 : ce;  // its part in this CTA
+    const int jf = warp_of(lo), jl = warp_of(hi - 1);
+    if (warp != jf) continue;
     float a = 0.f, b8 = 0.f;
-    for (int64_t j = jf; j <= jl; j++) {
-      const int64_t fj = 2 * (P * j / GW);  // first unit of warp j
-      const int slot = (fj / nunit == T && fj % nunit != 0) ? 0 : 1;
-      a += part[((j - cw0) * 2 + slot) * 64 + lane];
-      b8 += part[((j - cw0) * 2 + slot) * 64 + 32 + lane];
+    const int u0 = T * nunit, u1 = u0 + nunit;  // tile's unit range
+    for (int j = jf; j <= jl; j++) {
+      const int fj = 2 * (cb + PC * j / NW);  // first unit of warp j
+      const int slot = (fj > u0 && fj < u1) ? 0 : 1;  // it starts inside T: partial 0
+      a += part[(j * 2 + slot) * 64 + lane];
+      b8 += part[(j * 2 + slot) * 64 + 32 + lane];
     }
-    if (wf >= cw0 && wl < cw0 + NW) {
-      store_tile<EPI, 1>(y, rows, (int)T, lane, a, b8, scr.tp);
+    if (q0 >= cb && q1 <= ce) {  // the whole tile is in this CTA
+      store_tile<EPI, 1>(y, rows, T, lane, a, b8, scr.tp);
       continue;
     }
-    const int64_t cf = wf / NW, cl = wl / NW;
-    const int ncon = (int)(cl - cf + 1), cslot = (int)(blockIdx.x - cf);
-    float* base = scr.split + T * scr.maxc * 64;
+    // pair p lies in CTA ((p + 1) G - 1) / P (even-share mode only)
+    const int cf = ((q0 + 1) * G - 1) / P, cl = (q1 * G - 1) / P;
+    const int ncon = cl - cf + 1, cslot = cta - cf;
+    float* base = scr.split + (int64_t)T * scr.maxc * 64;
     base[cslot * 64 + lane] = a;
     base[cslot * 64 + 32 + lane] = b8;
     __threadfence();
@@ -981,7 +992,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
             sb += vb[j];
           }
       }
-      store_tile<EPI, 1>(y, rows, (int)T, lane, sa, sb, scr.tp);
+      store_tile<EPI, 1>(y, rows, T, lane, sa, sb, scr.tp);
       if (lane == 0) scr.count[T] = 0;
     }
   }
@@ -1081,41 +1092,9 @@ int launch_warp_cfg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, fl
 }
 
 // 16 warps with the deepest ring (<= 4) that fits, else 8 warps.
-// Largest ring (NS <= NS0 stages) of NW warps within `SMALL_MAX` bytes of
-// shared memory, so that two CTAs -- this launch's and the next one's -- fit
-// on one SM; -1 if none does.
-constexpr int SMALL_MAX = 112 * 1024;
-template <int QT, int EPI, int B, int NW, int NS>
-int launch_fit(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y, const ScratchCap& scr,
-               int gridcap, bool pdl) {
-  if constexpr (NS < 2) {
-    return -1;
-  } else if constexpr (WarpCfg<QT, B, NW, NS>::SMEM <= SMALL_MAX) {
-    return launch_warp_cfg<QT, EPI, B, NW, NS>(s, w, xprep, y, scr, gridcap, pdl);
-  } else {
-    return launch_fit<QT, EPI, B, NW, NS - 1>(s, w, xprep, y, scr, gridcap, pdl);
-  }
-}
-
-inline int qmv_cfg() {
-  static int c = getenv("SI_QMV_CFG") ? atoi(getenv("SI_QMV_CFG")) : 0;
-  return c;
-}
-
 template <int QT, int EPI, int B>
 int launch_warp(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y,
                 const ScratchCap& scr, int sms, bool pdl) {
-  {
-    int r = -1;
-    switch (qmv_cfg()) {
-      case 1: r = launch_fit<QT, EPI, B, 8, 6>(s, w, xprep, y, scr, sms, pdl); break;
-      case 2: r = launch_fit<QT, EPI, B, 8, 6>(s, w, xprep, y, scr, 2 * sms, pdl); break;
-      case 3: r = launch_fit<QT, EPI, B, 4, 8>(s, w, xprep, y, scr, 2 * sms, pdl); break;
-      case 4: r = launch_fit<QT, EPI, B, 4, 8>(s, w, xprep, y, scr, sms, pdl); break;
-      default: break;
-    }
-    if (r >= 0) return r;
-  }
   if constexpr (WarpCfg<QT, B, 16, 4>::SMEM <= WARP_SMEM_MAX)
     return launch_warp_cfg<QT, EPI, B, 16, 4>(s, w, xprep, y, scr, sms, pdl);
   else if constexpr (WarpCfg<QT, B, 16, 3>::SMEM <= WARP_SMEM_MAX)
@@ -1146,7 +1125,7 @@ int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y
   const int64_t nunit = w->nblk;
   const int64_t P = w->tiles * nunit / 2;
   const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit);
-  if ((nunit & 1) || P < NW || smem > 227 * 1024) return -1;
+  if ((nunit & 1) || P < NW || smem > 227 * 1024 || w->tiles * nunit >= (1 << 24)) return -1;
   static uint64_t attr_set = 0;
   int dev = 0;
   SI_CUDA(cudaGetDevice(&dev));
@@ -1154,16 +1133,30 @@ int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y
     SI_CUDA(cudaFuncSetAttribute(k_qmv1<EPI, NW, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     attr_set |= 1ull << dev;
   }
-  const int64_t grid = std::min<int64_t>(P / NW, sms);
-  const int64_t minr = P / (grid * NW), npt = nunit / 2;
-  const int maxc = (int)((npt - 1 + minr - 1) / minr + 1);
-  if ((size_t)w->tiles * maxc * 64 * 4 > scr.split_bytes || w->tiles > scr.count_n) return -1;
+  // Tile mode gives every CTA whole row tiles: no partial sums cross CTAs,
+  // at the price of up to one tile of imbalance.  Even-share mode balances
+  // the pairs exactly but combines the tiles cut between CTAs through global
+  // memory (a fence and a counter round trip, ~3 us).  Pick the shorter
+  // estimate, streaming at an equal share of the HBM bandwidth per SM.
+  const int64_t tiles = w->tiles, npt = nunit / 2;
+  const double sm_bytes_us = 6.5e6 / sms;  // bytes per microsecond per SM
+  const int64_t g_tile = std::min<int64_t>(tiles, sms);
+  const double t_tile = (double)((tiles + g_tile - 1) / g_tile) * nunit * Q1Cfg::TBB / sm_bytes_us;
+  const int64_t g_even = std::min<int64_t>(P / NW, sms);
+  const double t_even = (double)tiles * nunit * Q1Cfg::TBB / (sm_bytes_us * g_even) + 3.0;
+  const int tile_mode = t_tile <= t_even ? 1 : 0;
+  const int64_t grid = tile_mode ? g_tile : g_even;
   QmvScratch q = scr.scr;
-  q.maxc = maxc;
+  q.maxc = 0;
+  if (!tile_mode) {
+    const int64_t minr = P / (grid * NW);
+    q.maxc = (int)((npt - 1 + minr - 1) / minr + 1);
+    if ((size_t)tiles * q.maxc * 64 * 4 > scr.split_bytes || tiles > scr.count_n) return -1;
+  }
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)grid), dim3(NW * 32), smem, pdl, attr);
-  SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv1<EPI, NW, NS>, (const uint8_t*)w->dev, (int)nunit, w->rows, (int)w->tiles,
-                             xprep, y, q));
+  SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv1<EPI, NW, NS>, (const uint8_t*)w->dev, (int)nunit, w->rows, (int)tiles,
+                             tile_mode, xprep, y, q));
   return SI_OK;
 }
 
