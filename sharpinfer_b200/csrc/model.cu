@@ -104,13 +104,35 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
   const float* x = logits + (int64_t)b * vocab;
   float bv = -INFINITY;
   int bi = -1;
-  for (int64_t i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = x[i];
+  auto consider = [&](float v, int i) {
     if (v > bv || (bi < 0 && v == bv)) {  // -inf candidates still record an index
       bv = v;
-      bi = (int)i;
+      bi = i;
+    }
+  };
+  // Each thread visits its indices in increasing order: 16-byte loads, eight
+  // in flight, then the scalar tail.
+  const int nt = blockDim.x;
+  const int n4 = (vocab % 4 == 0 && ((uintptr_t)x & 15) == 0) ? (int)(vocab / 4) : 0;
+  for (int j0 = threadIdx.x; j0 < n4; j0 += 8 * nt) {
+    float4 r[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int j = j0 + u * nt;
+      r[u] = j < n4 ? __ldcg((const float4*)x + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; u++) {
+      const int j = j0 + u * nt;
+      if (j < n4) {
+        consider(r[u].x, 4 * j);
+        consider(r[u].y, 4 * j + 1);
+        consider(r[u].z, 4 * j + 2);
+        consider(r[u].w, 4 * j + 3);
+      }
     }
   }
+  for (int i = 4 * n4 + threadIdx.x; i < (int)vocab; i += nt) consider(x[i], i);
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
     const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);

@@ -88,6 +88,8 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
   const int nunit = gridDim.x;
   const int tid = threadIdx.x, k = 256 * u + tid;
   pdl_launch();  // dependents may start their independent prologue now
+  // the norm weights are not written by any kernel of the step
+  const float nwk = ((mode == 1 || mode == SI_PREP_RMSNORM_TP) && k < K) ? nw[k] : 0.f;
   pdl_wait();
   const float* xb = x + (int64_t)b * ldx;
   float scale = 1.f;
@@ -157,13 +159,33 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
     if (k < K) {
       const float a = res(k);
       xout[(int64_t)b * K + k] = a;
-      v = __fmul_rn(__fmul_rn(a, scale), nw[k]);
+      v = __fmul_rn(__fmul_rn(a, scale), nwk);
     }
     __syncthreads();  // red is reused below
   }
+  float xk = 0.f;
   if (mode == 1) {
+    // sum of squares: 16-byte loads, four in flight (plus this thread's own
+    // element), in the same order in every CTA of the row
+    xk = k < K ? xb[k] : 0.f;
     float ss = 0.f;
-    for (int i = tid; i < K; i += 256) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
+    if ((K & 1023) == 0 && ((uintptr_t)xb & 15) == 0) {
+      for (int i0 = 0; i0 < K; i0 += 4096) {
+        float4 r[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          r[j] = i0 + 1024 * j < K ? ((const float4*)(xb + i0 + 1024 * j))[tid] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          ss = __fadd_rn(ss, __fmul_rn(r[j].x, r[j].x));
+          ss = __fadd_rn(ss, __fmul_rn(r[j].y, r[j].y));
+          ss = __fadd_rn(ss, __fmul_rn(r[j].z, r[j].z));
+          ss = __fadd_rn(ss, __fmul_rn(r[j].w, r[j].w));
+        }
+      }
+    } else {
+      for (int i = tid; i < K; i += 256) ss = __fadd_rn(ss, __fmul_rn(xb[i], xb[i]));
+    }
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
     __syncthreads();
@@ -173,7 +195,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
   }
   if (k < K && mode != 3 && mode != SI_PREP_RMSNORM_TP) {
     if (mode == 1) {
-      v = __fmul_rn(__fmul_rn(xb[k], scale), nw[k]);
+      v = __fmul_rn(__fmul_rn(xk, scale), nwk);
     } else if (mode == 2) {
       const float gte = xb[k];
       const float sl = __fdiv_rn(gte, __fadd_rn(1.0f, expf(-gte)));
@@ -758,9 +780,11 @@ struct Q1Cfg {
   static constexpr int US = 2, TBB = 2304, SB = US * TBB;  // bytes per ring stage
   static constexpr int XB = 132 * 8 + 16;                   // prepared bytes per column unit
   static constexpr int ZERO = 1024;                         // zero fragments: 8 groups x 128 B
-  static size_t smem(int NW, int NS, int nunit) {
-    return (size_t)NW * NS * SB + ZERO + (size_t)nunit * XB + (size_t)(NW * NS + 1) * 8;
+  // ring | zero fragments | activations | barriers | partial sums [NW][2][64] f32
+  __host__ __device__ static size_t part_off(int NW, int NS, int nunit) {
+    return ((size_t)NW * NS * SB + ZERO + (size_t)nunit * XB + (size_t)(NW * NS + 1) * 8 + 15) & ~(size_t)15;
   }
+  static size_t smem(int NW, int NS, int nunit) { return part_off(NW, NS, nunit) + (size_t)NW * 2 * 64 * 4; }
 };
 
 __device__ __forceinline__ float red4(float v) {
@@ -935,7 +959,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   }
   // ---- tiles shared between warps of this CTA, then between CTAs ----
   __syncthreads();
-  float* part = (float*)smem;  // [NW][2][64]
+  float* part = (float*)(smem + Q1Cfg::part_off(NW, NS, nunit));  // [NW][2][64], apart from the ring
   part[(warp * 2 + 0) * 64 + lane] = p0a;
   part[(warp * 2 + 0) * 64 + 32 + lane] = p0b;
   part[(warp * 2 + 1) * 64 + lane] = p1a;
