@@ -213,6 +213,10 @@ int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const 
                 const PrepTp* tpp = nullptr);
 int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
                const QmvBuffers& qb, bool pdl);
+// y (op)= W RmsNorm(x) nw for a single row x (batch 1); xprep is the fallback's
+// prepared-activation buffer.
+int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const float* nw, float eps, float* y,
+                   int epi, const QmvBuffers& qb, uint8_t* xprep, bool pdl);
 int launch_synth_blocks(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma,
                         int64_t blk0, int64_t nblocks, uint8_t* dst);
 int launch_synth_blocks_2d(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma, int64_t grow0,

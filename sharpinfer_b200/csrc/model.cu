@@ -520,11 +520,14 @@ int enqueue_step(si_model* m, int B) {
       const PrepTp pt = tp_consumer(m, l - 1, 1);
       SI_TRY(launch_prep(s, m->x2, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
                          m->x, m->xprep, true, &pt));
+    } else if (!tp && B == 1) {  // RmsNorm inside the matvec where the kernel allows
+      SI_TRY(launch_qmv_rms(s, m->wqkv[l], m->x, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, m->qkv, SI_EPI_STORE, qb,
+                            m->xprep, true));
     } else {
       SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
                          nullptr, m->xprep, true));
     }
-    SI_TRY(launch_qmv(s, m->wqkv[l], m->xprep, B, m->qkv, SI_EPI_STORE, qb, true));
+    if (tp || B > 1) SI_TRY(launch_qmv(s, m->wqkv[l], m->xprep, B, m->qkv, SI_EPI_STORE, qb, true));
     SI_TRY(enqueue_attention(m, l, m->qkv, nullptr, B, true));
     if (tp) {
       SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, nullptr, SI_EPI_TP, tp_producer(m, l, 0), true));
@@ -533,10 +536,15 @@ int enqueue_step(si_model* m, int B) {
                          m->x2, m->xprep, true, &pt));
     } else {
       SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
-      SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
-                         nullptr, m->xprep, true));
+      if (B > 1)
+        SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
+                           nullptr, m->xprep, true));
     }
-    SI_TRY(launch_qmv(s, m->wgu[l], m->xprep, B, m->gu, SI_EPI_STORE, qb, true));
+    if (!tp && B == 1)
+      SI_TRY(launch_qmv_rms(s, m->wgu[l], m->x, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, m->gu, SI_EPI_STORE, qb,
+                            m->xprep, true));
+    else
+      SI_TRY(launch_qmv(s, m->wgu[l], m->xprep, B, m->gu, SI_EPI_STORE, qb, true));
     SI_TRY(launch_prep(s, m->gu, 2 * inter, m->gu + inter, nullptr, 0.f, SI_PREP_SILU_MUL, inter, B, nullptr,
                        m->xprep, true));
     if (tp) SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, nullptr, SI_EPI_TP, tp_producer(m, l, 1), true));

@@ -51,6 +51,17 @@ __device__ __forceinline__ uint32_t pack2(__half a, __half b) {
   return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
 }
 
+// Sum of the 32 values of Q4_K sub-block lane / 4 of a 256-value unit in
+// shared memory, returned in the four lanes 4j .. 4j + 3 of sub-block j: each
+// lane adds 8 consecutive values, then the four partial sums are combined.
+// The order is fixed, so every kernel that prepares a unit gets the same sums.
+__device__ __forceinline__ float subblock_sum(const float* sv, int lane) {
+  const float4 a = *(const float4*)(sv + 8 * lane), b = *(const float4*)(sv + 8 * lane + 4);
+  float p = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
+  p += __shfl_xor_sync(0xFFFFFFFFu, p, 1);
+  return p + __shfl_xor_sync(0xFFFFFFFFu, p, 2);
+}
+
 // Byte offset of MMA group mg, unit u in the prepared-activation buffer.
 // A unit of a group with LW lanes is 132*LW + 16 bytes: fragments, Q4_K
 // sub-block sums, then the 4 inverse activation scales of the group.
@@ -80,7 +91,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
                                               const float* __restrict__ nw, float eps, int mode,
                                               int K, int B, float* __restrict__ xout,
                                               uint8_t* __restrict__ xprep, PrepTp tpp) {
-  __shared__ float sv[256];
+  __shared__ __align__(16) float sv[256];
   __shared__ float red[8];
   __shared__ float mw[2][SI_ATTN_MAX_SPLITS + 1];  // mode 3: merge weights of the unit's two heads
   const int u = blockIdx.x, b = blockIdx.y, mg = b >> 2, cb = b & 3;
@@ -233,16 +244,18 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
       w[2 * h + 1] = pack2(split_part(v2, part), split_part(v3, part));
     }
     *(uint4*)(unit + (jj * LW + L) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-  } else if (tid < 72) {  // Q4_K sub-block sums (X_{2t}, X_{2t+1}) * 2^-5
-    const int part = (tid >> 2) & 1, t = tid & 3;
-    const int L = 8 * cb + 4 * part + t;
-    float X0 = 0.f, X1 = 0.f;
-    for (int i = 0; i < 32; i++) X0 += sv[64 * t + i];
-    for (int i = 0; i < 32; i++) X1 += sv[64 * t + 32 + i];
-    const float s5 = s * 0.03125f;
-    *(uint32_t*)(unit + 8 * LW * 16 + L * 4) = pack2(split_part(X0 * s5, part), split_part(X1 * s5, part));
-  } else if (tid == 72) {
-    *(float*)(unit + 132 * LW + 4 * cb) = ldexpf(1.0f, -e);
+  } else if (tid < 96) {  // warp 2: Q4_K sub-block sums (X_{2t}, X_{2t+1}) * 2^-5, and the scale
+    const int lane = tid & 31;
+    const float S = subblock_sum(sv, lane);
+    const int part = (lane >> 2) & 1, t = lane & 3;
+    const float X0 = __shfl_sync(0xFFFFFFFFu, S, 8 * t), X1 = __shfl_sync(0xFFFFFFFFu, S, 8 * t + 4);
+    if (lane < 8) {
+      const int L = 8 * cb + 4 * part + t;
+      const float s5 = s * 0.03125f;
+      *(uint32_t*)(unit + 8 * LW * 16 + L * 4) = pack2(split_part(X0 * s5, part), split_part(X1 * s5, part));
+    } else if (lane == 8) {
+      *(float*)(unit + 132 * LW + 4 * cb) = ldexpf(1.0f, -e);
+    }
   }
   __syncthreads();
 }
@@ -784,8 +797,98 @@ struct Q1Cfg {
   __host__ __device__ static size_t part_off(int NW, int NS, int nunit) {
     return ((size_t)NW * NS * SB + ZERO + (size_t)nunit * XB + (size_t)(NW * NS + 1) * 8 + 15) & ~(size_t)15;
   }
-  static size_t smem(int NW, int NS, int nunit) { return part_off(NW, NS, nunit) + (size_t)NW * 2 * 64 * 4; }
+  // ... | f32 [nunit * 256] staging of a fused RmsNorm
+  __host__ __device__ static size_t stage_off(int NW, int NS, int nunit) {
+    return part_off(NW, NS, nunit) + (size_t)NW * 2 * 64 * 4;
+  }
+  static size_t smem(int NW, int NS, int nunit, bool fused) {
+    return stage_off(NW, NS, nunit) + (fused ? (size_t)nunit * 256 * 4 : 0);
+  }
 };
+
+// Fused RmsNorm + activation preparation of a batch-1 k_qmv1 launch: every
+// CTA normalises the whole input x (K <= 8192 columns, 4 x 16-byte loads per
+// thread; nwv holds this thread's norm weights, read before the dependency
+// wait) and packs its prepared units into shared memory exactly as k_prep
+// mode 1 does (TensorOps.RmsNorm, TensorOps.cs:135-145: scale = 1 /
+// sqrtf(ss / n + eps), out = (x * scale) * w).  The sum of squares is taken
+// in the same order by every CTA.
+template <int NW>
+__device__ __forceinline__ void q1_rms_prep(const float* __restrict__ xf, const float4 (&nwv)[4], float eps, int nunit,
+                                            float* red, float* stage, uint8_t* xs) {
+  constexpr int XB = Q1Cfg::XB;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = nunit * 256;
+  float4 xv[4];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int i = 4 * tid + NW * 128 * j;
+    xv[j] = i < K ? __ldcg((const float4*)(xf + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    ss = __fadd_rn(ss, __fmul_rn(xv[j].x, xv[j].x));
+    ss = __fadd_rn(ss, __fmul_rn(xv[j].y, xv[j].y));
+    ss = __fadd_rn(ss, __fmul_rn(xv[j].z, xv[j].z));
+    ss = __fadd_rn(ss, __fmul_rn(xv[j].w, xv[j].w));
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; w++) tot += red[w];
+  const float scale = 1.0f / sqrtf(tot / (float)K + eps);
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int i = 4 * tid + NW * 128 * j;
+    if (i < K)
+      *(float4*)(stage + i) = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), nwv[j].x),
+                                          __fmul_rn(__fmul_rn(xv[j].y, scale), nwv[j].y),
+                                          __fmul_rn(__fmul_rn(xv[j].z, scale), nwv[j].z),
+                                          __fmul_rn(__fmul_rn(xv[j].w, scale), nwv[j].w));
+  }
+  __syncthreads();
+  for (int u = warp; u < nunit; u += NW) {  // one warp per 256-column unit
+    const float* sv = stage + 256 * u;
+    float amax = 0.f;
+    for (int i = lane; i < 256; i += 32) amax = fmaxf(amax, fabsf(sv[i]));
+    amax = warp_max(amax);
+    int e = 0;
+    if (amax > 0.f && amax <= 3.0e38f) {
+      int E;
+      frexpf(amax, &E);
+      e = 14 - E;
+      e = e < -100 ? -100 : (e > 100 ? 100 : e);
+    }
+    const float sc = ldexpf(1.0f, e);
+    uint8_t* unit = xs + u * XB;
+#pragma unroll
+    for (int r = 0; r < 2; r++) {  // fragments: 8 groups x (hi, lo) x 4 lanes
+      const int task = lane + 32 * r, jj = task >> 3, part = (task >> 2) & 1, t = task & 3;
+      uint32_t w[4];
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int base = 32 * jj + 16 * h + 2 * t;
+        const float v0 = sv[base] * sc, v1 = sv[base + 1] * sc, v2 = sv[base + 8] * sc, v3 = sv[base + 9] * sc;
+        w[2 * h] = pack2(split_part(v0, part), split_part(v1, part));
+        w[2 * h + 1] = pack2(split_part(v2, part), split_part(v3, part));
+      }
+      *(uint4*)(unit + (jj * 8 + 4 * part + t) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    {  // Q4_K sub-block sums (X_{2t}, X_{2t+1}) * 2^-5
+      const float S = subblock_sum(sv, lane);
+      const int part = (lane >> 2) & 1, t = lane & 3;
+      const float X0 = __shfl_sync(0xFFFFFFFFu, S, 8 * t), X1 = __shfl_sync(0xFFFFFFFFu, S, 8 * t + 4);
+      const float s5 = sc * 0.03125f;
+      if (lane < 8)
+        *(uint32_t*)(unit + 8 * 8 * 16 + (4 * part + t) * 4) = pack2(split_part(X0 * s5, part), split_part(X1 * s5, part));
+      else if (lane == 8)
+        *(float*)(unit + 132 * 8) = ldexpf(1.0f, -e);
+    }
+  }
+  __syncthreads();
+}
 
 __device__ __forceinline__ float red4(float v) {
   v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
@@ -798,7 +901,8 @@ __device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float
 template <int EPI, int NW, int NS>
 __global__ void __launch_bounds__(NW * 32, 1)
     k_qmv1(const uint8_t* __restrict__ W, int nunit, int64_t rows, int tiles, int tile_mode,
-           const uint8_t* __restrict__ xprep, float* __restrict__ y, QmvScratch scr) {
+           const uint8_t* __restrict__ xprep, const float* __restrict__ xf, const float* __restrict__ nw, float eps,
+           float* __restrict__ y, QmvScratch scr) {
   constexpr int SB = Q1Cfg::SB, TBB = Q1Cfg::TBB, XB = Q1Cfg::XB;
   constexpr int RING = NW * NS * SB;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -832,20 +936,44 @@ __global__ void __launch_bounds__(NW * 32, 1)
   mbar_fence_init();
   __syncthreads();
   const uint8_t* wsrc = W + (int64_t)ub * TBB;  // units are contiguous in range order
+  // One ring stage per warp is requested before the dependency wait, the
+  // rest once the activations are in: requests queued ahead of the
+  // activation loads delay them (the loads wait behind up to one stage per
+  // warp of weight bytes instead of the whole ring).
   const int pre = npair < NS ? npair : NS;
+  if (lane == 0 && pre > 0) {
+    mbar_arrive_expect_tx(bar0, SB);
+    bulk_g2s(smem_u32(ring), wsrc, SB, bar0);
+  }
+  pdl_launch();  // dependents may start their independent prologue now
+  // xf != nullptr: the input is f32 x, normalised here (RmsNorm with weights
+  // nw); else xprep holds the prepared units
+  float4 nwv[4];
+  if (xf) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {  // norm weights: not written by any kernel of the step
+      const int i = 4 * (int)threadIdx.x + NW * 128 * j;
+      nwv[j] = i < nunit * 256 ? *(const float4*)(nw + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  pdl_wait();
+  bool ok = true;
+  if (xf) {
+    q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)),
+                    (float*)(smem + Q1Cfg::stage_off(NW, NS, nunit)), (uint8_t*)xs);
+  } else {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(bar_x, (uint32_t)(nunit * XB));
+      bulk_g2s(smem_u32(xs), xprep, (uint32_t)(nunit * XB), bar_x);
+    }
+    ok = mbar_wait_bounded(bar_x, 0);
+    if (!ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
+  }
   if (lane == 0)
-    for (int s = 0; s < pre; s++) {
+    for (int s = 1; s < pre; s++) {
       mbar_arrive_expect_tx(bar0 + 8 * s, SB);
       bulk_g2s(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s);
     }
-  pdl_launch();  // dependents may start their independent prologue now
-  pdl_wait();
-  if (threadIdx.x == 0) {
-    mbar_arrive_expect_tx(bar_x, (uint32_t)(nunit * XB));
-    bulk_g2s(smem_u32(xs), xprep, (uint32_t)(nunit * XB), bar_x);
-  }
-  bool ok = mbar_wait_bounded(bar_x, 0);
-  if (!ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
 
   // per-lane constants
   const int cls = lane >> 3;                                   // MMA column class
@@ -1144,11 +1272,13 @@ int launch_reg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
 // keep resident in shared memory).
 template <int EPI>
 int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y, const ScratchCap& scr, int sms,
-              bool pdl) {
+              bool pdl, const float* xf = nullptr, const float* nw = nullptr, float eps = 0.f) {
   constexpr int NW = 16, NS = 2;
   const int64_t nunit = w->nblk;
   const int64_t P = w->tiles * nunit / 2;
-  const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit);
+  if (xf && (nunit * 256 > NW * 128 * 4 || (((uintptr_t)xf | (uintptr_t)nw) & 15)))
+    return -1;  // the fused RmsNorm holds K <= 8192 in registers, read 16 bytes at a time
+  const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit, xf != nullptr);
   if ((nunit & 1) || P < NW || smem > 227 * 1024 || w->tiles * nunit >= (1 << 24)) return -1;
   static uint64_t attr_set = 0;
   int dev = 0;
@@ -1180,7 +1310,7 @@ int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)grid), dim3(NW * 32), smem, pdl, attr);
   SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv1<EPI, NW, NS>, (const uint8_t*)w->dev, (int)nunit, w->rows, (int)tiles,
-                             tile_mode, xprep, y, q));
+                             tile_mode, xprep, xf, nw, eps, y, q));
   return SI_OK;
 }
 
@@ -1237,6 +1367,20 @@ int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const 
   SI_CUDA(cudaLaunchKernelEx(&cfg, k_prep, x, ldx, x2, norm_w, eps, mode, K, B, xout, xprep,
                              tpp ? *tpp : PrepTp{}));
   return SI_OK;
+}
+
+// y (op)= W RmsNorm(x) nw for one row x: the batch-1 Q4_K kernel normalises
+// and prepares x itself; other weights go through k_prep into xprep first.
+int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const float* nw, float eps, float* y,
+                   int epi, const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
+  if (w->qtype == SI_Q4_K && (epi == SI_EPI_STORE || epi == SI_EPI_ADD)) {
+    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp}, qb.split_bytes, qb.count_n};
+    const int r = epi == SI_EPI_ADD ? launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, x, nw, eps)
+                                    : launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, x, nw, eps);
+    if (r >= 0) return r;
+  }
+  SI_TRY(launch_prep(s, x, (int)w->cols, nullptr, nw, eps, SI_PREP_RMSNORM, (int)w->cols, 1, nullptr, xprep, pdl));
+  return launch_qmv(s, w, xprep, 1, y, epi, qb, pdl);
 }
 
 int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
