@@ -26,48 +26,17 @@
 // no load sits on the critical path of the MMAs.  Batch 5..16 reads the
 // weights and activations straight from global memory.
 #include "common.cuh"
+#include "prepfmt.cuh"
 
 namespace si {
 namespace {
 
 constexpr int QMV_WARPS = 8;
-constexpr int XUNIT_LANES_FULL = 32;
-
 __device__ __forceinline__ float h2f_lo(uint32_t w) {
   return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFF)));
 }
 __device__ __forceinline__ float h2f_hi(uint32_t w) {
   return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
-}
-
-// Split v into f16 hi + lo; part 0 -> hi, 1 -> lo.
-__device__ __forceinline__ __half split_part(float v, int part) {
-  __half hi = __float2half_rn(v);
-  if (part == 0) return hi;
-  return __float2half_rn(v - __half2float(hi));
-}
-
-__device__ __forceinline__ uint32_t pack2(__half a, __half b) {
-  return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
-}
-
-// Sum of the 32 values of Q4_K sub-block lane / 4 of a 256-value unit in
-// shared memory, returned in the four lanes 4j .. 4j + 3 of sub-block j: each
-// lane adds 8 consecutive values, then the four partial sums are combined.
-// The order is fixed, so every kernel that prepares a unit gets the same sums.
-__device__ __forceinline__ float subblock_sum(const float* sv, int lane) {
-  const float4 a = *(const float4*)(sv + 8 * lane), b = *(const float4*)(sv + 8 * lane + 4);
-  float p = ((a.x + a.y) + (a.z + a.w)) + ((b.x + b.y) + (b.z + b.w));
-  p += __shfl_xor_sync(0xFFFFFFFFu, p, 1);
-  return p + __shfl_xor_sync(0xFFFFFFFFu, p, 2);
-}
-
-// Byte offset of MMA group mg, unit u in the prepared-activation buffer.
-// A unit of a group with LW lanes is 132*LW + 16 bytes: fragments, Q4_K
-// sub-block sums, then the 4 inverse activation scales of the group.
-__device__ __forceinline__ int xunit_bytes(int LW) { return 132 * LW + 16; }
-__device__ __forceinline__ int64_t xprep_off(int mg, int nunit, int u, int LW) {
-  return (int64_t)mg * nunit * xunit_bytes(XUNIT_LANES_FULL) + (int64_t)u * xunit_bytes(LW);
 }
 
 // ---------------------------------------------------------------------------
@@ -223,13 +192,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
   __syncthreads();
   amax = 0.f;
   for (int i = 0; i < 8; i++) amax = fmaxf(amax, red[i]);
-  int e = 0;
-  if (amax > 0.f && amax <= 3.0e38f) {
-    int E;
-    frexpf(amax, &E);  // amax < 2^E
-    e = 14 - E;
-    e = e < -100 ? -100 : (e > 100 ? 100 : e);
-  }
+  const int e = unit_exponent(amax);
   const float s = ldexpf(1.0f, e);
   uint8_t* unit = xprep + xprep_off(mg, nunit, u, LW);
   if (tid < 64) {  // fragments: 8 groups x (hi, lo) x 4 lanes
@@ -849,44 +812,8 @@ __device__ __forceinline__ void q1_rms_prep(const float* __restrict__ xf, const 
                                           __fmul_rn(__fmul_rn(xv[j].w, scale), nwv[j].w));
   }
   __syncthreads();
-  for (int u = warp; u < nunit; u += NW) {  // one warp per 256-column unit
-    const float* sv = stage + 256 * u;
-    float amax = 0.f;
-    for (int i = lane; i < 256; i += 32) amax = fmaxf(amax, fabsf(sv[i]));
-    amax = warp_max(amax);
-    int e = 0;
-    if (amax > 0.f && amax <= 3.0e38f) {
-      int E;
-      frexpf(amax, &E);
-      e = 14 - E;
-      e = e < -100 ? -100 : (e > 100 ? 100 : e);
-    }
-    const float sc = ldexpf(1.0f, e);
-    uint8_t* unit = xs + u * XB;
-#pragma unroll
-    for (int r = 0; r < 2; r++) {  // fragments: 8 groups x (hi, lo) x 4 lanes
-      const int task = lane + 32 * r, jj = task >> 3, part = (task >> 2) & 1, t = task & 3;
-      uint32_t w[4];
-#pragma unroll
-      for (int h = 0; h < 2; h++) {
-        const int base = 32 * jj + 16 * h + 2 * t;
-        const float v0 = sv[base] * sc, v1 = sv[base + 1] * sc, v2 = sv[base + 8] * sc, v3 = sv[base + 9] * sc;
-        w[2 * h] = pack2(split_part(v0, part), split_part(v1, part));
-        w[2 * h + 1] = pack2(split_part(v2, part), split_part(v3, part));
-      }
-      *(uint4*)(unit + (jj * 8 + 4 * part + t) * 16) = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    {  // Q4_K sub-block sums (X_{2t}, X_{2t+1}) * 2^-5
-      const float S = subblock_sum(sv, lane);
-      const int part = (lane >> 2) & 1, t = lane & 3;
-      const float X0 = __shfl_sync(0xFFFFFFFFu, S, 8 * t), X1 = __shfl_sync(0xFFFFFFFFu, S, 8 * t + 4);
-      const float s5 = sc * 0.03125f;
-      if (lane < 8)
-        *(uint32_t*)(unit + 8 * 8 * 16 + (4 * part + t) * 4) = pack2(split_part(X0 * s5, part), split_part(X1 * s5, part));
-      else if (lane == 8)
-        *(float*)(unit + 132 * 8) = ldexpf(1.0f, -e);
-    }
-  }
+  for (int u = warp; u < nunit; u += NW)  // one warp per 256-column unit
+    pack_unit_warp(stage + 256 * u, xs + u * XB, 8, 0, lane);
   __syncthreads();
 }
 

@@ -79,7 +79,7 @@ def run_parity(ctx, cfg, kv_len, steps, start_tokens):
     return worst
 
 
-@pytest.mark.parametrize("G", [2, 4, 8])
+@pytest.mark.parametrize("G", [1, 2, 4, 8])  # G = 1: the splits are merged by k_prep, else in the kernel
 def test_decode_steps_match_oracle(ctx, G):
     worst = run_parity(ctx, small_cfg(G), kv_len=100, steps=5, start_tokens=[5, 777])
     assert worst < 2e-5, worst
