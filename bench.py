@@ -18,8 +18,10 @@ roofline: the dominant kernel, the fused gate/up Q4_K matvec (28672 x 4096,
 step's bytes per token against the same peak are reported beside it.
 --impl reference times the reference's CPU path -- the oracle restatement of
 SharpInfer's managed forward pass over the same weights -- on the host cores.
-Under torchrun the N ranks decode the one sequence tensor-parallel (TP = N,
-partial sums exchanged in peer memory); value is that sequence's tokens/s.
+Under torchrun (N > 1) the workload is the Llama-3-70B architecture in the
+same Q4_K_M form, f16 KV prefilled to 8192 positions: the N ranks decode the
+one sequence tensor-parallel (TP = N, partial sums exchanged in peer memory)
+and value is that sequence's tokens/s.  --model 70b runs it on one GPU too.
 """
 import argparse
 import json
@@ -38,7 +40,8 @@ sys.path.insert(0, ROOT)
 SEED = 20261201
 KV_LEN = 4096
 START_TOKEN = 128000
-METRIC = "decode tok/s (Llama-3-8B Q4_K_M, ctx 4096, batch 1)"
+KV_LEN_70B = 8192
+METRIC = "decode tok/s + Q4_K matvec HBM GB/s (8B Q4_K_M 1 GPU; 70B TP at 2/4/8)"
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up k_qmv1 launch
 # (28672 x 4096 Q4_K, batch 1) from an ncu --set full capture of
 # `bench.py --layers 2` (summary under profiles/): the algorithmic bytes,
@@ -119,19 +122,53 @@ def dist_setup():
 
 
 def model_cfg(args):
-    from sharpinfer_b200.model import config, llama3_8b
-    c = llama3_8b(max_seq=args.ctx + 2 * (args.steps + args.warmup) + 8, max_batch=1)
-    if args.layers != c.n_layers:
+    from sharpinfer_b200.model import config, llama3_8b, llama3_70b
+    make = llama3_70b if args.model == "70b" else llama3_8b
+    c = make(max_seq=args.ctx + 2 * (args.steps + args.warmup) + 8, max_batch=1)
+    if args.layers and args.layers != c.n_layers:
         c = config(args.layers, c.hidden, c.intermediate, c.n_heads, c.n_kv_heads, c.vocab, c.max_seq, 1)
     return c
 
 
-def workload_name(args):
-    name = "decode8b: Llama-3-8B arch (32 layers, hidden 4096, 32/8 heads, FFN 14336, vocab 128256) Q4_K_M, " \
-           "f16 KV prefilled to %d, batch 1, greedy" % args.ctx
-    if args.layers != 32:
-        name = name.replace("32 layers", "%d of its 32 layers" % args.layers)
+def workload_name(args, world=1):
+    if args.model == "70b":
+        name = "decode70b: Llama-3-70B arch (80 layers, hidden 8192, 64/8 heads, FFN 28672, vocab 128256) " \
+               "Q4_K_M, f16 KV prefilled to %d, batch 1, greedy, tensor parallel over %d GPU(s)" % (args.ctx, world)
+        full = 80
+    else:
+        name = "decode8b: Llama-3-8B arch (32 layers, hidden 4096, 32/8 heads, FFN 14336, vocab 128256) Q4_K_M, " \
+               "f16 KV prefilled to %d, batch 1, greedy" % args.ctx
+        full = 32
+        if world > 1:
+            name += ", tensor parallel over %d GPUs" % world
+    if args.layers and args.layers != full:
+        name = name.replace("%d layers" % full, "%d of its %d layers" % (args.layers, full))
     return name
+
+
+def cpu_decode_sampled(cfg, ctx_len, max_seconds):
+    """A model too large for a whole CPU decode (70B: 280 GB as f32): the
+    oracle decodes the same model cut to 1 and to 2 layers, and a token of
+    the full model is extrapolated as t1 + (L - 1) (t2 - t1)."""
+    from sharpinfer_b200.model import config
+    L = cfg.n_layers
+    cut = [config(n, cfg.hidden, cfg.intermediate, cfg.n_heads, cfg.n_kv_heads, cfg.vocab, cfg.max_seq, 1)
+           for n in (1, 2)]
+    r1 = cpu_decode(cut[0], ctx_len, 8, 1, max_seconds=max_seconds / 2)
+    r2 = cpu_decode(cut[1], ctx_len, 8, 1, max_seconds=max_seconds / 2)
+    t1, t2 = r1["ms_per_step"], r2["ms_per_step"]
+    t = t1 + (L - 1) * max(t2 - t1, 0.0)
+    return {"value": 1e3 / t, "unit": "tok/s", "cores": r1["cores"], "kind": "port", "tokens": r1["tokens"] + r2["tokens"],
+            "ms_per_step": t, "build_s": r1["build_s"] + r2["build_s"],
+            "sample": "oracle decode of the same model cut to 1 layer (%d steps, %.1f ms/token) and 2 layers (%d steps, "
+                      "%.1f ms/token) at ctx %d, %d threads; a %d-layer token extrapolated as t1 + %d (t2 - t1)"
+                      % (r1["tokens"], t1, r2["tokens"], t2, ctx_len, r1["cores"], L, L - 1)}
+
+
+def cpu_sample(cfg, ctx_len, seconds):
+    if cfg.n_layers > 32:
+        return cpu_decode_sampled(cfg, ctx_len, seconds)
+    return cpu_decode(cfg, ctx_len, 100, 1, max_seconds=seconds)
 
 
 def cpu_decode(cfg, ctx_len, ntokens, warmup, max_seconds=None):
@@ -156,20 +193,24 @@ def cpu_decode(cfg, ctx_len, ntokens, warmup, max_seconds=None):
     threads = oracle.nthreads()
     return {"value": n / dt, "unit": "tok/s", "cores": threads, "kind": "port", "tokens": n,
             "ms_per_step": dt / n * 1e3, "build_s": build_s,
-            "sample": "%d greedy decode steps of the same 8B Q4_K_M model at ctx %d (weights dequantised row by row, "
-                      "f32 arithmetic of TensorOps, KV values rounded through f16), %d threads" % (n, ctx_len, threads)}
+            "sample": "%d greedy decode steps of the same %d-layer Q4_K_M model at ctx %d (weights dequantised row by "
+                      "row, f32 arithmetic of TensorOps, KV values rounded through f16), %d threads"
+                      % (n, cfg.n_layers, ctx_len, threads)}
 
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
     cfg = model_cfg(args)
-    r = cpu_decode(cfg, args.ctx, args.steps, min(args.warmup, 2), max_seconds=args.ref_seconds)
+    if cfg.n_layers > 32:
+        r = cpu_decode_sampled(cfg, args.ctx, args.ref_seconds)
+    else:
+        r = cpu_decode(cfg, args.ctx, args.steps, min(args.warmup, 2), max_seconds=args.ref_seconds)
     line = {"metric": METRIC, "value": round(r["value"], 4), "unit": "tok/s", "n_gpus": args.gpus,
             "steps": r["tokens"], "warmup": min(args.warmup, 2), "ms_per_step": round(r["ms_per_step"], 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded Q4_K_M weights, f16-exact KV prefix)", "impl": "reference",
-            "config": {"workload": workload_name(args), "seq_len": args.ctx, "parallelism": "cpu"},
+            "config": {"workload": workload_name(args, world), "seq_len": args.ctx, "parallelism": "cpu"},
             "cpu_baseline": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()
                              if k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(r["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -177,25 +218,27 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def matvec_roofline(ctx, torch, dev, reps=40):
-    """Average duration of the fused gate/up Q4_K matvec (28672 x 4096) over
-    `reps` launches on 4 rotating weight copies (264 MB > L2), captured in one
-    CUDA graph so that host launch overhead does not enter the timing."""
+def matvec_roofline(ctx, torch, dev, rows=2 * 14336, cols=4096, reps=40):
+    """Average duration of the fused gate/up Q4_K matvec (rows x cols; 28672 x
+    4096 for the 8B model) over `reps` launches on rotating weight copies
+    (together > 250 MB, twice the L2), captured in one CUDA graph so that host
+    launch overhead does not enter the timing."""
     from sharpinfer_b200 import native as N
     from sharpinfer_b200.backend import synth_f32_host
-    rows, cols = 2 * 14336, 4096
-    ws = [ctx.synth_weight(N.SI_Q4_K, rows, cols, SEED + i, 77, N.SYNTH_MODEL, 1.0 / (23.3 * 64.0)) for i in range(4)]
+    ncopy = max(4, -(-250_000_000 // q4k_bytes(rows, cols)))
+    ws = [ctx.synth_weight(N.SI_Q4_K, rows, cols, SEED + i, 77, N.SYNTH_MODEL, 1.0 / (23.3 * 64.0))
+          for i in range(ncopy)]
     x = torch.from_numpy(synth_f32_host(cols, SEED, 78)).to(dev).reshape(1, -1)
     y = torch.empty((1, rows), device=dev)
     ctx.act_prepare(x)
     for i in range(8):
-        ctx.qmatvec_prepared(ws[i % 4], 1, out=y)
+        ctx.qmatvec_prepared(ws[i % ncopy], 1, out=y)
     s = ctx.torch_stream
     ctx.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
         for i in range(reps):
-            ctx.qmatvec_prepared(ws[i % 4], 1, out=y)
+            ctx.qmatvec_prepared(ws[i % ncopy], 1, out=y)
     g.replay()
     ctx.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -373,7 +416,9 @@ def run_ours(args, world, rank, local):
         pos += 1
     e2e_ms = (time.perf_counter() - w0) * 1e3 / args.steps
     kernels_per_step = m.step_kernels(1)
-    kern_ms, kern_bytes = matvec_roofline(ctx, torch, dev)
+    # the dominant kernel: this rank's fused gate/up matvec
+    gu_rows, gu_cols = 2 * cfg.intermediate // world, cfg.hidden
+    kern_ms, kern_bytes = matvec_roofline(ctx, torch, dev, gu_rows, gu_cols)
     t = torch.tensor([ms, e2e_ms, kern_ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -382,19 +427,21 @@ def run_ours(args, world, rank, local):
         peak, peak_kind = measured_peaks()
         achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
         tb = token_bytes(cfg, args.ctx + args.warmup + args.steps // 2)
-        traffic = GATEUP_TRAFFIC
+        # ncu measured the 8B shape (no re-reads); other shapes: the same bytes per unit
+        traffic = GATEUP_TRAFFIC if (gu_rows, gu_cols) == (28672, 4096) else int(kern_bytes)
         line = {
             "metric": METRIC, "value": round(1e3 / ms, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None,
             "dtype": "q4_k/q6_k weights x f32 activations (f16 hi/lo MMA, f32 accumulate), f16 KV",
             "data": "synthetic (seeded Q4_K_M weights and f16 KV prefix; no checkpoint offline)",
-            "config": {"workload": workload_name(args),
+            "config": {"workload": workload_name(args, world),
                        "global_batch": 1, "seq_len": args.ctx, "parallelism": "tp%d" % world if world > 1 else "single",
                        "l2": "inputs larger than L2 (%.2f GB streamed per step)" % (tb / 1e9)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": "k_qmv1 (batch-1 Q4_K), fused gate/up 28672x4096 (66 MB)",
+                         "kernel": "k_qmv1 (batch-1 Q4_K), fused gate/up %dx%d (%.1f MB)" % (gu_rows, gu_cols,
+                                                                                          kern_bytes / 1e6),
                          "peak_source": peak_kind + " (burst copy)"},
             "decode_roofline": {"bytes_per_token": tb, "achieved_gbs": round(tb / (ms * 1e-3) / 1e9, 1),
                                 "frac": round(tb / (ms * 1e-3) / 1e9 / (peak * world), 4)},
@@ -405,7 +452,7 @@ def run_ours(args, world, rank, local):
             "tokens_head": [int(v) for v in gen[:8, 0]],
         }
         if not args.no_cpu_baseline:
-            cb = cpu_decode(cfg, args.ctx, 100, 1, max_seconds=args.cpu_seconds)
+            cb = cpu_sample(cfg, args.ctx, args.cpu_seconds)
             line["cpu_baseline"] = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in cb.items()
                                     if k in ("value", "unit", "cores", "kind", "sample")}
         print(json.dumps(line), flush=True)
@@ -431,13 +478,19 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--layers", type=int, default=32, help="transformer layers (32 = the full 8B model)")
-    ap.add_argument("--ctx", type=int, default=KV_LEN, help="prefilled KV positions")
+    ap.add_argument("--model", default=None, choices=["8b", "70b"],
+                    help="decode model (default: 8b on one GPU, 70b tensor parallel on several)")
+    ap.add_argument("--layers", type=int, default=0, help="transformer layers (0: the whole model)")
+    ap.add_argument("--ctx", type=int, default=0, help="prefilled KV positions (0: 4096 for 8b, 8192 for 70b)")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
     ap.add_argument("--prefill-m", type=int, default=2048, help="tokens of the prefill GEMM workload")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     world, rank, local = dist_setup()
+    if args.model is None:
+        args.model = "70b" if world > 1 else "8b"
+    if not args.ctx:
+        args.ctx = KV_LEN_70B if args.model == "70b" else KV_LEN
     if args.impl == "reference":
         run_reference(args, world, rank)
     elif args.workload == "prefill":

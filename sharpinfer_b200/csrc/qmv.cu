@@ -115,20 +115,44 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
   }
   if (mode == SI_PREP_RMSNORM_TP) {
     // residual + the tp partial sums, added in rank order (identical on every
-    // rank); each partial-sum element is awaited through its tag
+    // rank); each partial-sum element is awaited through its tag.  Eight
+    // elements per thread are in flight at a time: their words are loaded
+    // together and only a word whose tag is not there yet is polled.
     const unsigned want = *tpp.epoch * (unsigned)tpp.nlayers2 + (unsigned)tpp.flag_add;
-    auto res = [&](int i) {
-      float a = xb[i];
-      for (int r = 0; r < tpp.tp; r++) {
-        const uint2* sl = (const uint2*)(tpp.comm + tpp.slots_off + r * tpp.src_stride) + (int64_t)b * tpp.ld + i;
-        a = __fadd_rn(a, __uint_as_float(wait_tagged(sl, want, tpp.err)));
+    const int nper = (K + 255) / 256;  // elements of this thread: tid + 256 m
+    float ss = 0.f, own = 0.f;
+    for (int m0 = 0; m0 < nper; m0 += 8) {
+      float a[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int i = tid + 256 * (m0 + j);
+        a[j] = (m0 + j < nper && i < K) ? xb[i] : 0.f;
       }
-      return a;
-    };
-    float ss = 0.f;
-    for (int i = tid; i < K; i += 256) {
-      const float a = res(i);
-      ss = __fadd_rn(ss, __fmul_rn(a, a));
+      for (int r = 0; r < tpp.tp; r++) {
+        const uint2* sl = (const uint2*)(tpp.comm + tpp.slots_off + r * tpp.src_stride) + (int64_t)b * tpp.ld;
+        uint2 w[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const int i = tid + 256 * (m0 + j);
+          w[j] = (m0 + j < nper && i < K) ? ld_tagged(sl + i) : make_uint2(0u, want);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const int i = tid + 256 * (m0 + j);
+          if (m0 + j < nper && i < K) {
+            const uint32_t bits = (int)(w[j].y - want) >= 0 ? w[j].x : wait_tagged(sl + i, want, tpp.err);
+            a[j] = __fadd_rn(a[j], __uint_as_float(bits));
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int i = tid + 256 * (m0 + j);
+        if (m0 + j < nper && i < K) {
+          ss = __fadd_rn(ss, __fmul_rn(a[j], a[j]));
+          if (m0 + j == u) own = a[j];
+        }
+      }
     }
     ss = warp_sum(ss);
     if ((tid & 31) == 0) red[tid >> 5] = ss;
@@ -137,9 +161,8 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
     for (int i = 0; i < 8; i++) t += red[i];
     scale = 1.0f / sqrtf(t / (float)K + eps);
     if (k < K) {
-      const float a = res(k);
-      xout[(int64_t)b * K + k] = a;
-      v = __fmul_rn(__fmul_rn(a, scale), nwk);
+      xout[(int64_t)b * K + k] = own;
+      v = __fmul_rn(__fmul_rn(own, scale), nwk);
     }
     __syncthreads();  // red is reused below
   }
