@@ -79,15 +79,23 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
     const int warp = tid >> 5, lane = tid & 31;
     if (warp < 2 && 2 * u + warp < nhd) {  // statistics of head 2u + warp
       const float2* ml = (const float2*)x2 + ((int64_t)b * nhd + 2 * u + warp) * S;
+      float2 pv[(SI_ATTN_MAX_SPLITS + 32) / 32];  // all of this lane's (max, sum) pairs in one round trip
+#pragma unroll
+      for (int j = 0; j < (SI_ATTN_MAX_SPLITS + 32) / 32; j++)
+        pv[j] = lane + 32 * j < S ? ml[lane + 32 * j] : make_float2(-INFINITY, 0.f);
       float M = -INFINITY;
-      for (int s = lane; s < S; s += 32) M = fmaxf(M, ml[s].x);
+#pragma unroll
+      for (int j = 0; j < (SI_ATTN_MAX_SPLITS + 32) / 32; j++) M = fmaxf(M, pv[j].x);
       M = warp_max(M);
       float den = 0.f;
-      for (int s = lane; s < S; s += 32) {
-        const float2 p = ml[s];
-        const float w = p.x == -INFINITY ? 0.f : expf(p.x - M);
-        mw[warp][s] = w;
-        den = fmaf(w, p.y, den);
+#pragma unroll
+      for (int j = 0; j < (SI_ATTN_MAX_SPLITS + 32) / 32; j++) {
+        const int s = lane + 32 * j;
+        if (s < S) {
+          const float w = pv[j].x == -INFINITY ? 0.f : expf(pv[j].x - M);
+          mw[warp][s] = w;
+          den = fmaf(w, pv[j].y, den);
+        }
       }
       den = warp_sum(den);
       if (lane == 0) mw[warp][SI_ATTN_MAX_SPLITS] = 1.0f / den;
@@ -98,13 +106,13 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
       const float* po = x + ((int64_t)b * nhd + h) * S * 128 + d;
       const float* wh = mw[hl];
       float n0 = 0.f, n1 = 0.f;
-      for (int s0 = 0; s0 < S; s0 += 16) {
-        float o[16];
+      for (int s0 = 0; s0 < S; s0 += 32) {  // 32 partial outputs in flight
+        float o[32];
 #pragma unroll
-        for (int j = 0; j < 16; j++)
+        for (int j = 0; j < 32; j++)
           if (s0 + j < S) o[j] = po[(int64_t)(s0 + j) * 128];
 #pragma unroll
-        for (int j = 0; j < 16; j += 2) {
+        for (int j = 0; j < 32; j += 2) {
           if (s0 + j < S) n0 = fmaf(wh[s0 + j], o[j], n0);
           if (s0 + j + 1 < S) n1 = fmaf(wh[s0 + j + 1], o[j + 1], n1);
         }
@@ -779,18 +787,23 @@ struct Q1Cfg {
   static constexpr int US = 2, TBB = 2304, SB = US * TBB;  // bytes per ring stage
   static constexpr int XB = 132 * 8 + 16;                   // prepared bytes per column unit
   static constexpr int ZERO = 1024;                         // zero fragments: 8 groups x 128 B
-  // ring | zero fragments | activations | barriers | partial sums [NW][2][64] f32
-  __host__ __device__ static size_t part_off(int NW, int NS, int nunit) {
+  // ring | zero fragments | activations | barriers | f32 [64] reduction |
+  // partial sums [NW][2][64] f32 after the main loop, sharing their space with
+  // the f32 staging (nunit * 256) of a fused RmsNorm before it
+  __host__ __device__ static size_t red_off(int NW, int NS, int nunit) {
     return ((size_t)NW * NS * SB + ZERO + (size_t)nunit * XB + (size_t)(NW * NS + 1) * 8 + 15) & ~(size_t)15;
   }
-  // ... | f32 [nunit * 256] staging of a fused RmsNorm
-  __host__ __device__ static size_t stage_off(int NW, int NS, int nunit) {
-    return part_off(NW, NS, nunit) + (size_t)NW * 2 * 64 * 4;
-  }
-  static size_t smem(int NW, int NS, int nunit, bool fused) {
-    return stage_off(NW, NS, nunit) + (fused ? (size_t)nunit * 256 * 4 : 0);
+  __host__ __device__ static size_t part_off(int NW, int NS, int nunit) { return red_off(NW, NS, nunit) + 256; }
+  static size_t smem(int NW, int NS, int nunit, int pmode) {
+    const size_t part = (size_t)NW * 2 * 64 * 4;
+    const size_t stage = pmode == 1 ? (size_t)nunit * 256 * 4 : 0;
+    return part_off(NW, NS, nunit) + (part > stage ? part : stage);
   }
 };
+
+// Input preparation of a k_qmv1 launch: 0 = prepared units copied from
+// xprep, 1 = RmsNorm of x (q1_rms_prep).
+enum { Q1_PREPARED = 0, Q1_RMSNORM = 1 };
 
 // Fused RmsNorm + activation preparation of a batch-1 k_qmv1 launch: every
 // CTA normalises the whole input x (K <= 8192 columns, 4 x 16-byte loads per
@@ -851,8 +864,8 @@ __device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float
 template <int EPI, int NW, int NS>
 __global__ void __launch_bounds__(NW * 32, 1)
     k_qmv1(const uint8_t* __restrict__ W, int nunit, int64_t rows, int tiles, int tile_mode,
-           const uint8_t* __restrict__ xprep, const float* __restrict__ xf, const float* __restrict__ nw, float eps,
-           float* __restrict__ y, QmvScratch scr) {
+           int pmode, const uint8_t* __restrict__ xprep, const float* __restrict__ xf, const float* __restrict__ nw,
+           float eps, float* __restrict__ y, QmvScratch scr) {
   constexpr int SB = Q1Cfg::SB, TBB = Q1Cfg::TBB, XB = Q1Cfg::XB;
   constexpr int RING = NW * NS * SB;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -896,10 +909,10 @@ __global__ void __launch_bounds__(NW * 32, 1)
     bulk_g2s(smem_u32(ring), wsrc, SB, bar0);
   }
   pdl_launch();  // dependents may start their independent prologue now
-  // xf != nullptr: the input is f32 x, normalised here (RmsNorm with weights
-  // nw); else xprep holds the prepared units
+  // pmode: prepared units in xprep, or the f32 input xf normalised here
+  // with weights nw
   float4 nwv[4];
-  if (xf) {
+  if (pmode == Q1_RMSNORM) {
 #pragma unroll
     for (int j = 0; j < 4; j++) {  // norm weights: not written by any kernel of the step
       const int i = 4 * (int)threadIdx.x + NW * 128 * j;
@@ -908,9 +921,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
   }
   pdl_wait();
   bool ok = true;
-  if (xf) {
-    q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)),
-                    (float*)(smem + Q1Cfg::stage_off(NW, NS, nunit)), (uint8_t*)xs);
+  if (pmode != Q1_PREPARED) {
+    q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
+                    (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
   } else {
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(bar_x, (uint32_t)(nunit * XB));
@@ -1222,13 +1235,14 @@ int launch_reg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
 // keep resident in shared memory).
 template <int EPI>
 int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y, const ScratchCap& scr, int sms,
-              bool pdl, const float* xf = nullptr, const float* nw = nullptr, float eps = 0.f) {
+              bool pdl, int pmode = Q1_PREPARED, const float* xf = nullptr, const float* nw = nullptr,
+              float eps = 0.f) {
   constexpr int NW = 16, NS = 2;
   const int64_t nunit = w->nblk;
   const int64_t P = w->tiles * nunit / 2;
-  if (xf && (nunit * 256 > NW * 128 * 4 || (((uintptr_t)xf | (uintptr_t)nw) & 15)))
-    return -1;  // the fused RmsNorm holds K <= 8192 in registers, read 16 bytes at a time
-  const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit, xf != nullptr);
+  // the fused RmsNorm holds K <= 8192 in registers, read 16 bytes at a time
+  if (pmode == Q1_RMSNORM && (nunit * 256 > NW * 128 * 4 || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
+  const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit, pmode);
   if ((nunit & 1) || P < NW || smem > 227 * 1024 || w->tiles * nunit >= (1 << 24)) return -1;
   static uint64_t attr_set = 0;
   int dev = 0;
@@ -1260,7 +1274,7 @@ int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)grid), dim3(NW * 32), smem, pdl, attr);
   SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv1<EPI, NW, NS>, (const uint8_t*)w->dev, (int)nunit, w->rows, (int)tiles,
-                             tile_mode, xprep, xf, nw, eps, y, q));
+                             tile_mode, pmode, xprep, xf, nw, eps, y, q));
   return SI_OK;
 }
 
@@ -1325,8 +1339,9 @@ int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const flo
                    int epi, const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
   if (w->qtype == SI_Q4_K && (epi == SI_EPI_STORE || epi == SI_EPI_ADD)) {
     const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp}, qb.split_bytes, qb.count_n};
-    const int r = epi == SI_EPI_ADD ? launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, x, nw, eps)
-                                    : launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, x, nw, eps);
+    const int r = epi == SI_EPI_ADD
+                      ? launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM, x, nw, eps)
+                      : launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM, x, nw, eps);
     if (r >= 0) return r;
   }
   SI_TRY(launch_prep(s, x, (int)w->cols, nullptr, nw, eps, SI_PREP_RMSNORM, (int)w->cols, 1, nullptr, xprep, pdl));
