@@ -253,6 +253,105 @@ def matvec_roofline(ctx, torch, dev, rows=2 * 14336, cols=4096, reps=40):
     return ms, q4k_bytes(rows, cols) + 4 * (cols + rows)
 
 
+def q8_bytes(rows, cols):
+    return rows * (cols // 32) * 34
+
+
+# (name, qtype, rows, cols): the single 4096 x 4096 Q4_K matvec and the 8B
+# layer set -- fused gate/up and down Q4_K, Q6_K lm_head, Q8_0 4096 x 4096
+MATVEC_SHAPES = (("q4k_4096x4096", 12, 4096, 4096), ("q4k_gateup_28672x4096", 12, 28672, 4096),
+                 ("q4k_down_4096x14336", 12, 4096, 14336), ("q6k_lmhead_128256x4096", 14, 128256, 4096),
+                 ("q8_0_4096x4096", 8, 4096, 4096))
+
+
+def run_matvec(args):
+    """The matvec set at batch 1, 4 and 16: microseconds per call of si_qmatvec
+    (activation preparation + matvec) and of the matvec alone on prepared
+    activations, each averaged over 40 launches in a CUDA graph on rotating
+    weight copies (together > 250 MB, twice the L2); GB/s of the algorithmic
+    bytes (weights + f32 x and y) against the measured HBM peak."""
+    import torch
+    from sharpinfer_b200 import B200Context, native as N
+    from sharpinfer_b200.backend import synth_f32_host
+    dev = torch.device("cuda", 0)
+    ctx = B200Context(0)
+    torch.cuda.set_stream(ctx.torch_stream)
+    s = ctx.torch_stream
+    peak, peak_kind = measured_peaks()
+    wbytes = {12: q4k_bytes, 14: q6k_bytes, 8: q8_bytes}
+    rows_out = []
+
+    def graph_us(fn, reps=40):
+        for _ in range(3):
+            fn(0)
+        ctx.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps):
+                fn(i)
+        g.replay()
+        ctx.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+        ctx.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        del g
+        return us
+
+    clocks = ClockSampler(0)
+    clocks.start()
+    for name, qt, rows, cols in MATVEC_SHAPES:
+        wb = wbytes[qt](rows, cols)
+        ncopy = max(2, -(-250_000_000 // wb))
+        ws = [ctx.synth_weight(qt, rows, cols, SEED + i, 90 + qt, N.SYNTH_PLAIN, 0.01) for i in range(ncopy)]
+        for B in (1, 4, 16):
+            x = torch.from_numpy(synth_f32_host(B * cols, SEED, 91)).to(dev).reshape(B, cols)
+            y = torch.empty((B, rows), device=dev)
+            nbytes = wb + 4 * B * (rows + cols)
+            us_op = graph_us(lambda i: ctx.qmatvec(ws[i % ncopy], x, out=y))
+            ctx.act_prepare(x)
+            us_k = graph_us(lambda i: ctx.qmatvec_prepared(ws[i % ncopy], B, out=y))
+            rows_out.append({"shape": name, "batch": B, "bytes": nbytes, "us_call": round(us_op, 2),
+                             "us_kernel": round(us_k, 2), "gbs_call": round(nbytes / us_op / 1e3, 1),
+                             "gbs_kernel": round(nbytes / us_k / 1e3, 1),
+                             "frac_kernel": round(nbytes / us_k / 1e3 / peak, 4)})
+            del x, y
+        for w in ws:
+            w.free()
+    clk = clocks.stop()
+    # e2e: the host-buffer call (x copied in, y copied out, synchronous) on the 4096 x 4096 Q4_K weight
+    w = ctx.synth_weight(12, 4096, 4096, SEED, 92, N.SYNTH_PLAIN, 0.01)
+    xh = synth_f32_host(4096, SEED, 93).reshape(1, 4096)
+    for _ in range(5):
+        ctx.qmatvec_host(w, xh)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        ctx.qmatvec_host(w, xh)
+    e2e_us = (time.perf_counter() - t0) * 1e6 / args.steps
+    w.free()
+    c1 = next(r for r in rows_out if r["shape"] == "q4k_4096x4096" and r["batch"] == 1)
+    gu = next(r for r in rows_out if r["shape"] == "q4k_gateup_28672x4096" and r["batch"] == 1)
+    line = {"metric": METRIC, "value": c1["gbs_call"], "unit": "GB/s", "n_gpus": 1, "steps": 40,
+            "warmup": 3, "ms_per_step": round(c1["us_call"] / 1e3, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "q4_k/q6_k/q8_0 weights x f32 activations (f16 hi/lo MMA, f32 accumulate)",
+            "data": "synthetic (seeded quant blocks, x ~ N(0, 1))",
+            "config": {"workload": "matvec: 4096x4096 Q4_K and the 8B layer set at batch 1/4/16",
+                       "l2": "rotating weight copies, > 250 MB per shape"},
+            "shapes": rows_out,
+            "roofline": {"bound": "hbm", "achieved": gu["gbs_kernel"], "peak": peak, "unit": "GB/s",
+                         "frac": gu["frac_kernel"], "traffic": GATEUP_TRAFFIC,
+                         "kernel": "k_qmv1, fused gate/up 28672x4096, batch 1", "peak_source": peak_kind},
+            "e2e": {"value": round((4096 * 16 * 144 + 8 * 4096) / e2e_us / 1e3, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": 4 * 4096, "d2h_bytes_per_step": 4 * 4096},
+            "gpu_launches": 3 * 40 * len(rows_out), "clocks": clk}
+    print(json.dumps(line), flush=True)
+    ctx.synchronize()
+    torch.cuda.set_stream(torch.cuda.default_stream(dev))
+    ctx.close()
+
+
 PREFILL_SHAPES = ((4096, 4096), (14336, 4096), (4096, 14336))  # (N rows, K cols): q/o, gate/up, down
 
 
@@ -482,7 +581,7 @@ def main():
                     help="decode model (default: 8b on one GPU, 70b tensor parallel on several)")
     ap.add_argument("--layers", type=int, default=0, help="transformer layers (0: the whole model)")
     ap.add_argument("--ctx", type=int, default=0, help="prefilled KV positions (0: 4096 for 8b, 8192 for 70b)")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "matvec"])
     ap.add_argument("--prefill-m", type=int, default=2048, help="tokens of the prefill GEMM workload")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -496,6 +595,9 @@ def main():
     elif args.workload == "prefill":
         if rank == 0:
             run_prefill(args, world, rank, local)
+    elif args.workload == "matvec":
+        if rank == 0:
+            run_matvec(args)
     else:
         run_ours(args, world, rank, local)
 
