@@ -442,7 +442,7 @@ def run_prefill(args, world, rank, local):
             "config": {"workload": "prefill%d: M=%d x (N,K) in %s, Q4_K weights" % (M, M, list(PREFILL_SHAPES)),
                        "l2": "weights and activations per shape > L2 (HBM-resident)"},
             "shapes": rows,
-            "attention": {"kernel": "k_attn_prefill (mma.sync bf16, causal, 32/8 heads, d 128)", "seq": M,
+            "attention": {"kernel": "k_attn_fa_tc (tcgen05, S and O in TMEM; causal, 32/8 heads, d 128)", "seq": M,
                           "us": round(att_ms * 1e3, 1), "tflops": round(att_flops / att_ms / 1e9, 1)},
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(ach / peak, 4), "traffic": None,
