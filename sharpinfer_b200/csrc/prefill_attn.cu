@@ -246,9 +246,11 @@ __global__ void __launch_bounds__(128) k_attn_prefill(const __nv_bfloat16* __res
 
 // ---------------------------------------------------------------------------
 // tcgen05 flash attention.  One CTA = 128 queries (M) of one head, key tiles
-// of 64 (N).  Warp 0: TMA (Q once, K and V^T tiles through a 4-stage ring);
-// warp 1: tcgen05.mma issuer; warps 2-5: softmax, one query row per thread
-// (TMEM lanes 32 (warp % 4) .. + 31).  Per key tile j:
+// of 64 (N).  Warp 0: TMA (Q once, K and V^T tiles through a 3-stage ring);
+// warp 1: tcgen05.mma issuer; warps 2-9: softmax, two threads per query row
+// (TMEM lanes 32 (warp % 4) .. + 31), warps 2-5 on key columns 0-31 and
+// output dims 0-63, warps 6-9 on the other halves; the two exchange their
+// row maxima through shared memory.  Per key tile j:
 //   S_j = Q K_j^T            (M 128, N 64, K 128: 8 MMAs) -> TMEM S[j % 2]
 //   softmax: masked row max, p = exp(s - m), running sum, P_j written to
 //            shared memory as bf16 hi + lo in the K-major 128-byte-swizzled
@@ -258,17 +260,19 @@ __global__ void __launch_bounds__(128) k_attn_prefill(const __nv_bfloat16* __res
 // S_{j+1} is issued before O_j, so the softmax of tile j overlaps it.  V is
 // used transposed (V^T [d][keys], made by k_vt) so that both operands of
 // every MMA are K-major.  All waits are bounded.
-constexpr int FA_BQ = 128, FA_BK = 64, FA_NST = 4;
+constexpr int FA_BQ = 128, FA_BK = 64, FA_NST = 3;
 constexpr int FA_QB = FA_BQ * 256;  // Q: two 64-dim chunks of [128 rows][128 B]
 constexpr int FA_KB = FA_BK * 256;  // K tile: two chunks of [64 keys][128 B]
 constexpr int FA_VB = 128 * 128;    // V^T tile: [128 dims][64 keys * 2 B]
 constexpr int FA_PB = FA_BQ * 128;  // P (hi or lo): [128 rows][64 keys * 2 B]
-constexpr int FA_SMEM = 1024 + FA_QB + FA_NST * (FA_KB + FA_VB) + 4 * FA_PB + 256;
+constexpr int FA_XCH = 3 * 256 * 4;  // row maxima [2 tiles][2 halves][128] and row sums [2][128]
+constexpr int FA_SMEM = 1024 + FA_QB + FA_NST * (FA_KB + FA_VB) + 4 * FA_PB + 256 + FA_XCH;
+constexpr int FA_THREADS = 320;  // TMA warp, MMA warp, 8 softmax warps
 // kind::f16 instruction descriptors: D f32, A and B bf16, both K-major
 constexpr uint32_t FA_IDESC_S = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
 constexpr uint32_t FA_IDESC_O = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
 
-__global__ void __launch_bounds__(192, 1) k_attn_fa_tc(const __grid_constant__ CUtensorMap tmQ,
+__global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_constant__ CUtensorMap tmQ,
                                                        const __grid_constant__ CUtensorMap tmK,
                                                        const __grid_constant__ CUtensorMap tmV, float* __restrict__ O,
                                                        int Hq, int Hkv, int S, int KV, float scale, int causal,
@@ -277,6 +281,7 @@ __global__ void __launch_bounds__(192, 1) k_attn_fa_tc(const __grid_constant__ C
   const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = base, sK = sQ + FA_QB, sV = sK + FA_NST * FA_KB, sP = sV + FA_NST * FA_VB;
   const uint32_t bars = sP + 4 * FA_PB;
+  float* xch = (float*)(smem_raw + (bars + 256 - smem_u32(smem_raw)));  // [3][256] f32
   // barriers: kv_full[NST] kv_empty[NST] s_full[2] s_free[2] p_full[2] o_full[2] o_free[2] q_full, TMEM slot
   const uint32_t kv_full = bars, kv_empty = bars + 8 * FA_NST, s_full = bars + 16 * FA_NST, s_free = s_full + 16,
                  p_full = s_full + 32, o_full = s_full + 48, o_free = s_full + 64, q_full = s_full + 80,
@@ -293,10 +298,10 @@ __global__ void __launch_bounds__(192, 1) k_attn_fa_tc(const __grid_constant__ C
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(s_full + 8 * i, 1);
-      mbar_init(s_free + 8 * i, 128);
-      mbar_init(p_full + 8 * i, 128);
+      mbar_init(s_free + 8 * i, 256);
+      mbar_init(p_full + 8 * i, 256);
       mbar_init(o_full + 8 * i, 1);
-      mbar_init(o_free + 8 * i, 128);
+      mbar_init(o_free + 8 * i, 256);
     }
     mbar_init(q_full, 1);
     mbar_fence_init();
@@ -365,76 +370,77 @@ __global__ void __launch_bounds__(192, 1) k_attn_fa_tc(const __grid_constant__ C
       }
       if (!ok) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
     }
-  } else {  // softmax: thread = query row r of the tile
-    const int qq = warp & 3, r = 32 * qq + lane, qrow = q0 + r;
+  } else {  // softmax: two threads per query row r of the tile
+    const int qq = warp & 3, half = (warp - 2) >> 2, r = 32 * qq + lane, qrow = q0 + r;
     const uint32_t lanes = (uint32_t)(32 * qq) << 16;
-    float oacc[128];
+    float oacc[64];  // output dims 64 half .. + 63
 #pragma unroll
-    for (int i = 0; i < 128; i++) oacc[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;  // m in base-2 units
+    for (int i = 0; i < 64; i++) oacc[i] = 0.f;
+    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;  // m in base-2 units; l over this thread's keys
     const float sc2 = scale * 1.4426950408889634f;  // scale * log2(e)
     for (int j = 0; j < nt; j++) {
       const int pb = j & 1;
       if (ok && !mbar_wait_bounded(s_full + 8 * pb, (uint32_t)((j / 2) & 1))) ok = false;
       tc_fence_after();
-      float sv[64];
+      float sv[32];
       {
         uint32_t r32[32];
-        tmem_ld32(tmem + lanes + 64 * pb, r32);
+        tmem_ld32(tmem + lanes + 64 * pb + 32 * half, r32);
 #pragma unroll
         for (int i = 0; i < 32; i++) sv[i] = __uint_as_float(r32[i]);
-        tmem_ld32(tmem + lanes + 64 * pb + 32, r32);
-#pragma unroll
-        for (int i = 0; i < 32; i++) sv[32 + i] = __uint_as_float(r32[i]);
       }
       tc_fence_before();
       mbar_arrive(s_free + 8 * pb);
       // mask, running max (FlashAttention.cs:206-224, 238-325), in base-2
       // units: t = s * scale * log2(e), p = 2^(t - max t) = e^(s scale - max)
-      const int k0 = j * FA_BK;
-      const bool full = k0 + FA_BK <= KV && (!causal || k0 + FA_BK - 1 <= q0 + start_pos);  // no key masked
+      const int k0 = j * FA_BK + 32 * half;
+      const bool full = k0 + 32 <= KV && (!causal || k0 + 31 <= q0 + start_pos);  // no key masked
       float mx = -INFINITY;
       if (full) {
 #pragma unroll
-        for (int i = 0; i < 64; i++) {
+        for (int i = 0; i < 32; i++) {
           sv[i] *= sc2;
           mx = fmaxf(mx, sv[i]);
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 64; i++) {
+        for (int i = 0; i < 32; i++) {
           const int key = k0 + i;
           const float v = (key >= KV || (causal && key > qrow + start_pos)) ? -INFINITY : sv[i] * sc2;
           sv[i] = v;
           mx = fmaxf(mx, v);
         }
       }
+      xch[pb * 256 + half * 128 + r] = mx;  // the row maximum needs both halves
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      mx = fmaxf(mx, xch[pb * 256 + (half ^ 1) * 128 + r]);
       const float mn = fmaxf(m, mx);
       const float alpha = mn == -INFINITY ? 1.f : exp2f(m - mn);
       float ps = 0.f;
       if (mn != -INFINITY) {
 #pragma unroll
-        for (int i = 0; i < 64; i++) {
+        for (int i = 0; i < 32; i++) {
           const float p = exp2f(sv[i] - mn);  // 2^-inf = 0 for masked keys
           sv[i] = p;
           ps += p;
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 64; i++) sv[i] = 0.f;
+        for (int i = 0; i < 32; i++) sv[i] = 0.f;
       }
       l = l * alpha + ps;
       m = mn;
-      // P_{j-2} has been read once O_{j-1} is complete (the MMAs finish in order)
-      if (ok && j >= 1 && !mbar_wait_bounded(o_full + 8 * ((j - 1) & 1), (uint32_t)(((j - 1) / 2) & 1))) ok = false;
-      {  // P_j as bf16 hi + lo: row r, 8 chunks of 8 keys, chunk g at (g ^ (r % 8)) * 16 in the 128-byte row
+      // P_j goes to the buffer P_{j-2} used; that product was complete when
+      // O_{j-2} was added in the previous iteration
+      {  // P_j as bf16 hi + lo: row r, chunks of 8 keys, chunk g at (g ^ (r % 8)) * 16 in the 128-byte row
         const uint32_t ph = sP + pb * 2 * FA_PB + r * 128;
 #pragma unroll
-        for (int g = 0; g < 8; g++) {
+        for (int gg = 0; gg < 4; gg++) {
+          const int g = 4 * half + gg;
           uint32_t hi[4], lo[4];
 #pragma unroll
           for (int e = 0; e < 4; e++) {
-            const float a0 = sv[8 * g + 2 * e], a1 = sv[8 * g + 2 * e + 1];
+            const float a0 = sv[8 * gg + 2 * e], a1 = sv[8 * gg + 2 * e + 1];
             const __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
             const float2 hf = __bfloat1622float2(h);
             const __nv_bfloat162 lw = __floats2bfloat162_rn(a0 - hf.x, a1 - hf.y);
@@ -453,10 +459,11 @@ __global__ void __launch_bounds__(192, 1) k_attn_fa_tc(const __grid_constant__ C
       fence_proxy_async_smem();
       mbar_arrive(p_full + 8 * pb);
       if (j >= 1) {  // O += rescaled O_{j-1}
+        if (ok && !mbar_wait_bounded(o_full + 8 * ((j - 1) & 1), (uint32_t)(((j - 1) / 2) & 1))) ok = false;
         tc_fence_after();
-        const uint32_t ob = tmem + lanes + 128 + 128 * ((j - 1) & 1);
+        const uint32_t ob = tmem + lanes + 128 + 128 * ((j - 1) & 1) + 64 * half;
 #pragma unroll
-        for (int c = 0; c < 4; c++) {
+        for (int c = 0; c < 2; c++) {
           uint32_t t32[32];
           tmem_ld32(ob + 32 * c, t32);
 #pragma unroll
@@ -471,21 +478,24 @@ __global__ void __launch_bounds__(192, 1) k_attn_fa_tc(const __grid_constant__ C
       const int j = nt - 1;
       if (ok && !mbar_wait_bounded(o_full + 8 * (j & 1), (uint32_t)((j / 2) & 1))) ok = false;
       tc_fence_after();
-      const uint32_t ob = tmem + lanes + 128 + 128 * (j & 1);
+      const uint32_t ob = tmem + lanes + 128 + 128 * (j & 1) + 64 * half;
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
+      for (int c = 0; c < 2; c++) {
         uint32_t t32[32];
         tmem_ld32(ob + 32 * c, t32);
 #pragma unroll
         for (int i = 0; i < 32; i++) oacc[32 * c + i] = fmaf(oacc[32 * c + i], alpha_prev, __uint_as_float(t32[i]));
       }
     }
+    xch[512 + half * 128 + r] = l;  // the row sum adds both halves' keys
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    const float lr = l + xch[512 + (half ^ 1) * 128 + r];
     if (!ok && lane == 0) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
     if (qrow < S) {  // a row without a visible key is 0 (FlashAttention.cs:155-163)
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      float4* orow = (float4*)(O + (((int64_t)b * Hq + h) * S + qrow) * PA_D);
+      const float inv = lr > 0.f ? 1.0f / lr : 0.f;
+      float4* orow = (float4*)(O + (((int64_t)b * Hq + h) * S + qrow) * PA_D + 64 * half);
 #pragma unroll
-      for (int i = 0; i < 32; i++)
+      for (int i = 0; i < 16; i++)
         orow[i] = make_float4(oacc[4 * i] * inv, oacc[4 * i + 1] * inv, oacc[4 * i + 2] * inv, oacc[4 * i + 3] * inv);
     }
   }
@@ -563,7 +573,7 @@ extern "C" SI_EXPORT int si_attn_prefill(si_ctx* c, const uint16_t* q, const uin
       fa_attr |= 1ull << c->device;
     }
     dim3 grid((unsigned)((seq + FA_BQ - 1) / FA_BQ), (unsigned)heads, (unsigned)batch);
-    k_attn_fa_tc<<<grid, 192, FA_SMEM, c->stream>>>(tq, tk, tv, o, heads, kv_heads, seq, kv, scale, causal,
+    k_attn_fa_tc<<<grid, FA_THREADS, FA_SMEM, c->stream>>>(tq, tk, tv, o, heads, kv_heads, seq, kv, scale, causal,
                                                     start_pos, c->dev_err);
     SI_CUDA(cudaGetLastError());
     return SI_OK;
