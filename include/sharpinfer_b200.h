@@ -166,9 +166,10 @@ SI_EXPORT int si_qgemm(si_ctx* ctx, const si_weight* w, const uint16_t* x_bf16_d
  * (src/SharpInfer.Core/Layers/FlashAttention.cs:59-167) for bf16 q [batch][heads][seq][128],
  * k, v [batch][kv_heads][kv][128] (grouped-query: head h reads kv head
  * h / (heads / kv_heads)), f32 o [batch][heads][seq][128], all device
- * pointers (16-byte aligned).  causal != 0 lets query i see keys
- * j <= i + start_pos; a query with no visible key gets 0.  Asynchronous on
- * the context stream. */
+ * pointers (16-byte aligned; k and v may be NULL when kv = 0).  causal != 0
+ * lets query i see keys j <= i + start_pos; a query with no visible key gets
+ * 0.  Runs on tcgen05 with S and O in tensor memory; v is transposed into
+ * context scratch first.  Asynchronous on the context stream. */
 SI_EXPORT int si_attn_prefill(si_ctx* ctx, const uint16_t* q_bf16, const uint16_t* k_bf16, const uint16_t* v_bf16,
                               float* o, int batch, int heads, int kv_heads, int seq, int kv, int head_dim, float scale,
                               int causal, int start_pos);

@@ -23,7 +23,9 @@ def bf16(a):
     (2, 4, 2, 130, 130, True),    # ragged tiles
     (1, 2, 2, 70, 200, True),     # cached prefix: start_pos = KV - S
     (1, 8, 2, 96, 33, False),     # non-causal, KV < one tile
-    (1, 2, 1, 256, 256, True),
+    (1, 2, 1, 256, 256, True),    # key tiles wrap the 3-stage ring
+    (1, 4, 1, 200, 520, True),    # two query blocks over 9 key tiles, start_pos 320
+    (1, 2, 1, 1, 70, True),       # a single query row
 ])
 def test_prefill_attention_matches_oracle(ctx, B, H, Hkv, S, KV, causal):
     import torch
@@ -40,6 +42,14 @@ def test_prefill_attention_matches_oracle(ctx, B, H, Hkv, S, KV, causal):
             ref = oracle.flash_attention(qf[b, h], kf[b, h // G], vf[b, h // G], scale, causal, start_pos=KV - S)
             err = rel_l2(out[b, h], ref)
             assert err < 1e-4, (b, h, err)
+
+
+def test_prefill_attention_without_keys_is_zero(ctx):
+    import torch
+    q = torch.ones(1, 2, 5, 128, dtype=torch.bfloat16, device="cuda")
+    k = torch.zeros(1, 1, 0, 128, dtype=torch.bfloat16, device="cuda")
+    out = ctx.attn_prefill(q, k, k, 0.1, True, start_pos=0)
+    assert out.shape == (1, 2, 5, 128) and float(out.abs().max()) == 0.0
 
 
 def test_prefill_attention_rejects_bad_shapes(ctx):
