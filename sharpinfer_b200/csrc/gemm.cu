@@ -5,11 +5,14 @@
 // DequantizeTensor produces, Quantization.cs:415-469).
 //
 // Pipeline (one call):
-//  1. k_dequant_f16: the weight's blocks -> f16 [N][K] in a context scratch
-//     buffer (element = the reference's f32 value d*sc*q - dmin*m, rounded to
-//     f16 once).  Dequantising inside the GEMM mainloop would cost each weight
-//     ~1 CUDA-core instruction per 128-256 MACs, several times the issue
-//     budget the tensor cores leave free, so it is a bandwidth-bound pre-pass.
+//  1. W to f16.  Q4_K with M <= 896: inside the GEMM (k_gemm_q4k), eight
+//     warps dequantise each 64-column step into the shared-memory B tile in
+//     f16x2 arithmetic, about 3 instructions per 2 weights, which hides under
+//     the tensor cores while each weight is dequantised by few row blocks.
+//     Otherwise (larger M, Q6_K, Q8_0) a pre-pass (k_dequant_f16) writes f16
+//     [N][K] to a context scratch buffer: element = the reference's f32 value
+//     d*sc*q - dmin*m, rounded to f16 once.  si_qgemm_cache_weight keeps that
+//     copy for later calls.
 //  2. k_bf16_to_f16: X -> f16 (exact for |x| < 65504; kind::f16 needs A and
 //     B of one type, and f16 keeps 3 more mantissa bits of W than bf16).
 //  3. k_gemm_tc: 128 x 256 output tile per CTA, K in steps of 64.  Warp 0
@@ -17,8 +20,8 @@
 //     tcgen05.mma (kind::f16, f32 accumulator in TMEM, 4 MMAs of K = 16 per
 //     stage) and tcgen05.commit to free stages, warps 2-5 read the
 //     accumulator back with tcgen05.ld and store Y.
-// Accuracy: the only rounding beyond f32 is W's f16 rounding (2^-12
-// relative), ~1e-4 relative L2 on Y.
+// Accuracy: W's f16 rounding (2^-12 relative; in the fused kernel also the
+// f16 rounding of d*sc and dmin*m and of the HFMA2), ~1e-4 relative L2 on Y.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -272,6 +275,223 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
   }
 }
 
+// Q4_K GEMM with the weight dequantised in shared memory (no f16 copy of W):
+// the same tile and warp plan as k_gemm_tc, except that B is produced by
+// eight dequantising warps (2-9) instead of TMA.  A 64-column K step is one
+// 512-byte nibble chunk of a tile-block (4 k-tiles), so for each of its
+// BN / 128 row tiles a lane loads one 16-byte word group (rows g and g+8,
+// k = 2t, 2t+1, 2t+8, 2t+9 of the chunk's 4 k-tiles) and writes 16 f16
+// pairs into the 128-byte-swizzled K-major B tile (conflict free: the 16-byte
+// chunk index is XORed with g).  Values are computed in f16x2:
+// (1024 + q) from the nibble bits (the device layout's exact f16 pairs),
+// minus 1024, times d*sc plus -dmin*m (both rounded to f16 once per
+// sub-block) -- one HFMA2 per pair.  The superblock header and the next
+// chunk are loaded one step ahead.  After the main loop warps 2-5 drain the
+// accumulator as in k_gemm_tc.  All waits are bounded; after one gives up, a
+// thread waits no more.
+__device__ __forceinline__ __half2 u2h2(uint32_t v) { return *(__half2*)&v; }
+__device__ __forceinline__ uint32_t h22u(__half2 v) { return *(uint32_t*)&v; }
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(m), "r"(o));  // (a & m) | o
+  return r;
+}
+
+template <int GN>
+__global__ void __launch_bounds__(320, 1) k_gemm_q4k(const __grid_constant__ CUtensorMap tmA, const uint8_t* __restrict__ W,
+                                                     int tiles, float* __restrict__ Y, int M, int N, int K, int* err) {
+  constexpr int B_BYTES = GemmCfg<GN>::B_BYTES;
+  constexpr uint32_t IDESC = GemmCfg<GN>::IDESC;
+  constexpr int RT = GN / 128;  // row tiles per dequantising warp
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sA = base, sB = base + GST * A_BYTES, bars = sB + GST * B_BYTES;
+  // a_full[GST] b_full[GST] empty[GST] done, TMEM slot
+  const uint32_t a_full = bars, b_full = bars + 8 * GST, empty = bars + 16 * GST, done = bars + 24 * GST,
+                 tslot = done + 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * GM, n0 = blockIdx.x * GN, nk = K / GK, nblk = K / 256;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < GST; s++) {
+      mbar_init(a_full + 8 * s, 1);
+      mbar_init(b_full + 8 * s, 256);
+      mbar_init(empty + 8 * s, 1);
+    }
+    mbar_init(done, 1);
+    mbar_fence_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tslot), "r"(GN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = lds_u32(tslot);
+  pdl_launch();
+  pdl_wait();  // A is written by the preceding conversion kernel
+
+  bool ok = true;
+  if (warp == 0) {
+    if (lane == 0) {  // TMA producer of A
+      for (int kt = 0; kt < nk && ok; kt++) {
+        const int s = kt % GST;
+        if (kt >= GST && !mbar_wait_bounded(empty + 8 * s, (uint32_t)((kt / GST - 1) & 1))) ok = false;
+        mbar_arrive_expect_tx(a_full + 8 * s, A_BYTES);
+        tma_load_2d(sA + s * A_BYTES, &tmA, kt * GK, m0, a_full + 8 * s);
+      }
+      if (!ok) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // MMA issuer
+      for (int kt = 0; kt < nk; kt++) {
+        const int s = kt % GST;
+        if (ok && !mbar_wait_bounded(a_full + 8 * s, (uint32_t)((kt / GST) & 1))) ok = false;
+        if (ok && !mbar_wait_bounded(b_full + 8 * s, (uint32_t)((kt / GST) & 1))) ok = false;
+        tc_fence_after();
+        if (ok) {
+          const uint64_t da = sdesc_k128(sA + s * A_BYTES), db = sdesc_k128(sB + s * B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < GK / 16; kk++) umma_f16(tmem, da + 2 * kk, db + 2 * kk, IDESC, (kt | kk) != 0);
+        }
+        umma_commit(empty + 8 * s);
+      }
+      umma_commit(done);
+      if (!ok) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
+    }
+  } else {
+    {  // B producers: dequantising warp dw takes row tiles dw and dw + 8 of the CTA's GN rows
+      const int dw = warp - 2, g = lane >> 2, t = lane & 3;
+      const uint8_t* tb[RT];
+      bool have[RT];
+#pragma unroll
+      for (int rt = 0; rt < RT; rt++) {
+        const int Tg = n0 / 16 + dw + 8 * rt;
+        have[rt] = Tg < tiles;
+        tb[rt] = W + (int64_t)(have[rt] ? Tg : 0) * nblk * 2304;
+      }
+      uint4 qc[RT], hc[RT][2];  // this step's nibble words; this superblock's headers (rows g, g+8)
+#pragma unroll
+      for (int rt = 0; rt < RT; rt++) {
+        qc[rt] = __ldg((const uint4*)(tb[rt] + 256 + 16 * lane));
+        hc[rt][0] = __ldg((const uint4*)(tb[rt] + 16 * g));
+        hc[rt][1] = __ldg((const uint4*)(tb[rt] + 16 * (g + 8)));
+      }
+      uint32_t ds[RT][2][8], nm[RT][2][8];  // (d sc, d sc) and (-dmin m, -dmin m) per sub-block; row g+8: d sc / 16
+      for (int sb = 0; sb < nblk; sb++) {
+#pragma unroll
+        for (int rt = 0; rt < RT; rt++)
+#pragma unroll
+          for (int h = 0; h < 2; h++) {  // GetScaleMinK4 (Quantization.cs:302-314)
+            const uint4 hd = hc[rt][h];
+            const float d = h2f(hd.x & 0xFFFF), dmin = h2f(hd.x >> 16);
+            const uint32_t qw[3] = {hd.y, hd.z, hd.w};
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+              auto qb = [&](int k) { return (qw[k >> 2] >> (8 * (k & 3))) & 0xFF; };
+              uint32_t sc, mn;
+              if (j < 4) {
+                sc = qb(j) & 63;
+                mn = qb(j + 4) & 63;
+              } else {
+                sc = (qb(j + 4) & 0xF) | ((qb(j - 4) >> 6) << 4);
+                mn = (qb(j + 4) >> 4) | ((qb(j) >> 6) << 4);
+              }
+              const float dsc = __fmul_rn(d, (float)sc) * (h ? 0.0625f : 1.0f);
+              const float ndm = -__fmul_rn(dmin, (float)mn);
+              ds[rt][h][j] = h22u(__float2half2_rn(dsc));
+              nm[rt][h][j] = h22u(__float2half2_rn(ndm));
+            }
+          }
+#pragma unroll
+        for (int c = 0; c < 4; c++) {  // the superblock's four 64-column steps
+          const int kt = 4 * sb + c, s = kt % GST, kn = kt + 1;
+          uint4 qn[RT], hn[RT][2];  // one step ahead
+          if (kn < nk) {
+#pragma unroll
+            for (int rt = 0; rt < RT; rt++) {
+              const uint8_t* tbn = tb[rt] + (int64_t)(kn >> 2) * 2304;
+              qn[rt] = __ldg((const uint4*)(tbn + 256 + 512 * (kn & 3) + 16 * lane));
+              if (c == 3) {
+                hn[rt][0] = __ldg((const uint4*)(tbn + 16 * g));
+                hn[rt][1] = __ldg((const uint4*)(tbn + 16 * (g + 8)));
+              }
+            }
+          }
+          if (ok && kt >= GST && !mbar_wait_bounded(empty + 8 * s, (uint32_t)((kt / GST - 1) & 1))) ok = false;
+          const uint32_t bst = sB + s * B_BYTES;
+          const __half2 k1024 = u2h2(0x64006400u);
+#pragma unroll
+          for (int rt = 0; rt < RT; rt++) {
+            if (!have[rt]) continue;  // rows past the weight: their output columns are not stored
+            const uint32_t row0 = bst + (uint32_t)(16 * (dw + 8 * rt) + g) * 128u + 4u * t;  // row g; g + 8 at +1024
+            const uint32_t q4[4] = {qc[rt].x, qc[rt].y, qc[rt].z, qc[rt].w};
+#pragma unroll
+            for (int i = 0; i < 4; i++) {  // k-tile 4c + i: groups of 8 columns 2i and 2i + 1
+              const int j = 2 * c + (i >> 1);  // sub-block
+              const uint32_t w = q4[i], w8 = w >> 8;
+              const __half2 dg = u2h2(ds[rt][0][j]), mg = u2h2(nm[rt][0][j]);
+              const __half2 d8 = u2h2(ds[rt][1][j]), m8 = u2h2(nm[rt][1][j]);
+              const uint32_t a0 = h22u(__hfma2(__hsub2(u2h2(lop_and_or(w, 0x000F000Fu, 0x64006400u)), k1024), dg, mg));
+              const uint32_t a1 = h22u(__hfma2(__hsub2(u2h2(lop_and_or(w8, 0x000F000Fu, 0x64006400u)), k1024), dg, mg));
+              const uint32_t b0 = h22u(__hfma2(__hsub2(u2h2(lop_and_or(w, 0x00F000F0u, 0x64006400u)), k1024), d8, m8));
+              const uint32_t b1 = h22u(__hfma2(__hsub2(u2h2(lop_and_or(w8, 0x00F000F0u, 0x64006400u)), k1024), d8, m8));
+              const uint32_t c0 = (uint32_t)(((2 * i) ^ g) << 4), c1 = (uint32_t)(((2 * i + 1) ^ g) << 4);
+              asm volatile("st.shared.u32 [%0], %1;" ::"r"(row0 + c0), "r"(a0) : "memory");
+              asm volatile("st.shared.u32 [%0], %1;" ::"r"(row0 + c1), "r"(a1) : "memory");
+              asm volatile("st.shared.u32 [%0], %1;" ::"r"(row0 + 1024u + c0), "r"(b0) : "memory");
+              asm volatile("st.shared.u32 [%0], %1;" ::"r"(row0 + 1024u + c1), "r"(b1) : "memory");
+            }
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(b_full + 8 * s);
+          if (kn < nk) {
+#pragma unroll
+            for (int rt = 0; rt < RT; rt++) {
+              qc[rt] = qn[rt];
+              if (c == 3) {
+                hc[rt][0] = hn[rt][0];
+                hc[rt][1] = hn[rt][1];
+              }
+            }
+          }
+        }
+      }
+    }
+    if (warp < 6) {  // epilogue: TMEM lanes 32 (warp % 4) .. +31 = tile rows
+      if (ok && !mbar_wait_bounded(done, 0)) ok = false;
+      if (!ok && lane == 0) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
+      tc_fence_after();
+      const int q = warp & 3;
+      const int row = m0 + 32 * q + lane;
+      float* yr = Y + (int64_t)row * N;
+      for (int c0 = 0; c0 < GN; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
+        if (!ok || row >= M) continue;
+        const int col0 = n0 + c0;
+        if (col0 + 32 <= N && (N & 3) == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *(float4*)(yr + col0 + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                    __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j++)
+            if (col0 + j < N) yr[col0 + j] = __uint_as_float(r[j]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GN) : "memory");
+  }
+}
+
 // 2D f16 tensor [rows][cols] (row-major), box [box_rows][64], 128-byte swizzle.
 int make_tmap(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t cols, int box_rows) {
   auto fn = encode_fn();
@@ -309,7 +529,12 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
   if (K % GK) SI_FAIL(SI_ERR_UNSUPPORTED, "qgemm: cols %lld not a multiple of %d", (long long)K, GK);
   SI_TRY(ensure(c->stage[1], (size_t)M * K * 2));
   __half* wf = (__half*)w->f16;
-  if (!wf) {  // no cached copy: dequantise into scratch for this call
+  // Q4_K without a cached copy: dequantised in shared memory while the row
+  // blocks of X are few (each one dequantises W again; measured on the 8B
+  // shapes the fused kernel wins at M = 512 and loses at M = 2048 to the
+  // pre-pass, crossing near M = 900).
+  const bool fused = !wf && w->qtype == SI_Q4_K && (M + GM - 1) / GM <= 7;
+  if (!wf && !fused) {  // no cached copy: dequantise into scratch for this call
     SI_TRY(ensure(c->stage[0], (size_t)N * K * 2));
     wf = (__half*)c->stage[0].ptr;
     SI_TRY(dequant_f16(c, w, wf));
@@ -324,6 +549,32 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
   const int GN = tiles256 < c->sm_count ? 128 : 256;
   CUtensorMap ta, tb;
   SI_TRY(make_tmap(&ta, xf, M, K, GM));
+  if (fused) {
+    static uint64_t fattr[2] = {0, 0};
+    const int fi = GN == 128 ? 0 : 1;
+    const int fsmem = GN == 128 ? GemmCfg<128>::SMEM : GemmCfg<256>::SMEM;
+    if (c->device < 64 && !(fattr[fi] & (1ull << c->device))) {
+      if (GN == 128) SI_CUDA(cudaFuncSetAttribute(k_gemm_q4k<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, fsmem));
+      else SI_CUDA(cudaFuncSetAttribute(k_gemm_q4k<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, fsmem));
+      fattr[fi] |= 1ull << c->device;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((N + GN - 1) / GN), (unsigned)((M + GM - 1) / GM));
+    cfg.blockDim = dim3(320);
+    cfg.dynamicSmemBytes = fsmem;
+    cfg.stream = c->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const uint8_t* wd = (const uint8_t*)w->dev;
+    if (GN == 128)
+      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<128>, ta, wd, (int)w->tiles, y, M, (int)N, (int)K, c->dev_err));
+    else
+      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<256>, ta, wd, (int)w->tiles, y, M, (int)N, (int)K, c->dev_err));
+    return SI_OK;
+  }
   SI_TRY(make_tmap(&tb, wf, N, K, GN));
   static uint64_t attr_set[2] = {0, 0};
   const int ai = GN == 128 ? 0 : 1;

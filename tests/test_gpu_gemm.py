@@ -58,14 +58,19 @@ def test_qgemm_repeatable_and_rejects_bad_shapes(ctx):
     w.free()
 
 
-def test_cached_f16_weight_gives_the_same_result(ctx):
+def test_cached_f16_weight_matches_the_oracle_too(ctx):
+    """Q4_K without a cached copy is dequantised in shared memory (f16x2
+    arithmetic); with si_qgemm_cache_weight the GEMM reads the f16 copy (f32
+    arithmetic, one rounding).  Both stay within the bar of the oracle."""
     import torch
     blocks = synth_blocks_host(N.SI_Q4_K, 512, 1024, 8, 2, N.SYNTH_PLAIN, 0.01)
+    xb, xf = bf16_round(np.random.default_rng(8).standard_normal((200, 1024)))
+    ref = oracle.qmatvec(N.SI_Q4_K, blocks, 512, 1024, xf)
     w = ctx.upload(N.SI_Q4_K, blocks, 512, 1024)
-    x = torch.randn(200, 1024, device="cuda").to(torch.bfloat16)
-    a = ctx.qgemm(w, x)
+    x = torch.from_numpy(xb.view(np.int16)).cuda().view(torch.bfloat16)
+    a = ctx.qgemm(w, x).cpu().numpy()
     ctx.qgemm_cache_weight(w)
-    b = ctx.qgemm(w, x)
+    b = ctx.qgemm(w, x).cpu().numpy()
     ctx.synchronize()
-    assert torch.equal(a, b)
+    assert rel_l2(a, ref) < TOL and rel_l2(b, ref) < TOL, (rel_l2(a, ref), rel_l2(b, ref))
     w.free()
