@@ -574,7 +574,7 @@ __device__ __forceinline__ void store_tile(float* __restrict__ y, int64_t rows, 
 
 template <int QT, int EPI, int B, int NW, int NS>
 __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
-    k_qmv_warp(const uint8_t* __restrict__ W, int nblk, int64_t rows, int tiles,
+    k_qmv_warp(const uint8_t* __restrict__ W, int nblk, int64_t rows, int tiles, int tile_mode,
                const uint8_t* __restrict__ xprep, float* __restrict__ y, QmvScratch scr) {
   using Cfg = WarpCfg<QT, B, NW, NS>;
   constexpr int TBB = Cfg::TBB, QPU = Cfg::QPU, LW = Cfg::LW, XB = Cfg::XB, WB = Cfg::WB, SB = Cfg::SB;
@@ -586,10 +586,17 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   const uint32_t bar0 = smem_u32(zero + Cfg::ZERO) + warp * NS * 8;
 
   const int nunit = (nblk + QPU - 1) / QPU;
-  const int64_t U = (int64_t)tiles * nunit;
-  const int64_t GW = (int64_t)gridDim.x * NW, gw = (int64_t)blockIdx.x * NW + warp;
-  const int64_t ub = U * gw / GW, ue = U * (gw + 1) / GW;
-  const int total = (int)(ue - ub);
+  // Work split: the CTA takes units [cb, ce) -- whole row tiles in tile mode,
+  // so no tile is shared between CTAs, else an even share -- and warp w the
+  // w-th of NW even parts of that range.  32-bit index math (the host checks
+  // tiles * nunit * grid < 2^31): a 64-bit division is a long subroutine.
+  const int U = tiles * nunit;
+  const int G = gridDim.x, cta = blockIdx.x;
+  const int cb = tile_mode ? tiles * cta / G * nunit : U * cta / G;
+  const int ce = tile_mode ? tiles * (cta + 1) / G * nunit : U * (cta + 1) / G;
+  const int PC = ce - cb;
+  const int ub = cb + PC * warp / NW, ue = cb + PC * (warp + 1) / NW;
+  const int total = ue - ub;
 
   for (int i = threadIdx.x; i < Cfg::ZERO / 4; i += blockDim.x) ((uint32_t*)zero)[i] = 0u;
   if (lane == 0) {
@@ -600,9 +607,9 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
 
   // Units are contiguous in memory in range order, so the weight cursor only
   // advances; the activation cursor wraps to unit 0 at each tile.
-  const int64_t c0T = ub / nunit;
-  const int c0U = (int)(ub - c0T * nunit);
-  const uint8_t* wsrc = W + (c0T * nblk + (int64_t)c0U * QPU) * TBB;
+  const int c0T = ub / nunit;
+  const int c0U = ub - c0T * nunit;
+  const uint8_t* wsrc = W + ((int64_t)c0T * nblk + (int64_t)c0U * QPU) * TBB;
   int iU = c0U;                      // unit index (in its tile) of the next copy to issue
   const int pre = total < NS ? total : NS;
   if (lane == 0) {
@@ -639,9 +646,9 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   bool has0 = false, has1 = false;
   bool ok = true;
   uint32_t ph = 0;
-  int cT = (int)c0T, cU = c0U;
+  int cT = c0T, cU = c0U;
   int left = min(nunit - c0U, total);  // units of the current tile in this range
-  int64_t tile_first = c0T * nunit;
+  int tile_first = c0T * nunit;
   for (int k0 = 0; k0 < total; k0 += NS) {
 #pragma unroll
     for (int s = 0; s < NS; s++) {
@@ -677,10 +684,10 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
       cU++;
       if (--left == 0) {
         // ---- this warp's part of tile cT is done ----
-        const int64_t t0 = tile_first, t1 = tile_first + nunit;  // tile's unit range
+        const int t0 = tile_first, t1 = tile_first + nunit;  // tile's unit range
         if (t0 >= ub && t1 <= ue) {
           store_tile<EPI, B>(y, rows, cT, lane, tg[0], tg8[0], scr.tp);
-        } else if (cT == (int)c0T) {  // first tile of the range, shared with other warps
+        } else if (cT == c0T) {  // first tile of the range, shared with other warps
           p0a = tg[0];
           p0b = tg8[0];
           has0 = true;
@@ -712,29 +719,30 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   part[(warp * 2 + 1) * 64 + lane] = p1a;
   part[(warp * 2 + 1) * 64 + 32 + lane] = p1b;
   __syncthreads();
-  const int64_t cw0 = (int64_t)blockIdx.x * NW;  // global id of this CTA's warp 0
+  auto warp_of = [&](int q) { return ((q - cb + 1) * NW - 1) / PC; };  // warp holding unit q
 #pragma unroll 1
   for (int sl = 0; sl < 2; sl++) {
     if (!(sl == 0 ? has0 : has1) || !ok) continue;
-    const int64_t T = sl == 0 ? c0T : (int64_t)cT - 1;
-    const int64_t t0 = T * nunit, t1 = t0 + nunit;
-    // owner(x) = the last warp whose range starts at or before unit x
-    const int64_t wf = ((t0 + 1) * GW - 1) / U, wl = (t1 * GW - 1) / U;
-    const int64_t jf = wf > cw0 ? wf : cw0, jl = wl < cw0 + NW - 1 ? wl : cw0 + NW - 1;
-    if (gw != jf) continue;  // another warp of this CTA combines this tile
+    const int T = sl == 0 ? c0T : cT - 1;
+    const int t0 = T * nunit, t1 = t0 + nunit;
+    const int lo = t0 > cb ? t0 : cb, hi = t1 < ce ? t1 : ce;  // the tile's part in this CTA
+    const int jf = warp_of(lo), jl = warp_of(hi - 1);
+    if (warp != jf) continue;  // another warp of this CTA combines this tile
     float a = 0.f, b8 = 0.f;
-    for (int64_t j = jf; j <= jl; j++) {
-      const int slot = (U * j / GW) / nunit == T ? 0 : 1;  // T is warp j's first tile?
-      a += part[((j - cw0) * 2 + slot) * 64 + lane];
-      b8 += part[((j - cw0) * 2 + slot) * 64 + 32 + lane];
+    for (int j = jf; j <= jl; j++) {
+      const int fj = cb + PC * j / NW;                    // first unit of warp j
+      const int slot = (fj >= t0 && fj < t1) ? 0 : 1;  // T is warp j's first tile?
+      a += part[(j * 2 + slot) * 64 + lane];
+      b8 += part[(j * 2 + slot) * 64 + 32 + lane];
     }
-    if (wf >= cw0 && wl < cw0 + NW) {
-      store_tile<EPI, B>(y, rows, (int)T, lane, a, b8, scr.tp);
+    if (t0 >= cb && t1 <= ce) {  // the whole tile is in this CTA
+      store_tile<EPI, B>(y, rows, T, lane, a, b8, scr.tp);
       continue;
     }
-    const int64_t cf = wf / NW, cl = wl / NW;
-    const int ncon = (int)(cl - cf + 1), cslot = (int)(blockIdx.x - cf);
-    float* base = scr.split + T * scr.maxc * 64;
+    // unit x lies in CTA ((x + 1) G - 1) / U (even-share mode only)
+    const int cf = ((t0 + 1) * G - 1) / U, cl = (t1 * G - 1) / U;
+    const int ncon = cl - cf + 1, cslot = cta - cf;
+    float* base = scr.split + (int64_t)T * scr.maxc * 64;
     base[cslot * 64 + lane] = a;
     base[cslot * 64 + 32 + lane] = b8;
     __threadfence();
@@ -761,7 +769,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
             sb += vb[j];
           }
       }
-      store_tile<EPI, B>(y, rows, (int)T, lane, sa, sb, scr.tp);
+      store_tile<EPI, B>(y, rows, T, lane, sa, sb, scr.tp);
       if (lane == 0) scr.count[T] = 0;
     }
   }
@@ -1188,21 +1196,35 @@ int launch_warp_cfg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, fl
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     attr_set |= 1ull << dev;
   }
-  // every warp gets a non-empty range: GW = grid * NW <= units
   const int64_t nunit = (w->nblk + Cfg::QPU - 1) / Cfg::QPU;
   const int64_t units = w->tiles * nunit;
-  const int64_t grid = qmv_warp_grid(units, NW, sms);
-  const int64_t minr = units / (grid * NW);
-  const int maxc = (int)((nunit - 1 + minr - 1) / minr + 1);
-  if ((size_t)w->tiles * maxc * 64 * 4 > scr_cap.split_bytes || w->tiles > scr_cap.count_n)
-    SI_FAIL(SI_ERR_INVALID, "qmatvec: scratch too small (need %lld tiles x %d slots)",
-            (long long)w->tiles, maxc);
+  if (units * sms >= (int64_t)1 << 31)
+    SI_FAIL(SI_ERR_UNSUPPORTED, "qmatvec: %lld x %lld is too large for one launch", (long long)w->rows,
+            (long long)w->cols);
+  // Tile mode (whole row tiles per CTA, no partial sums between CTAs) unless
+  // one tile of imbalance costs more than the ~3 us cross-CTA combine; in
+  // even-share mode every warp gets a non-empty range (grid * NW <= units).
+  const double sm_bytes_us = 6.5e6 / sms;  // bytes per microsecond per SM
+  const double ubytes = (double)Cfg::TBB * Cfg::QPU;
+  const int64_t g_tile = std::min<int64_t>(w->tiles, sms);
+  const double t_tile = (double)((w->tiles + g_tile - 1) / g_tile) * nunit * ubytes / sm_bytes_us;
+  const int64_t g_even = qmv_warp_grid(units, NW, sms);
+  const double t_even = (double)units * ubytes / (sm_bytes_us * g_even) + 3.0;
+  const int tile_mode = t_tile <= t_even ? 1 : 0;
+  const int64_t grid = tile_mode ? g_tile : g_even;
   QmvScratch scr = scr_cap.scr;
-  scr.maxc = maxc;
+  scr.maxc = 0;
+  if (!tile_mode) {
+    const int64_t minr = units / (grid * NW);
+    scr.maxc = (int)((nunit - 1 + minr - 1) / minr + 1);
+    if ((size_t)w->tiles * scr.maxc * 64 * 4 > scr_cap.split_bytes || w->tiles > scr_cap.count_n)
+      SI_FAIL(SI_ERR_INVALID, "qmatvec: scratch too small (need %lld tiles x %d slots)", (long long)w->tiles,
+              scr.maxc);
+  }
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)grid), dim3(NW * 32), Cfg::SMEM, pdl, attr);
-  SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv_warp<QT, EPI, B, NW, NS>, (const uint8_t*)w->dev,
-                             (int)w->nblk, w->rows, (int)w->tiles, xprep, y, scr));
+  SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv_warp<QT, EPI, B, NW, NS>, (const uint8_t*)w->dev, (int)w->nblk, w->rows,
+                             (int)w->tiles, tile_mode, xprep, y, scr));
   return SI_OK;
 }
 
