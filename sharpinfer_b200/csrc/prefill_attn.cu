@@ -30,8 +30,9 @@ __device__ __forceinline__ float ex2(float x) {
 // of 64 (N).  Warp 0: TMA (Q once, K and V^T tiles through a 3-stage ring);
 // warp 1: tcgen05.mma issuer; warps 2-9: softmax, two threads per query row
 // (TMEM lanes 32 (warp % 4) .. + 31), warps 2-5 on key columns 0-31 and
-// output dims 0-63, warps 6-9 on the other halves; the two exchange their
-// row maxima through shared memory.  Per key tile j:
+// output dims 0-63, warps 6-9 on the other halves; the two warps of a row
+// quarter exchange their row maxima through shared memory (a 64-thread named
+// barrier per pair).  Per key tile j:
 //   S_j = Q K_j^T            (M 128, N 64, K 128: 8 MMAs) -> TMEM S[j % 2]
 //   softmax: masked row max, p = exp(s - m), running sum, P_j written to
 //            shared memory as bf16 hi + lo in the K-major 128-byte-swizzled
@@ -193,7 +194,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
         }
       }
       xch[pb * 256 + half * 128 + r] = mx;  // the row maximum needs both halves
-      asm volatile("bar.sync 1, 256;" ::: "memory");
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + qq) : "memory");  // the two warps of this row quarter
       mx = fmaxf(mx, xch[pb * 256 + (half ^ 1) * 128 + r]);
       const float mn = fmaxf(m, mx);
       const float alpha = mn == -INFINITY ? 1.f : ex2(m - mn);
@@ -269,7 +270,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
       }
     }
     xch[512 + half * 128 + r] = l;  // the row sum adds both halves' keys
-    asm volatile("bar.sync 1, 256;" ::: "memory");
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + qq) : "memory");  // the two warps of this row quarter
     const float lr = l + xch[512 + (half ^ 1) * 128 + r];
     if (!ok && lane == 0) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
     if (qrow < S) {  // a row without a visible key is 0 (FlashAttention.cs:155-163)
