@@ -37,8 +37,9 @@ __device__ __forceinline__ float ex2(float x) {
 //   softmax: masked row max, p = exp(s - m), running sum, P_j written to
 //            shared memory as bf16 hi + lo in the K-major 128-byte-swizzled
 //            A-operand layout
-//   O_j = P_hi V_j + P_lo V_j (M 128, N 128, K 64: 8 MMAs)  -> TMEM O[j % 2]
-//   softmax warps: O += O_{j-1} rescaled (in registers), one tile behind.
+//   O += P_hi V_j + P_lo V_j (M 128, N 128, K 64: 8 MMAs), one TMEM accumulator
+//   the maximum in use is raised only when the row maximum passes it by
+//   more than 8 (base 2); then the softmax threads rescale O in TMEM first.
 // S_{j+1} is issued before O_j, so the softmax of tile j overlaps it.  V is
 // used transposed (V^T [d][keys], made by k_vt) so that both operands of
 // every MMA are K-major.  All waits are bounded.
@@ -64,9 +65,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
   const uint32_t sQ = base, sK = sQ + FA_QB, sV = sK + FA_NST * FA_KB, sP = sV + FA_NST * FA_VB;
   const uint32_t bars = sP + 4 * FA_PB;
   float* xch = (float*)(smem_raw + (bars + 256 - smem_u32(smem_raw)));  // [3][256] f32
-  // barriers: kv_full[NST] kv_empty[NST] s_full[2] s_free[2] p_full[2] o_full[2] o_free[2] q_full, TMEM slot
+  // barriers: kv_full[NST] kv_empty[NST] s_full[2] s_free[2] p_full[2] o_full[2] (unused slot) q_full, TMEM slot
   const uint32_t kv_full = bars, kv_empty = bars + 8 * FA_NST, s_full = bars + 16 * FA_NST, s_free = s_full + 16,
-                 p_full = s_full + 32, o_full = s_full + 48, o_free = s_full + 64, q_full = s_full + 80,
+                 p_full = s_full + 32, o_full = s_full + 48, q_full = s_full + 80,
                  tslot = s_full + 88;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qblk = causal ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;  // longest key ranges first
@@ -83,7 +84,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
       mbar_init(s_free + 8 * i, 256);
       mbar_init(p_full + 8 * i, 256);
       mbar_init(o_full + 8 * i, 1);
-      mbar_init(o_free + 8 * i, 256);
     }
     mbar_init(q_full, 1);
     mbar_fence_init();
@@ -136,13 +136,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
         if (j + 1 < nt) issue_s(j + 1);
         const int st = j % FA_NST, pb = j & 1;
         if (ok && !mbar_wait_bounded(p_full + 8 * pb, (uint32_t)((j / 2) & 1))) ok = false;
-        if (ok && j >= 2 && !mbar_wait_bounded(o_free + 8 * pb, (uint32_t)((j / 2 - 1) & 1))) ok = false;
         tc_fence_after();
-        if (ok) {
-          const uint32_t ph = sP + pb * 2 * FA_PB, vt = sV + st * FA_VB, d = tmem + 128 + 128 * pb;
+        if (ok) {  // O accumulates over the tiles in one TMEM buffer
+          const uint32_t ph = sP + pb * 2 * FA_PB, vt = sV + st * FA_VB, d = tmem + 128;
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
-            umma_f16(d, sdesc_k128(ph) + 2 * kk, sdesc_k128(vt) + 2 * kk, FA_IDESC_O, kk != 0);
+            umma_f16(d, sdesc_k128(ph) + 2 * kk, sdesc_k128(vt) + 2 * kk, FA_IDESC_O, (j | kk) != 0);
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
             umma_f16(d, sdesc_k128(ph + FA_PB) + 2 * kk, sdesc_k128(vt) + 2 * kk, FA_IDESC_O, 1);
@@ -155,10 +154,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
   } else {  // softmax: two threads per query row r of the tile
     const int qq = warp & 3, half = (warp - 2) >> 2, r = 32 * qq + lane, qrow = q0 + r;
     const uint32_t lanes = (uint32_t)(32 * qq) << 16;
-    float oacc[64];  // output dims 64 half .. + 63
-#pragma unroll
-    for (int i = 0; i < 64; i++) oacc[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;  // m in base-2 units; l over this thread's keys
+    const uint32_t ocol = tmem + lanes + 128 + 64 * half;  // this thread's 64 dims of O
+    // Base-2 units: t = s * scale * log2(e), p = 2^(t - m) = e^(s scale - m')
+    // with m the maximum in use.  O accumulates in TMEM with that m; it is
+    // raised (and O and l rescaled) only when the row maximum exceeds it by
+    // more than 8, so p <= 2^8 and most tiles need no rescale.
+    float m = -INFINITY, l = 0.f;  // l over this thread's keys
     const float sc2 = scale * 1.4426950408889634f;  // scale * log2(e)
     for (int j = 0; j < nt; j++) {
       const int pb = j & 1;
@@ -173,8 +174,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
       }
       tc_fence_before();
       mbar_arrive(s_free + 8 * pb);
-      // mask, running max (FlashAttention.cs:206-224, 238-325), in base-2
-      // units: t = s * scale * log2(e), p = 2^(t - max t) = e^(s scale - max)
+      // mask, row maximum (FlashAttention.cs:206-224, 238-325)
       const int k0 = j * FA_BK + 32 * half;
       const bool full = k0 + 32 <= KV && (!causal || k0 + 31 <= q0 + start_pos);  // no key masked
       float mx = -INFINITY;
@@ -196,13 +196,30 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
       xch[pb * 256 + half * 128 + r] = mx;  // the row maximum needs both halves
       asm volatile("bar.sync %0, 64;" ::"r"(1 + qq) : "memory");  // the two warps of this row quarter
       mx = fmaxf(mx, xch[pb * 256 + (half ^ 1) * 128 + r]);
-      const float mn = fmaxf(m, mx);
-      const float alpha = mn == -INFINITY ? 1.f : ex2(m - mn);
+      if (mx > m + 8.f) {  // raise the maximum in use (both threads of the row decide alike)
+        const bool had = m != -INFINITY;
+        const float alpha = had ? ex2(m - mx) : 0.f;
+        l *= alpha;
+        m = mx;
+        if (had && j >= 1) {  // O so far (tiles < j) is complete and rescaled in place
+          if (ok && !mbar_wait_bounded(o_full + 8 * ((j - 1) & 1), (uint32_t)(((j - 1) / 2) & 1))) ok = false;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 2; c++) {
+            uint32_t t32[32];
+            tmem_ld32(ocol + 32 * c, t32);
+#pragma unroll
+            for (int i = 0; i < 32; i++) t32[i] = __float_as_uint(__uint_as_float(t32[i]) * alpha);
+            tmem_st32(ocol + 32 * c, t32);
+          }
+          tc_fence_before();
+        }
+      }
       float ps = 0.f;
-      if (mn != -INFINITY) {
+      if (m != -INFINITY) {
 #pragma unroll
         for (int i = 0; i < 32; i++) {
-          const float p = ex2(sv[i] - mn);  // 2^-inf = 0 for masked keys
+          const float p = ex2(sv[i] - m);  // 2^-inf = 0 for masked keys; <= 2^8
           sv[i] = p;
           ps += p;
         }
@@ -210,10 +227,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
 #pragma unroll
         for (int i = 0; i < 32; i++) sv[i] = 0.f;
       }
-      l = l * alpha + ps;
-      m = mn;
-      // P_j goes to the buffer P_{j-2} used; that product was complete when
-      // O_{j-2} was added in the previous iteration
+      l += ps;
+      // P_j goes to the buffer P_{j-2} used: wait for that product
+      if (ok && j >= 2 && !mbar_wait_bounded(o_full + 8 * pb, (uint32_t)(((j - 2) / 2) & 1))) ok = false;
       {  // P_j as bf16 hi + lo: row r, chunks of 8 keys, chunk g at (g ^ (r % 8)) * 16 in the 128-byte row
         const uint32_t ph = sP + pb * 2 * FA_PB + r * 128;
 #pragma unroll
@@ -240,38 +256,26 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
       }
       fence_proxy_async_smem();
       mbar_arrive(p_full + 8 * pb);
-      if (j >= 1) {  // O += rescaled O_{j-1}
-        if (ok && !mbar_wait_bounded(o_full + 8 * ((j - 1) & 1), (uint32_t)(((j - 1) / 2) & 1))) ok = false;
-        tc_fence_after();
-        const uint32_t ob = tmem + lanes + 128 + 128 * ((j - 1) & 1) + 64 * half;
-#pragma unroll
-        for (int c = 0; c < 2; c++) {
-          uint32_t t32[32];
-          tmem_ld32(ob + 32 * c, t32);
-#pragma unroll
-          for (int i = 0; i < 32; i++) oacc[32 * c + i] = fmaf(oacc[32 * c + i], alpha_prev, __uint_as_float(t32[i]));
-        }
-        tc_fence_before();
-        mbar_arrive(o_free + 8 * ((j - 1) & 1));
-      }
-      alpha_prev = alpha;
     }
-    if (nt > 0) {  // the last tile's O
-      const int j = nt - 1;
-      if (ok && !mbar_wait_bounded(o_full + 8 * (j & 1), (uint32_t)((j / 2) & 1))) ok = false;
+    xch[512 + half * 128 + r] = l;  // the row sum adds both halves' keys
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + qq) : "memory");
+    const float lr = l + xch[512 + (half ^ 1) * 128 + r];
+    float oacc[64];
+    if (nt > 0) {  // O after the last tile's product
+      const int jl = nt - 1;
+      if (ok && !mbar_wait_bounded(o_full + 8 * (jl & 1), (uint32_t)((jl / 2) & 1))) ok = false;
       tc_fence_after();
-      const uint32_t ob = tmem + lanes + 128 + 128 * (j & 1) + 64 * half;
 #pragma unroll
       for (int c = 0; c < 2; c++) {
         uint32_t t32[32];
-        tmem_ld32(ob + 32 * c, t32);
+        tmem_ld32(ocol + 32 * c, t32);
 #pragma unroll
-        for (int i = 0; i < 32; i++) oacc[32 * c + i] = fmaf(oacc[32 * c + i], alpha_prev, __uint_as_float(t32[i]));
+        for (int i = 0; i < 32; i++) oacc[32 * c + i] = __uint_as_float(t32[i]);
       }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; i++) oacc[i] = 0.f;
     }
-    xch[512 + half * 128 + r] = l;  // the row sum adds both halves' keys
-    asm volatile("bar.sync %0, 64;" ::"r"(1 + qq) : "memory");  // the two warps of this row quarter
-    const float lr = l + xch[512 + (half ^ 1) * 128 + r];
     if (!ok && lane == 0) atomicOr(err, SI_DEVERR_WAIT_TIMEOUT);
     if (qrow < S) {  // a row without a visible key is 0 (FlashAttention.cs:155-163)
       const float inv = lr > 0.f ? 1.0f / lr : 0.f;
