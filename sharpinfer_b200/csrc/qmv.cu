@@ -123,38 +123,47 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
   }
   if (mode == SI_PREP_RMSNORM_TP) {
     // residual + the tp partial sums, added in rank order (identical on every
-    // rank); each partial-sum element is awaited through its tag.  Eight
-    // elements per thread are in flight at a time: their words are loaded
-    // together and only a word whose tag is not there yet is polled.
+    // rank); each partial-sum element is awaited through its tag.  Four
+    // elements per thread at a time, the words of every rank loaded together
+    // (up to 32 loads in flight, whatever the rank count); only a word whose
+    // tag is not there yet is polled.
     const unsigned want = *tpp.epoch * (unsigned)tpp.nlayers2 + (unsigned)tpp.flag_add;
     const int nper = (K + 255) / 256;  // elements of this thread: tid + 256 m
     float ss = 0.f, own = 0.f;
-    for (int m0 = 0; m0 < nper; m0 += 8) {
-      float a[8];
+    const uint8_t* slot0 = tpp.comm + tpp.slots_off + (int64_t)b * tpp.ld * (int64_t)sizeof(uint2);
+    for (int m0 = 0; m0 < nper; m0 += 4) {
+      float a[4];
+      uint2 w[SI_TP_MAX][4];
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
+      for (int j = 0; j < 4; j++) {
         const int i = tid + 256 * (m0 + j);
         a[j] = (m0 + j < nper && i < K) ? xb[i] : 0.f;
       }
-      for (int r = 0; r < tpp.tp; r++) {
-        const uint2* sl = (const uint2*)(tpp.comm + tpp.slots_off + r * tpp.src_stride) + (int64_t)b * tpp.ld;
-        uint2 w[8];
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+      for (int r = 0; r < SI_TP_MAX; r++) {
+        const uint2* sl = (const uint2*)(slot0 + (int64_t)r * tpp.src_stride);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
           const int i = tid + 256 * (m0 + j);
-          w[j] = (m0 + j < nper && i < K) ? ld_tagged(sl + i) : make_uint2(0u, want);
+          w[r][j] = (r < tpp.tp && m0 + j < nper && i < K) ? ld_tagged(sl + i) : make_uint2(0u, want);
         }
+      }
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          const int i = tid + 256 * (m0 + j);
-          if (m0 + j < nper && i < K) {
-            const uint32_t bits = (int)(w[j].y - want) >= 0 ? w[j].x : wait_tagged(sl + i, want, tpp.err);
-            a[j] = __fadd_rn(a[j], __uint_as_float(bits));
+      for (int r = 0; r < SI_TP_MAX; r++) {
+        if (r < tpp.tp) {
+          const uint2* sl = (const uint2*)(slot0 + (int64_t)r * tpp.src_stride);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int i = tid + 256 * (m0 + j);
+            if (m0 + j < nper && i < K) {
+              const uint32_t bits = (int)(w[r][j].y - want) >= 0 ? w[r][j].x : wait_tagged(sl + i, want, tpp.err);
+              a[j] = __fadd_rn(a[j], __uint_as_float(bits));
+            }
           }
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
+      for (int j = 0; j < 4; j++) {
         const int i = tid + 256 * (m0 + j);
         if (m0 + j < nper && i < K) {
           ss = __fadd_rn(ss, __fmul_rn(a[j], a[j]));
