@@ -192,10 +192,12 @@ SI_EXPORT int si_qmatvec_host(si_ctx* ctx, const si_weight* w, const float* x_ho
  * Limits: rows <= 32768, cols <= 16384, batch 1..16; larger shapes return
  * SI_ERR_UNSUPPORTED.  x [batch][cols] and y [batch][rows] are f32 device
  * pointers on w's device; `stream` is a cudaStream_t (NULL = legacy default
- * stream).  The call is synchronous on that stream.  The first call on a
- * device looks up the array's device address; make that first call before
- * any stream capture.  All calls on one GPU share the array: calls whose
- * work overlaps on the GPU (other streams or threads) race -- serialise them. */
+ * stream).  The call is synchronous on that stream.  Every call looks up the
+ * array's device address (so a device reset between calls is harmless); the
+ * first call on a device may load the library's kernels there, so make that
+ * first call before any stream capture.  All calls on one GPU share the
+ * array: calls whose work overlaps on the GPU (other streams or threads)
+ * race -- serialise them. */
 SI_EXPORT int si_qmatvec_noalloc(const si_weight* w, const float* x_dev, float* y_dev, int batch,
                                  void* stream);
 
@@ -257,6 +259,16 @@ SI_EXPORT int si_model_tp_handle(si_model* m, void* handle_out, int len);
 /* Map every rank's buffer: handles of ranks 0 .. tp-1, 64 bytes each
  * (the handles of si_model_tp_handle, gathered by the host). */
 SI_EXPORT int si_model_tp_connect(si_model* m, const void* handles, int len);
+/* Connect ranks that live in one process (for example one host thread per
+ * GPU) by their models instead of IPC handles: ranks[r] is rank r's model,
+ * r = 0 .. tp-1, all of one configuration.  Peer access is enabled between
+ * their devices.  Replaces the rank wiring of InferenceCluster
+ * (DistributedInference.cs:33-160) for workers in one process.  A rank that
+ * never steps makes the others' bounded waits give up -- the device-side
+ * counterpart of WaitForResponseAsync's timeout (DistributedInference.cs:158,
+ * :802): their si_decode_step returns SI_ERR_TIMEOUT after about a second
+ * and the context stays usable. */
+SI_EXPORT int si_model_tp_connect_local(si_model* m, si_model* const* ranks, int tp);
 /* The part of a whole tensor a rank holds: global rows grow0 .. grow0 + rows,
  * and in each row quant blocks gb0 .. gb0 + nblk of gnblk.  No device work. */
 SI_EXPORT int si_tp_slice(const si_model_config* cfg, int tp, int rank, int tensor, int64_t* grow0, int64_t* rows,

@@ -42,6 +42,9 @@ _SIGS = {
     "or_model_forward": (_i32, [_c_p, _i32, _i32, _i32, _i32, _c_p]),
     "or_round_f16": (_f32, [_f32]),
     "or_num_threads": (_i32, []),
+    "or_synth_blocks": (_i32, [_i32, _i64, _i64, ctypes.c_uint64, ctypes.c_uint64, _i32, _f32, _c_p]),
+    "or_synth_f32": (None, [_i64, ctypes.c_uint64, ctypes.c_uint64, _f32, _f32, _c_p]),
+    "or_synth_f16": (None, [_i64, ctypes.c_uint64, ctypes.c_uint64, _f32, _c_p]),
 }
 
 _lib = None
@@ -54,7 +57,8 @@ def build():
 def load():
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB) or os.path.getmtime(LIB) < os.path.getmtime(os.path.join(HERE, "oracle.cpp")):
+        srcs = [os.path.join(HERE, f) for f in ("oracle.cpp", "synth_host.cpp")]
+        if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(f) for f in srcs):
             build()
         lib = ctypes.CDLL(LIB)
         for n, (r, a) in _SIGS.items():
@@ -212,21 +216,110 @@ class OracleModel:
             pass
 
 
+# ---- seeded synthetic model (the inputs both sides are given) ----------------
+# Tensor ids and quant-type ids of the library's C ABI (si_tensor, si_qtype).
+T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_ATTN_NORM, T_FFN_NORM = range(9)
+T_EMB, T_LM_HEAD, T_FINAL_NORM = 100, 101, 102
+F32, Q8_0, Q4_K, Q6_K = 0, 8, 12, 14
+PLAIN, MODEL = 0, 1
+BLOCK = {Q4_K: (256, 144), Q6_K: (256, 210), Q8_0: (32, 34)}
+
+
+def synth_blocks(qt, rows, cols, seed, tag, recipe, sigma):
+    """Seeded GGUF blocks (the bytes of the library's si_synth_blocks_host)."""
+    be, bb = BLOCK[qt]
+    out = np.empty(rows * (cols // be) * bb, np.uint8)
+    if load().or_synth_blocks(qt, rows, cols, seed, tag, recipe, sigma, _p(out)):
+        raise ValueError("oracle: bad synthetic shape")
+    return out
+
+
+def synth_f32(n, seed, tag, mean, sigma):
+    out = np.empty(n, np.float32)
+    load().or_synth_f32(n, seed, tag, mean, sigma, _p(out))
+    return out
+
+
+def synth_f16(n, seed, tag, sigma=1.0):
+    out = np.empty(n, np.uint16)
+    load().or_synth_f16(n, seed, tag, sigma, _p(out))
+    return out
+
+
+def _recipe_sigma(qt, recipe, cols):
+    rc = np.sqrt(np.float32(cols))  # binary32 arithmetic, as the library computes it
+    if qt == Q4_K:
+        return np.float32(1.0) / (np.float32(23.3) * rc) if recipe == MODEL else np.float32(0.01)
+    if qt == Q6_K:
+        return np.float32(1.0) / (np.float32(348.0) * rc)
+    return np.float32(1.0) / (np.float32(73.9) * rc)
+
+
+def tensor_recipe(cfg, layer, t):
+    """(tag, qtype, recipe, sigma, mean, rows, cols) of a tensor of the seeded
+    synthetic model -- the same table as the library's si_model_tensor_recipe
+    (a CPU test checks that the two agree)."""
+    hd = cfg.head_dim
+    qr, kr = cfg.n_heads * hd, cfg.n_kv_heads * hd
+    q, rc, mu, sg = cfg.weight_qtype, MODEL, np.float32(0), np.float32(0)
+    if layer < 0:
+        tag = t - T_EMB + 1
+        if t == T_EMB:
+            q, r, k = cfg.emb_qtype, cfg.vocab, cfg.hidden
+        elif t == T_LM_HEAD:
+            q, r, k, rc = cfg.lm_head_qtype, cfg.vocab, cfg.hidden, PLAIN
+        elif t == T_FINAL_NORM:
+            q, r, k = F32, 1, cfg.hidden
+        else:
+            raise ValueError("unknown global tensor %d" % t)
+    else:
+        tag = 1000 * (layer + 1) + t
+        r, k = {T_Q: (qr, cfg.hidden), T_K: (kr, cfg.hidden), T_V: (kr, cfg.hidden), T_O: (cfg.hidden, qr),
+                T_GATE: (cfg.intermediate, cfg.hidden), T_UP: (cfg.intermediate, cfg.hidden),
+                T_DOWN: (cfg.hidden, cfg.intermediate), T_ATTN_NORM: (1, cfg.hidden),
+                T_FFN_NORM: (1, cfg.hidden)}[t]
+        if t in (T_ATTN_NORM, T_FFN_NORM):
+            q = F32
+    if q == F32:
+        mu, sg, rc = np.float32(1.0), np.float32(0.01), 0
+    elif t == T_EMB:
+        sg = np.float32(1.0) / np.float32(23.3) if q == Q4_K else _recipe_sigma(q, rc, 1)
+    else:
+        sg = _recipe_sigma(q, rc, k)
+    return tag, q, rc, float(sg), float(mu), r, k
+
+
+def host_tensor(cfg, seed, layer, t):
+    tag, qt, rc, sg, mu, rows, cols = tensor_recipe(cfg, layer, t)
+    if qt == F32:
+        return synth_f32(cols, seed, tag, mu, sg)
+    return synth_blocks(qt, rows, cols, seed, tag, rc, sg)
+
+
+def kv_tag(layer, seq, is_value):
+    return 0x4B560000 + (layer * 64 + seq) * 2 + int(bool(is_value))
+
+
+def host_kv(cfg, seed, layer, seq, length):
+    """f16 K and V of cache positions [0, length) in the reference layout [pos][kv head][dim]."""
+    n = length * cfg.n_kv_heads * cfg.head_dim
+    return synth_f16(n, seed, kv_tag(layer, seq, 0)), synth_f16(n, seed, kv_tag(layer, seq, 1))
+
+
 def synthetic_model(cfg, seed, n_seq, kv_len, threads=None):
-    """OracleModel holding exactly the tensors and KV prefix that si_model_synth / si_model_kv_synth
-    put on the device (generated on the host by the library's seeded generators)."""
-    from sharpinfer_b200 import native as N
-    from sharpinfer_b200.model import host_kv, host_tensor
+    """OracleModel holding exactly the tensors and KV prefix that the library's
+    si_model_synth / si_model_kv_synth put on the device (same generator, run
+    here on the host)."""
     om = OracleModel(cfg, n_seq, threads)
-    ids = [N.T_Q, N.T_K, N.T_V, N.T_O, N.T_GATE, N.T_UP, N.T_DOWN]
+    ids = [T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN]
     for l in range(cfg.n_layers):
         for which, t in enumerate(ids):
             om.set(l, which, cfg.weight_qtype, host_tensor(cfg, seed, l, t))
-        om.set(l, 7, 0, host_tensor(cfg, seed, l, N.T_ATTN_NORM))
-        om.set(l, 8, 0, host_tensor(cfg, seed, l, N.T_FFN_NORM))
-    om.set(-1, 0, cfg.emb_qtype, host_tensor(cfg, seed, -1, N.T_EMB))
-    om.set(-1, 1, cfg.lm_head_qtype, host_tensor(cfg, seed, -1, N.T_LM_HEAD))
-    om.set(-1, 2, 0, host_tensor(cfg, seed, -1, N.T_FINAL_NORM))
+        om.set(l, 7, 0, host_tensor(cfg, seed, l, T_ATTN_NORM))
+        om.set(l, 8, 0, host_tensor(cfg, seed, l, T_FFN_NORM))
+    om.set(-1, 0, cfg.emb_qtype, host_tensor(cfg, seed, -1, T_EMB))
+    om.set(-1, 1, cfg.lm_head_qtype, host_tensor(cfg, seed, -1, T_LM_HEAD))
+    om.set(-1, 2, 0, host_tensor(cfg, seed, -1, T_FINAL_NORM))
     if kv_len:
         for b in range(n_seq):
             for l in range(cfg.n_layers):

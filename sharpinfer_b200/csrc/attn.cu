@@ -191,11 +191,18 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   }
 
   bool ok = true;
+  // After a wait gives up (agreed by the whole CTA at the stage's barrier)
+  // nothing more is issued; thread 0 waits once, bounded, on each item still
+  // in flight -- items it .. it + AT_NS - 1 -- and the CTA skips the rest.
+  auto drain = [&](int it) {
+    if (tid == 0)
+      for (int j = it; j < min(items, it + AT_NS); j++) mbar_wait_bounded(bar0 + 8 * (j % AT_NS), (uint32_t)((j / AT_NS) & 1));
+  };
   const int p0 = 16 * warp;  // this warp's block in every stage
   // ---- pass 1: scores ----
   for (int it = 0; it < nsub; it++) {
     const int st = it % AT_NS;
-    if (!mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / AT_NS) & 1))) ok = false;
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / AT_NS) & 1)))) ok = false;
     const int rb = it * AT_SUB;
     const int np = min(AT_SUB, n - rb);
     if (ok && p0 < np) {
@@ -222,11 +229,15 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
         }
       }
     }
-    __syncthreads();  // stage consumed by every warp
+    ok = !__syncthreads_or(!ok);  // stage consumed by every warp
+    if (!ok) {
+      drain(it);
+      break;
+    }
     if (tid == 0 && it + AT_NS < items) issue(it + AT_NS);
   }
   // ---- softmax statistics per head (TensorOps.Softmax: max, exp, sum) ----
-  for (int h = warp; h < G; h += AT_WARPS) {
+  for (int h = warp; h < G && ok; h += AT_WARPS) {
     float m = -INFINITY;
     for (int i = lane; i < n; i += 32) m = fmaxf(m, sc[h * cp + i]);
     m = warp_max(m);
@@ -256,9 +267,9 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   for (int nt = 0; nt < NT; nt++)
 #pragma unroll
     for (int mt = 0; mt < 8; mt++) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
-  for (int it = nsub; it < items; it++) {
+  for (int it = nsub; it < items && ok; it++) {
     const int st = it % AT_NS;
-    if (!mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / AT_NS) & 1))) ok = false;
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / AT_NS) & 1)))) ok = false;
     const int rb = (it - nsub) * AT_SUB;
     const int np = min(AT_SUB, n - rb);
     uint8_t* vst = ring + st * AT_STAGE;
@@ -291,7 +302,11 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
         for (int nt = 0; nt < NT; nt++) mma16816(o[nt][mt], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
       }
     }
-    __syncthreads();
+    ok = !__syncthreads_or(!ok);
+    if (!ok) {
+      drain(it);
+      break;
+    }
     if (tid == 0 && it + AT_NS < items) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // zeroed rows before the refill
       issue(it + AT_NS);

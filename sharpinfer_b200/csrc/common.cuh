@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "../../include/sharpinfer_b200.h"
@@ -115,6 +116,19 @@ inline void qmv_scratch_need(int64_t tiles, int64_t nunit, int sms, size_t* spli
   *split_bytes = (size_t)tiles * worst * 64 * 4;
   *counts = tiles;
 }
+}  // namespace si
+
+namespace si {
+// One bit per device, set once a one-time per-device step (a kernel's
+// shared-memory attribute) has been done there.  Host threads working on
+// different GPUs may test and set it concurrently: at worst both do the step.
+struct DeviceOnce {
+  std::atomic<uint64_t> bits{0};
+  bool done(int dev) const { return dev >= 64 || ((bits.load(std::memory_order_acquire) >> dev) & 1u); }
+  void mark(int dev) {
+    if (dev < 64) bits.fetch_or(1ull << dev, std::memory_order_acq_rel);
+  }
+};
 }  // namespace si
 
 // Grow-only device buffer owned by a context.
@@ -333,6 +347,14 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity)
   }
   return false;
 }
+// After a bounded wait gave up: wait once more, bounded, for each ring stage s
+// whose copy may still be in flight (bit s of `pend`; bit s of `par` is the
+// phase it completes), so that no bulk copy is still writing shared memory
+// when the block moves on.  Worst case ns x 200 ms, not one wait per stage use.
+__device__ __forceinline__ void mbar_drain(uint32_t bar0, uint32_t pend, uint32_t par, int ns) {
+  for (int s = 0; s < ns; s++)
+    if ((pend >> s) & 1u) mbar_wait_bounded(bar0 + 8 * s, (par >> s) & 1u);
+}
 // Bulk global -> shared copy (16-byte aligned addresses, size a multiple of 16)
 // completing `bytes` transactions on the barrier.
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
@@ -374,15 +396,19 @@ __device__ __forceinline__ uint2 ld_tagged(const void* p) {
   return make_uint2((uint32_t)w, (uint32_t)(w >> 32));
 }
 // The word at p once its tag is `want` (tags only grow); after ~1 s gives up,
-// sets *err and returns what is there.
+// sets *err and returns what is there.  Once any wait of the step has given up
+// (the peer-timeout bit is in *err), later waits return at once: a rank that
+// never arrives costs one timeout per step, not one per awaited word.
 __device__ __forceinline__ uint32_t wait_tagged(const void* p, unsigned want, int* err) {
   uint2 v = ld_tagged(p);
   if ((int)(v.y - want) >= 0) return v.x;
+  const volatile int* verr = err;
+  if (*verr & SI_DEVERR_PEER_TIMEOUT) return v.x;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < (1u << 26); i++) {
     v = ld_tagged(p);
     if ((int)(v.y - want) >= 0) return v.x;
-    if ((i & 63u) == 63u && globaltimer_ns() - t0 > 1000000000ull) break;
+    if ((i & 63u) == 63u && ((*verr & SI_DEVERR_PEER_TIMEOUT) || globaltimer_ns() - t0 > 1000000000ull)) break;
   }
   atomicOr(err, SI_DEVERR_PEER_TIMEOUT);
   return v.x;

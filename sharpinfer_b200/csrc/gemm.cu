@@ -13,8 +13,10 @@
 //     [N][K] to a context scratch buffer: element = the reference's f32 value
 //     d*sc*q - dmin*m, rounded to f16 once.  si_qgemm_cache_weight keeps that
 //     copy for later calls.
-//  2. k_bf16_to_f16: X -> f16 (exact for |x| < 65504; kind::f16 needs A and
-//     B of one type, and f16 keeps 3 more mantissa bits of W than bf16).
+//  2. k_bf16_rows_to_f16: X -> f16, each row scaled by a power of two that
+//     puts its largest |x| in [2^14, 2^15) (undone in the epilogue), so the
+//     whole bf16 range converts without overflow; kind::f16 needs A and B of
+//     one type, and f16 keeps 3 more mantissa bits of W than bf16.
 //  3. k_gemm_tc: 128 x 256 output tile per CTA, K in steps of 64.  Warp 0
 //     issues TMA loads (128B-swizzled, 4-stage mbarrier ring), warp 1 issues
 //     tcgen05.mma (kind::f16, f32 accumulator in TMEM, 4 MMAs of K = 16 per
@@ -160,30 +162,63 @@ __global__ void __launch_bounds__(256) k_dequant_q4k_f16(const uint8_t* __restri
   }
 }
 
-__global__ void k_bf16_to_f16(const uint16_t* __restrict__ x, __half* __restrict__ y, int64_t n) {
-  const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+// Row m of X -> f16 scaled by 2^e_m, with e_m chosen so that the row's
+// largest |x| lands in [2^14, 2^15); rs[m] = 2^-e_m undoes the scale in the
+// GEMM epilogue.  Every product and f32 sum then carries the factor 2^e_m
+// exactly, so y is what unscaled f16 arithmetic would give -- but no bf16
+// value overflows f16 (|x| up to 3.4e38) and none below f16's normal range
+// (6.1e-5) loses bits unless it lies more than 2^28 under its row's maximum,
+// where its share of the row's products is below 2^-28 of the largest.
+__global__ void __launch_bounds__(256) k_bf16_rows_to_f16(const uint16_t* __restrict__ x, __half* __restrict__ y,
+                                                          float* __restrict__ rs, int K) {
+  __shared__ uint32_t red[8];
+  const int m = blockIdx.x, tid = threadIdx.x;
+  const uint4* xr = (const uint4*)(x + (int64_t)m * K);
+  uint4* yr = (uint4*)(y + (int64_t)m * K);
+  const int n8 = K / 8;  // K is a multiple of 64
   pdl_launch();
   pdl_wait();
-  if (i + 8 <= n) {
-    const uint4 v = *(const uint4*)(x + i);
+  // the largest magnitude from the bits: |x| orders like its bits with the sign cleared
+  uint32_t mb = 0;
+  for (int i = tid; i < n8; i += 256) {
+    const uint4 v = xr[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; k++) mb = max(mb, max(w[k] & 0x7FFFu, (w[k] >> 16) & 0x7FFFu));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xFFFFFFFFu, mb, o));
+  if ((tid & 31) == 0) red[tid >> 5] = mb;
+  __syncthreads();
+  mb = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) mb = max(mb, red[i]);
+  int e = 0;
+  if (mb != 0 && mb < 0x7F80u) {  // finite, non-zero maximum
+    const int E = (int)(mb >> 7) - 127;  // its binary exponent (bf16 subnormals count as 2^-127)
+    e = 14 - E;
+    e = e < -100 ? -100 : (e > 100 ? 100 : e);
+  }
+  const float sc = ldexpf(1.0f, e);
+  if (tid == 0) rs[m] = ldexpf(1.0f, -e);
+  for (int i = tid; i < n8; i += 256) {
+    const uint4 v = xr[i];
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; k++) {
-      const __half lo = __float2half_rn(__uint_as_float(w[k] << 16));
-      const __half hi = __float2half_rn(__uint_as_float(w[k] & 0xFFFF0000u));
+      const __half lo = __float2half_rn(__uint_as_float(w[k] << 16) * sc);
+      const __half hi = __float2half_rn(__uint_as_float(w[k] & 0xFFFF0000u) * sc);
       o[k] = (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
     }
-    *(uint4*)(y + i) = make_uint4(o[0], o[1], o[2], o[3]);
-  } else {
-    for (int64_t j = i; j < n; j++) y[j] = __float2half_rn(__uint_as_float((uint32_t)x[j] << 16));
+    yr[i] = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
 template <int GN>
 __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                     const __grid_constant__ CUtensorMap tmB, float* __restrict__ Y,
-                                                    int M, int N, int K, int* err) {
+                                                    const float* __restrict__ rs, int M, int N, int K, int* err) {
   constexpr int B_BYTES = GemmCfg<GN>::B_BYTES;
   constexpr uint32_t IDESC = GemmCfg<GN>::IDESC;
   extern __shared__ uint8_t smem_raw[];
@@ -228,7 +263,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     if (lane == 0) {  // MMA issuer
       for (int kt = 0; kt < nk; kt++) {
         const int s = kt % GST;
-        if (!mbar_wait_bounded(bars + 8 * s, (uint32_t)((kt / GST) & 1))) ok = false;
+        if (ok && !mbar_wait_bounded(bars + 8 * s, (uint32_t)((kt / GST) & 1))) ok = false;
         tc_fence_after();
         if (ok) {
           const uint64_t da = sdesc_k128(sA + s * A_BYTES), db = sdesc_k128(sB + s * B_BYTES);
@@ -250,6 +285,7 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
     const int q = warp & 3;
     const int row = m0 + 32 * q + lane;
     float* yr = Y + (int64_t)row * N;
+    const float rsc = row < M ? rs[row] : 0.f;  // the row's 2^-e
     for (int c0 = 0; c0 < GN; c0 += 32) {
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
@@ -258,12 +294,12 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       if (col0 + 32 <= N && (N & 3) == 0) {
 #pragma unroll
         for (int j = 0; j < 32; j += 4)
-          *(float4*)(yr + col0 + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                  __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+          *(float4*)(yr + col0 + j) = make_float4(__uint_as_float(r[j]) * rsc, __uint_as_float(r[j + 1]) * rsc,
+                                                  __uint_as_float(r[j + 2]) * rsc, __uint_as_float(r[j + 3]) * rsc);
       } else {
 #pragma unroll
         for (int j = 0; j < 32; j++)
-          if (col0 + j < N) yr[col0 + j] = __uint_as_float(r[j]);
+          if (col0 + j < N) yr[col0 + j] = __uint_as_float(r[j]) * rsc;
       }
     }
   }
@@ -299,7 +335,8 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t 
 
 template <int GN>
 __global__ void __launch_bounds__(320, 1) k_gemm_q4k(const __grid_constant__ CUtensorMap tmA, const uint8_t* __restrict__ W,
-                                                     int tiles, float* __restrict__ Y, int M, int N, int K, int* err) {
+                                                     int tiles, float* __restrict__ Y, const float* __restrict__ rs, int M,
+                                                     int N, int K, int* err) {
   constexpr int B_BYTES = GemmCfg<GN>::B_BYTES;
   constexpr uint32_t IDESC = GemmCfg<GN>::IDESC;
   constexpr int RT = GN / 128;  // row tiles per dequantising warp
@@ -466,6 +503,7 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q4k(const __grid_constant__ CUt
       const int q = warp & 3;
       const int row = m0 + 32 * q + lane;
       float* yr = Y + (int64_t)row * N;
+      const float rsc = row < M ? rs[row] : 0.f;  // the row's 2^-e
       for (int c0 = 0; c0 < GN; c0 += 32) {
         uint32_t r[32];
         tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, r);
@@ -474,12 +512,12 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q4k(const __grid_constant__ CUt
         if (col0 + 32 <= N && (N & 3) == 0) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
-            *(float4*)(yr + col0 + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                                                    __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+            *(float4*)(yr + col0 + j) = make_float4(__uint_as_float(r[j]) * rsc, __uint_as_float(r[j + 1]) * rsc,
+                                                    __uint_as_float(r[j + 2]) * rsc, __uint_as_float(r[j + 3]) * rsc);
         } else {
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            if (col0 + j < N) yr[col0 + j] = __uint_as_float(r[j]);
+            if (col0 + j < N) yr[col0 + j] = __uint_as_float(r[j]) * rsc;
         }
       }
     }
@@ -527,7 +565,8 @@ int dequant_f16(si_ctx* c, const si_weight* w, __half* dst) {
 int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int M) {
   const int64_t N = w->rows, K = w->cols;
   if (K % GK) SI_FAIL(SI_ERR_UNSUPPORTED, "qgemm: cols %lld not a multiple of %d", (long long)K, GK);
-  SI_TRY(ensure(c->stage[1], (size_t)M * K * 2));
+  const size_t xbytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
+  SI_TRY(ensure(c->stage[1], xbytes + (size_t)M * 4));
   __half* wf = (__half*)w->f16;
   // Q4_K without a cached copy: dequantised in shared memory while the row
   // blocks of X are few (each one dequantises W again; measured on the 8B
@@ -540,9 +579,9 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
     SI_TRY(dequant_f16(c, w, wf));
   }
   __half* xf = (__half*)c->stage[1].ptr;
-  const int64_t nx = (int64_t)M * K;
+  float* rs = (float*)((uint8_t*)c->stage[1].ptr + xbytes);  // per-row 2^-e of the conversion
   if (((uintptr_t)x & 15) != 0) SI_FAIL(SI_ERR_INVALID, "si_qgemm: x must be 16-byte aligned");
-  k_bf16_to_f16<<<(unsigned)((nx / 8 + 256) / 256), 256, 0, c->stream>>>(x, xf, nx);
+  k_bf16_rows_to_f16<<<(unsigned)M, 256, 0, c->stream>>>(x, xf, rs, (int)K);
   SI_CUDA(cudaGetLastError());
   // 256-wide tiles, or 128-wide when 256 would leave SMs idle
   const int64_t tiles256 = ((N + 255) / 256) * (((int64_t)M + GM - 1) / GM);
@@ -550,13 +589,13 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
   CUtensorMap ta, tb;
   SI_TRY(make_tmap(&ta, xf, M, K, GM));
   if (fused) {
-    static uint64_t fattr[2] = {0, 0};
+    static DeviceOnce fattr[2];
     const int fi = GN == 128 ? 0 : 1;
     const int fsmem = GN == 128 ? GemmCfg<128>::SMEM : GemmCfg<256>::SMEM;
-    if (c->device < 64 && !(fattr[fi] & (1ull << c->device))) {
+    if (!fattr[fi].done(c->device)) {
       if (GN == 128) SI_CUDA(cudaFuncSetAttribute(k_gemm_q4k<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, fsmem));
       else SI_CUDA(cudaFuncSetAttribute(k_gemm_q4k<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, fsmem));
-      fattr[fi] |= 1ull << c->device;
+      fattr[fi].mark(c->device);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)((N + GN - 1) / GN), (unsigned)((M + GM - 1) / GM));
@@ -570,19 +609,21 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
     cfg.numAttrs = 1;
     const uint8_t* wd = (const uint8_t*)w->dev;
     if (GN == 128)
-      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<128>, ta, wd, (int)w->tiles, y, M, (int)N, (int)K, c->dev_err));
+      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<128>, ta, wd, (int)w->tiles, y, (const float*)rs, M, (int)N, (int)K,
+                                 c->dev_err));
     else
-      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<256>, ta, wd, (int)w->tiles, y, M, (int)N, (int)K, c->dev_err));
+      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<256>, ta, wd, (int)w->tiles, y, (const float*)rs, M, (int)N, (int)K,
+                                 c->dev_err));
     return SI_OK;
   }
   SI_TRY(make_tmap(&tb, wf, N, K, GN));
-  static uint64_t attr_set[2] = {0, 0};
+  static DeviceOnce attr_set[2];
   const int ai = GN == 128 ? 0 : 1;
   const int smem = GN == 128 ? GemmCfg<128>::SMEM : GemmCfg<256>::SMEM;
-  if (c->device < 64 && !(attr_set[ai] & (1ull << c->device))) {
+  if (!attr_set[ai].done(c->device)) {
     if (GN == 128) SI_CUDA(cudaFuncSetAttribute(k_gemm_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     else SI_CUDA(cudaFuncSetAttribute(k_gemm_tc<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set[ai] |= 1ull << c->device;
+    attr_set[ai].mark(c->device);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((N + GN - 1) / GN), (unsigned)((M + GM - 1) / GM));
@@ -594,8 +635,10 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (GN == 128) SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<128>, ta, tb, y, M, (int)N, (int)K, c->dev_err));
-  else SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<256>, ta, tb, y, M, (int)N, (int)K, c->dev_err));
+  if (GN == 128)
+    SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<128>, ta, tb, y, (const float*)rs, M, (int)N, (int)K, c->dev_err));
+  else
+    SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<256>, ta, tb, y, (const float*)rs, M, (int)N, (int)K, c->dev_err));
   return SI_OK;
 }
 

@@ -279,6 +279,7 @@ struct si_model {
   uint8_t* peer_base[SI_TP_MAX] = {};      // every rank's buffer mapped here
   uint8_t** peers_dev = nullptr;           // the same table on the device
   bool connected = false;
+  bool ipc = false;                        // peers mapped through CUDA IPC (closed on free)
   unsigned epoch = 0;                      // steps taken (mirrors StepParams::epoch)
   int G = 0, qkv_rows = 0, Kmax = 0;
   int splits_max = 0, chunk_max = 0;
@@ -833,6 +834,36 @@ SI_EXPORT int si_model_tp_connect(si_model* m, const void* handles, int len) {
     }
     m->peer_base[r] = (uint8_t*)p;
   }
+  m->ipc = true;
+  SI_CUDA(cudaMemcpy(m->peers_dev, m->peer_base, SI_TP_MAX * sizeof(uint8_t*), cudaMemcpyHostToDevice));
+  m->connected = true;
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_tp_connect_local(si_model* m, si_model* const* ranks, int n) {
+  clear_error();
+  if (!m || !ranks) SI_FAIL(SI_ERR_INVALID, "si_model_tp_connect_local: NULL argument");
+  if (m->tp == 1 || n != m->tp) SI_FAIL(SI_ERR_INVALID, "si_model_tp_connect_local: need %d ranks", m->tp);
+  if (m->connected) SI_FAIL(SI_ERR_INVALID, "si_model_tp_connect_local: already connected");
+  for (int r = 0; r < n; r++) {
+    const si_model* o = ranks[r];
+    if (!o || o->tp != m->tp || o->rank != r || memcmp(&o->gcfg, &m->gcfg, sizeof(si_model_config)) != 0)
+      SI_FAIL(SI_ERR_INVALID, "si_model_tp_connect_local: entry %d is not rank %d of the same model", r, r);
+  }
+  SI_TRY(bind_device(m->c));
+  for (int r = 0; r < n; r++) {
+    const int pd = ranks[r]->c->device;
+    if (pd != m->c->device) {
+      int can = 0;
+      SI_CUDA(cudaDeviceCanAccessPeer(&can, m->c->device, pd));
+      if (!can) SI_FAIL(SI_ERR_UNSUPPORTED, "device %d cannot access device %d's memory", m->c->device, pd);
+      const cudaError_t e = cudaDeviceEnablePeerAccess(pd, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else if (e != cudaSuccess) SI_FAIL(SI_ERR_CUDA, "enabling access to device %d failed: %s", pd, cudaGetErrorString(e));
+    }
+    m->peer_base[r] = ranks[r]->comm;
+  }
+  m->ipc = false;
   SI_CUDA(cudaMemcpy(m->peers_dev, m->peer_base, SI_TP_MAX * sizeof(uint8_t*), cudaMemcpyHostToDevice));
   m->connected = true;
   return SI_OK;
@@ -844,7 +875,7 @@ SI_EXPORT int si_model_free(si_model* m) {
   cudaSetDevice(m->c->device);
   cudaStreamSynchronize(m->c->stream);
   for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
-  if (m->connected)
+  if (m->connected && m->ipc)
     for (int r = 0; r < m->tp; r++)
       if (r != m->rank && m->peer_base[r]) cudaIpcCloseMemHandle(m->peer_base[r]);
   for (auto* v : {&m->wqkv, &m->wo, &m->wgu, &m->wdown})

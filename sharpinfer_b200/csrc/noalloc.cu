@@ -50,26 +50,27 @@ struct DeviceScratch {
 };
 
 std::mutex g_setup_mu;
-DeviceScratch g_scratch[kMaxDevices];
+int g_sms[kMaxDevices];  // SM count per device, 0 until first asked
 
-// Once per device, with `dev` current: the array's device address and the SM
-// count.  This may load the module on the device, so the first call on a
-// device must not happen during stream capture.
+// With `dev` current: the array's device address and the SM count.  The
+// address is looked up on every call (a cheap runtime query), so it stays
+// right when the caller has reset the device or rebuilt its primary context
+// between calls.  The first lookup on a device may load the module there, so
+// the first call on a device must not happen during stream capture.
 int scratch_for(int dev, DeviceScratch* out) {
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess)
+    SI_FAIL(SI_ERR_CUDA, "si_qmatvec_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+            cudaGetErrorString(e));
+  out->base = (uint8_t*)p;
   std::lock_guard<std::mutex> lock(g_setup_mu);
-  DeviceScratch& d = g_scratch[dev];
-  if (!d.base) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess)
-      SI_FAIL(SI_ERR_CUDA, "si_qmatvec_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-              cudaGetErrorString(e));
+  if (!g_sms[dev]) {
     int sms = 0;
     SI_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    d.sms = sms;
-    d.base = (uint8_t*)p;
+    g_sms[dev] = sms;
   }
-  *out = d;
+  out->sms = g_sms[dev];
   return SI_OK;
 }
 

@@ -654,19 +654,25 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   float p0a = 0.f, p0b = 0.f, p1a = 0.f, p1b = 0.f;  // partials of the shared first / last tile
   bool has0 = false, has1 = false;
   bool ok = true;
-  uint32_t ph = 0;
+  // pend: stages with a copy in flight; par: the phase each completes next.
+  // After a wait gives up the warp issues nothing more and waits (bounded)
+  // only once on each stage still in flight.
+  uint32_t pend = (1u << pre) - 1u, par = 0u;
   int cT = c0T, cU = c0U;
   int left = min(nunit - c0U, total);  // units of the current tile in this range
   int tile_first = c0T * nunit;
-  for (int k0 = 0; k0 < total; k0 += NS) {
+  for (int k0 = 0; k0 < total && ok; k0 += NS) {
 #pragma unroll
     for (int s = 0; s < NS; s++) {
       if (k0 + s >= total) break;
-      if (!mbar_wait_bounded(bar0 + 8 * s, ph)) {  // waited even after a failure
-        if (ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar0 + 8 * s, (par >> s) & 1u))) {
+        if (lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
         ok = false;
+        break;
       }
-      if (ok) {
+      pend &= ~(1u << s);
+      par ^= 1u << s;
+      {
         const uint8_t* st = ring + s * SB;
         SmemLd ld[1];
         ld[0].w = st;
@@ -689,6 +695,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
         wsrc += wb;
         if (++iU == nunit) iU = 0;
         issued++;
+        pend |= 1u << s;
       }
       cU++;
       if (--left == 0) {
@@ -712,8 +719,8 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
         left = min(nunit, total - (k0 + s) - 1);
       }
     }
-    ph ^= 1u;
   }
+  if (!ok) mbar_drain(bar0, pend, par, NS);
   // ---- tiles shared between warps ----
   // Every warp has drained its ring; the ring memory now holds each warp's (at
   // most two) shared-tile partials.  The first contributor of a tile inside
@@ -970,7 +977,6 @@ __global__ void __launch_bounds__(NW * 32, 1)
   int cT = c0T;
   int cU = ub - c0T * nunit;  // even
   const bool first_partial = cU != 0;
-  uint32_t ph = 0;
 
   auto unit = [&](const uint8_t* st, int cu) {
     const uint8_t* xu = xs + cu * XB;
@@ -1016,24 +1022,32 @@ __global__ void __launch_bounds__(NW * 32, 1)
     tg8 += d1 * (sa1 * (C0[2] + C0[3]) + sb1 * (C1[2] + C1[3])) - dm1 * (Cm[2] + Cm[3]);
   };
 
-  for (int k0 = 0; k0 < npair; k0 += NS) {
+  // pend: stages with a copy in flight; par: the phase each completes next.
+  // After a wait gives up the warp issues nothing more and waits (bounded)
+  // only once on each stage still in flight.
+  uint32_t pend = (1u << pre) - 1u, par = 0u;
+  for (int k0 = 0; k0 < npair && ok; k0 += NS) {
 #pragma unroll
     for (int s = 0; s < NS; s++) {
       const int k = k0 + s;
       if (k >= npair) break;
-      if (!mbar_wait_bounded(bar0 + 8 * s, ph)) {  // waited even after a failure
-        if (ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
+      if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar0 + 8 * s, (par >> s) & 1u))) {
+        if (lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
         ok = false;
+        break;
       }
+      pend &= ~(1u << s);
+      par ^= 1u << s;
       uint8_t* st = ring + s * SB;
-      if (ok) {
-        unit(st, cU);
-        unit(st + TBB, cU + 1);
-      }
+      unit(st, cU);
+      unit(st + TBB, cU + 1);
       __syncwarp();
-      if (k + NS < npair && lane == 0) {  // refill this stage with pair k + NS
-        mbar_arrive_expect_tx(bar0 + 8 * s, SB);
-        bulk_g2s(smem_u32(st), wsrc + (int64_t)(k + NS) * SB, SB, bar0 + 8 * s);
+      if (k + NS < npair) {  // refill this stage with pair k + NS
+        if (lane == 0) {
+          mbar_arrive_expect_tx(bar0 + 8 * s, SB);
+          bulk_g2s(smem_u32(st), wsrc + (int64_t)(k + NS) * SB, SB, bar0 + 8 * s);
+        }
+        pend |= 1u << s;
       }
       cU += 2;
       if (cU == nunit) {  // this warp's part of tile cT is done
@@ -1050,8 +1064,8 @@ __global__ void __launch_bounds__(NW * 32, 1)
         cT++;
       }
     }
-    ph ^= 1u;
   }
+  if (!ok) mbar_drain(bar0, pend, par, NS);
   const int T1 = cT;
   if (cU != 0 && npair > 0) {  // the range ends inside tile cT
     const float a = red4(tg), b8 = red4(tg8);
@@ -1197,13 +1211,13 @@ int launch_warp_cfg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, fl
                     const ScratchCap& scr_cap, int sms, bool pdl) {
   using Cfg = WarpCfg<QT, B, NW, NS>;
   static_assert(Cfg::SMEM <= WARP_SMEM_MAX, "ring too large");
-  static uint64_t attr_set = 0;
+  static DeviceOnce attr_set;
   int dev = 0;
   SI_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !(attr_set & (1ull << dev))) {
+  if (!attr_set.done(dev)) {
     SI_CUDA(cudaFuncSetAttribute(k_qmv_warp<QT, EPI, B, NW, NS>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-    attr_set |= 1ull << dev;
+    attr_set.mark(dev);
   }
   const int64_t nunit = (w->nblk + Cfg::QPU - 1) / Cfg::QPU;
   const int64_t units = w->tiles * nunit;
@@ -1275,12 +1289,12 @@ int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y
   if (pmode == Q1_RMSNORM && (nunit * 256 > NW * 128 * 4 || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
   const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit, pmode);
   if ((nunit & 1) || P < NW || smem > 227 * 1024 || w->tiles * nunit >= (1 << 24)) return -1;
-  static uint64_t attr_set = 0;
+  static DeviceOnce attr_set;
   int dev = 0;
   SI_CUDA(cudaGetDevice(&dev));
-  if (dev < 64 && !(attr_set & (1ull << dev))) {
+  if (!attr_set.done(dev)) {
     SI_CUDA(cudaFuncSetAttribute(k_qmv1<EPI, NW, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    attr_set |= 1ull << dev;
+    attr_set.mark(dev);
   }
   // Tile mode gives every CTA whole row tiles: no partial sums cross CTAs,
   // at the price of up to one tile of imbalance.  Even-share mode balances

@@ -93,6 +93,11 @@ class DecodeModel:
     def tp_connect(self, handles):
         N.call("si_model_tp_connect", self.handle, handles, len(handles))
 
+    def tp_connect_local(self, ranks):
+        """Connect to the other ranks' models living in this process (rank order)."""
+        arr = (ctypes.c_void_p * len(ranks))(*[r.handle.value for r in ranks])
+        N.call("si_model_tp_connect_local", self.handle, arr, len(ranks))
+
     def free(self):
         if self.handle:
             N.call("si_model_free", self.handle)

@@ -74,6 +74,7 @@ _SIGS = {
     "si_model_create_tp": (_i32, [_c_p, ctypes.POINTER(ModelConfig), _i32, _i32, ctypes.POINTER(_c_p)]),
     "si_model_tp_handle": (_i32, [_c_p, _c_p, _i32]),
     "si_model_tp_connect": (_i32, [_c_p, _c_p, _i32]),
+    "si_model_tp_connect_local": (_i32, [_c_p, ctypes.POINTER(_c_p), _i32]),
     "si_tp_slice": (_i32, [ctypes.POINTER(ModelConfig), _i32, _i32, _i32] + [ctypes.POINTER(ctypes.c_int64)] * 5),
     "si_decode_step_kernels": (_i32, [_c_p, _i32, ctypes.POINTER(_i32)]),
     "cuda_init": (_c_p, [_i32]),
