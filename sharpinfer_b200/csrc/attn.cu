@@ -28,6 +28,7 @@
 // waiting for the kernel that produces q.
 #include "common.cuh"
 #include "model.cuh"
+#include "prepfmt.cuh"
 
 namespace si {
 namespace {
@@ -69,6 +70,79 @@ struct AttnSmem {
   __host__ __device__ size_t bars() const { return (stat() + (2 * G + 2) * 4 + 7) & ~(size_t)7; }
   __host__ __device__ size_t total() const { return bars() + AT_NS * 8; }
 };
+
+// The last CTA of (sequence b, kv head kvh) to finish merges the S splits of
+// its G heads -- the softmax of Transformer.cs:99-129 over all positions:
+// M = max_s m_s, w_s = exp(m_s - M), o = sum_s w_s o_s / sum_s w_s l_s --
+// and packs the G * 128 merged values (G / 2 whole 256-column units) as the
+// O projection's prepared input.  Every CTA's partials are made visible
+// (fence) before it counts itself in; the order of the sums is fixed, so the
+// result does not depend on which CTA merges.  smem: the K/V ring, idle by now.
+template <int G>
+__device__ __forceinline__ void attn_merge_last(const AttnArgs& a, uint8_t* smem, int b, int kvh, int S) {
+  __shared__ int is_last;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __threadfence();
+  __syncthreads();
+  int* cnt = a.merge_cnt + b * gridDim.y + kvh;
+  if (tid == 0) is_last = atomicAdd(cnt, 1) == S - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  static_assert(8 * SI_ATTN_MAX_SPLITS * 4 <= 16384 && 16640 + 8 * HD * 4 <= AT_NS * AT_STAGE, "merge scratch");
+  float* wts = (float*)smem;                        // [G][S] merge weights
+  float* inv = (float*)(smem + 16384);              // [G] 1 / sum_s w_s l_s
+  float* sv = (float*)(smem + 16640);               // [G][128] merged values (16-byte aligned)
+  const int64_t hb = (int64_t)b * a.nh + kvh * G;   // first head of the group, this sequence
+  for (int h = warp; h < G; h += AT_WARPS) {
+    const float2* ml = (const float2*)a.part_ml + (hb + h) * S;
+    float M = -INFINITY;
+    for (int s = lane; s < S; s += 32) M = fmaxf(M, __ldcg(ml + s).x);
+    M = warp_max(M);
+    float den = 0.f;
+    for (int s = lane; s < S; s += 32) {
+      const float2 v = __ldcg(ml + s);
+      const float w = v.x == -INFINITY ? 0.f : expf(v.x - M);
+      wts[h * SI_ATTN_MAX_SPLITS + s] = w;
+      den = fmaf(w, v.y, den);
+    }
+    den = warp_sum(den);
+    if (lane == 0) inv[h] = 1.0f / den;
+  }
+  __syncthreads();
+  for (int i = tid; i < G * 32; i += blockDim.x) {  // (head, 4 dims) per thread
+    const int h = i >> 5, d4 = i & 31;
+    const float4* po = (const float4*)(a.part_o + (hb + h) * S * HD) + d4;
+    const float* wh = wts + h * SI_ATTN_MAX_SPLITS;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < S; s0 += 16) {  // 16 partial outputs in flight
+      float4 o[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+        if (s0 + j < S) o[j] = __ldcg(po + (int64_t)(s0 + j) * (HD / 4));
+#pragma unroll
+      for (int j = 0; j < 16; j++)
+        if (s0 + j < S) {
+          const float w = wh[s0 + j];
+          acc.x = fmaf(w, o[j].x, acc.x);
+          acc.y = fmaf(w, o[j].y, acc.y);
+          acc.z = fmaf(w, o[j].z, acc.z);
+          acc.w = fmaf(w, o[j].w, acc.w);
+        }
+    }
+    const float r = inv[h];
+    const float4 v = make_float4(acc.x * r, acc.y * r, acc.z * r, acc.w * r);
+    *(float4*)(sv + h * HD + 4 * d4) = v;
+    if (a.out) *(float4*)(a.out + (hb + h) * HD + 4 * d4) = v;
+  }
+  __syncthreads();
+  // prepared units: the group's heads cover units kvh * G / 2 .. + G / 2 - 1
+  const int B = gridDim.z, nunit = a.nh * HD / 256, mg = b >> 2, cb = b & 3;
+  const int LW = 8 * min(4, B - 4 * mg);
+  for (int u = warp; u < G / 2; u += AT_WARPS)
+    pack_unit_warp(sv + 256 * u, a.xprep + xprep_off(mg, nunit, kvh * (G / 2) + u, LW), LW, cb, lane);
+  if (tid == 0) *cnt = 0;
+}
 
 template <int G>
 __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
@@ -338,6 +412,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
     a.part_ml[(pbase + (int64_t)tid * S) * 2 + 1] = stat[2 * tid + 1];
   }
   if (!ok && tid == 0) atomicOr(a.err, SI_DEVERR_WAIT_TIMEOUT);
+  if (G >= 2 && a.merge_cnt) attn_merge_last<G>(a, smem, b, kvh, S);
 }
 
 }  // namespace

@@ -231,6 +231,9 @@ int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
 // prepared-activation buffer.
 int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const float* nw, float eps, float* y,
                    int epi, const QmvBuffers& qb, uint8_t* xprep, bool pdl);
+// y (op)= W (SiLU(gate) * up) for one row (batch 1).
+int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const float* up, float* y, int epi,
+                    const QmvBuffers& qb, uint8_t* xprep, bool pdl);
 int launch_synth_blocks(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma,
                         int64_t blk0, int64_t nblocks, uint8_t* dst);
 int launch_synth_blocks_2d(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma, int64_t grow0,

@@ -294,6 +294,7 @@ struct si_model {
   int* argmax = nullptr;
   uint8_t* xprep = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
+  int* merge_cnt = nullptr;  // [max_batch][kv heads] CTAs of the attention kernel done (merge in the kernel)
   StepParams* dparams = nullptr;
   StepParams* hparams = nullptr;  // pinned
   int* hargmax = nullptr;         // pinned
@@ -467,8 +468,15 @@ int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int 
   a.part_o = m->part_o;
   a.part_ml = m->part_ml;
   a.err = m->c->dev_err;
+  if (m->G >= 2) {  // the last CTA of each kv head merges and packs the O-projection input
+    a.merge_cnt = m->merge_cnt;
+    a.xprep = m->xprep;
+    a.out = out;
+    return launch_attn(m->c->stream, a, m->G, S, B, c.n_kv_heads, pdl);
+  }
   SI_TRY(launch_attn(m->c->stream, a, m->G, S, B, c.n_kv_heads, pdl));
-  // merge the splits into the O-projection's prepared input (and into `out`)
+  // one q head per kv head: a 256-column unit spans two kv heads, so a
+  // separate kernel merges the splits into the prepared input (and `out`)
   return launch_prep(m->c->stream, m->part_o, S, m->part_ml, nullptr, 0.f, SI_PREP_ATTN_MERGE,
                      c.n_heads * c.head_dim, B, out, m->xprep, pdl);
 }
@@ -546,10 +554,18 @@ int enqueue_step(si_model* m, int B) {
                             m->xprep, true));
     else
       SI_TRY(launch_qmv(s, m->wgu[l], m->xprep, B, m->gu, SI_EPI_STORE, qb, true));
-    SI_TRY(launch_prep(s, m->gu, 2 * inter, m->gu + inter, nullptr, 0.f, SI_PREP_SILU_MUL, inter, B, nullptr,
-                       m->xprep, true));
-    if (tp) SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, nullptr, SI_EPI_TP, tp_producer(m, l, 1), true));
-    else SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
+    if (B == 1) {  // SiLU(gate) * up inside the down-projection matvec where the kernel allows
+      if (tp)
+        SI_TRY(launch_qmv_silu(s, m->wdown[l], m->gu, m->gu + inter, nullptr, SI_EPI_TP, tp_producer(m, l, 1),
+                               m->xprep, true));
+      else
+        SI_TRY(launch_qmv_silu(s, m->wdown[l], m->gu, m->gu + inter, m->x, SI_EPI_ADD, qb, m->xprep, true));
+    } else {
+      SI_TRY(launch_prep(s, m->gu, 2 * inter, m->gu + inter, nullptr, 0.f, SI_PREP_SILU_MUL, inter, B, nullptr,
+                         m->xprep, true));
+      if (tp) SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, nullptr, SI_EPI_TP, tp_producer(m, l, 1), true));
+      else SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
+    }
   }
   if (tp) {
     const PrepTp pt = tp_consumer(m, c.n_layers - 1, 1);
@@ -763,11 +779,13 @@ SI_EXPORT int si_model_create_tp(si_ctx* ctx, const si_model_config* cfg, int tp
   ALLOC(xprep, xprep_bytes(m->Kmax, B));
   ALLOC(part_o, (size_t)B * c.n_heads * m->splits_max * c.head_dim * 4);
   ALLOC(part_ml, (size_t)B * c.n_heads * m->splits_max * 2 * 4);
+  ALLOC(merge_cnt, (size_t)B * c.n_kv_heads * 4);
   ALLOC(dparams, sizeof(StepParams));
 #undef ALLOC
   cudaError_t e = cudaMemset(m->kcache, 0, kv_elems * 2);
   if (e == cudaSuccess && m->comm) e = cudaMemset(m->comm, 0, SI_TP_SLOTS + (size_t)2 * tp * B * h * 8);
   if (e == cudaSuccess) e = cudaMemset(m->vcache, 0, kv_elems * 2);
+  if (e == cudaSuccess) e = cudaMemset(m->merge_cnt, 0, (size_t)B * c.n_kv_heads * 4);
   if (e == cudaSuccess) e = cudaMallocHost(&m->hparams, sizeof(StepParams));
   if (e == cudaSuccess) e = cudaMallocHost(&m->hargmax, sizeof(int) * SI_MAX_BATCH);
   if (e != cudaSuccess) {

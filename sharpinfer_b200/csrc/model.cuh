@@ -29,6 +29,13 @@ struct AttnArgs {
   float* part_o;      // [batch][nh][splits][head_dim]
   float* part_ml;     // [batch][nh][splits][2]
   int* err;
+  // Merge in the kernel (G >= 2): the last CTA of each (sequence, kv head) to
+  // finish merges the splits of its G heads and packs them as prepared
+  // O-projection input.  merge_cnt [max_batch][kv heads] counts finished
+  // CTAs (zero between launches; the merging CTA resets it).
+  int* merge_cnt = nullptr;
+  uint8_t* xprep = nullptr;  // prepared-activation buffer of the O projection
+  float* out = nullptr;      // optional f32 copy of the merged output [batch][nh * head_dim]
 };
 
 // KV cache rows are 128 f16 (256 B).  The 16-byte chunk c (dims 8c..8c+7) of

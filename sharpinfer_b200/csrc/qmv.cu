@@ -820,14 +820,16 @@ struct Q1Cfg {
   __host__ __device__ static size_t part_off(int NW, int NS, int nunit) { return red_off(NW, NS, nunit) + 256; }
   static size_t smem(int NW, int NS, int nunit, int pmode) {
     const size_t part = (size_t)NW * 2 * 64 * 4;
-    const size_t stage = pmode == 1 ? (size_t)nunit * 256 * 4 : 0;
+    const size_t stage = pmode == 1 ? (size_t)nunit * 256 * 4 : pmode == 2 ? (size_t)NW * 256 * 4 : 0;
     return part_off(NW, NS, nunit) + (part > stage ? part : stage);
   }
 };
 
 // Input preparation of a k_qmv1 launch: 0 = prepared units copied from
 // xprep, 1 = RmsNorm of x (q1_rms_prep).
-enum { Q1_PREPARED = 0, Q1_RMSNORM = 1 };
+// 2 = SiLU(gate) * up of two f32 inputs (q1_silu_prep).
+enum { Q1_PREPARED = 0, Q1_RMSNORM = 1, Q1_SILU = 2 };
+constexpr int Q1_SILU_MAX_UNITS = 64;  // 4 units per warp of 16
 
 // Fused RmsNorm + activation preparation of a batch-1 k_qmv1 launch: every
 // CTA normalises the whole input x (K <= 8192 columns, 4 x 16-byte loads per
@@ -874,6 +876,44 @@ __device__ __forceinline__ void q1_rms_prep(const float* __restrict__ xf, const 
   __syncthreads();
   for (int u = warp; u < nunit; u += NW)  // one warp per 256-column unit
     pack_unit_warp(stage + 256 * u, xs + u * XB, 8, 0, lane);
+  __syncthreads();
+}
+
+// Fused SiLU * up + activation preparation of a batch-1 k_qmv1 launch (the
+// down projection's input): v = SiLU(gate) * up (TensorOps.SiLU then
+// MulInPlace, TensorOps.cs:191-195, :169-185, in k_prep's arithmetic), one
+// warp per 256-column unit with all of the warp's loads (<= 4 units) issued
+// before any is used; each unit is packed exactly as k_prep does.  stage:
+// 1 KB per warp.
+template <int NW>
+__device__ __forceinline__ void q1_silu_prep(const float* __restrict__ gate, const float* __restrict__ up, int nunit,
+                                             float* stage, uint8_t* xs) {
+  constexpr int XB = Q1Cfg::XB, MAXU = Q1_SILU_MAX_UNITS / NW;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sv = stage + warp * 256;
+  float4 g[MAXU][2], u[MAXU][2];
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int un = warp + NW * i;
+#pragma unroll
+    for (int j = 0; j < 2; j++) {
+      g[i][j] = un < nunit ? __ldcg((const float4*)(gate + 256 * un) + 2 * lane + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+      u[i][j] = un < nunit ? __ldcg((const float4*)(up + 256 * un) + 2 * lane + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  auto sm = [](float gv, float uv) { return __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, expf(-gv))), uv); };
+#pragma unroll
+  for (int i = 0; i < MAXU; i++) {
+    const int un = warp + NW * i;
+    if (un >= nunit) break;
+#pragma unroll
+    for (int j = 0; j < 2; j++)
+      *(float4*)(sv + 8 * lane + 4 * j) = make_float4(sm(g[i][j].x, u[i][j].x), sm(g[i][j].y, u[i][j].y),
+                                                      sm(g[i][j].z, u[i][j].z), sm(g[i][j].w, u[i][j].w));
+    __syncwarp();
+    pack_unit_warp(sv, xs + un * XB, 8, 0, lane);
+    __syncwarp();
+  }
   __syncthreads();
 }
 
@@ -945,7 +985,9 @@ __global__ void __launch_bounds__(NW * 32, 1)
   }
   pdl_wait();
   bool ok = true;
-  if (pmode != Q1_PREPARED) {
+  if (pmode == Q1_SILU) {  // xf: gate, nw: up
+    q1_silu_prep<NW>(xf, nw, nunit, (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
+  } else if (pmode != Q1_PREPARED) {
     q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
                     (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
   } else {
@@ -1287,6 +1329,8 @@ int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y
   const int64_t P = w->tiles * nunit / 2;
   // the fused RmsNorm holds K <= 8192 in registers, read 16 bytes at a time
   if (pmode == Q1_RMSNORM && (nunit * 256 > NW * 128 * 4 || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
+  // the fused SiLU * up keeps at most 4 units per warp in registers
+  if (pmode == Q1_SILU && (nunit > Q1_SILU_MAX_UNITS || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
   const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit, pmode);
   if ((nunit & 1) || P < NW || smem > 227 * 1024 || w->tiles * nunit >= (1 << 24)) return -1;
   static DeviceOnce attr_set;
@@ -1390,6 +1434,23 @@ int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const flo
     if (r >= 0) return r;
   }
   SI_TRY(launch_prep(s, x, (int)w->cols, nullptr, nw, eps, SI_PREP_RMSNORM, (int)w->cols, 1, nullptr, xprep, pdl));
+  return launch_qmv(s, w, xprep, 1, y, epi, qb, pdl);
+}
+
+// y (op)= W (SiLU(gate) * up) for one row (batch 1): the batch-1 Q4_K kernel
+// computes and prepares its input itself; otherwise k_prep does it first.
+int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const float* up, float* y, int epi,
+                    const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
+  if (w->qtype == SI_Q4_K) {
+    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp}, qb.split_bytes, qb.count_n};
+    int r = -1;
+    if (epi == SI_EPI_ADD) r = launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
+    else if (epi == SI_EPI_STORE) r = launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
+    else if (epi == SI_EPI_TP) r = launch_q1<SI_EPI_TP>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
+    if (r >= 0) return r;
+  }
+  const int K = (int)w->cols;
+  SI_TRY(launch_prep(s, gate, K, up, nullptr, 0.f, SI_PREP_SILU_MUL, K, 1, nullptr, xprep, pdl));
   return launch_qmv(s, w, xprep, 1, y, epi, qb, pdl);
 }
 
