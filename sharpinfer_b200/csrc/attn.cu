@@ -183,6 +183,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   __syncthreads();
   // ring items: K sub-chunks 0..nsub-1, then V sub-chunks 0..nsub-1
   const int items = 2 * nsub;
+  const uint64_t pol = l2_evict_first_policy();  // the cache is read once per step
   auto issue = [&](int it) {
     const int st = it % AT_NS;
     const int sub = it < nsub ? it : it - nsub;
@@ -191,10 +192,11 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
     const int np = min(AT_SUB, t1 - p0);
     const uint32_t bytes = (uint32_t)np * HD * 2;
     mbar_arrive_expect_tx(bar0 + 8 * st, bytes);
-    bulk_g2s(smem_u32(ring + st * AT_STAGE), base + (int64_t)p0 * HD, bytes, bar0 + 8 * st);
+    bulk_g2s_ef(smem_u32(ring + st * AT_STAGE), base + (int64_t)p0 * HD, bytes, bar0 + 8 * st, pol);
   };
   if (tid == 0 && !appends)
     for (int it = 0; it < min(items, AT_NS); it++) issue(it);
+  l2_prefetch_share(a.pf);
   pdl_wait();
   const float* qkv = a.qkv + (int64_t)b * a.qkv_ld;
   const float2* rope = (const float2*)(a.rope + (int64_t)pos * HD);  // [HD/2] (cos, sin)

@@ -79,6 +79,14 @@ struct PrepTp {
   int64_t src_stride = 0;           // bytes between source ranks' slots
   int ld = 0;                       // elements per batch row
 };
+// A range of device memory to pull into L2 ahead of the kernel that will read
+// it (cp.async.bulk.prefetch.L2): a kernel whose own bytes are already in L2,
+// or whose critical path is latency rather than bytes, keeps HBM busy with the
+// next kernel's weights.  ptr 16-byte aligned, bytes a multiple of 16, < 4 GB.
+struct L2Prefetch {
+  const uint8_t* ptr = nullptr;
+  uint32_t bytes = 0;
+};
 // Device scratch of the streaming matvec: partial sums of row tiles split
 // between warps ([tiles][slots][64] f32) and per-tile arrival counters
 // ([tiles] int, zero between launches).
@@ -90,6 +98,7 @@ struct QmvBuffers {
   int* err;
   int sms;
   TpArgs tp;  // used by the SI_EPI_TP epilogue
+  L2Prefetch pf;  // weights of a later kernel, pulled into L2 at launch
 };
 // CTAs (of nw warps) of the streaming matvec for `units` 16x256 units.
 inline int64_t qmv_warp_grid(int64_t units, int nw, int sms) {
@@ -151,7 +160,7 @@ struct si_ctx {
   si_devbuf qmv_count;                // and their counters (zero between launches)
   si::QmvBuffers qmv() const {
     return si::QmvBuffers{(float*)qmv_split.ptr, qmv_split.bytes, (int*)qmv_count.ptr,
-                          (int64_t)(qmv_count.bytes / 4), dev_err, sm_count, si::TpArgs{}};
+                          (int64_t)(qmv_count.bytes / 4), dev_err, sm_count, si::TpArgs{}, si::L2Prefetch{}};
   }
   // Host-pointer entry points: device staging and pinned host staging.
   si_devbuf stage[4];
@@ -366,6 +375,37 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
+}
+// The same copy with an L2 evict-first hint: for bytes read exactly once per
+// step (weights, KV cache), so that streaming them does not push out lines
+// prefetched for the next kernel.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void bulk_g2s_ef(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
+                                            uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
+// This CTA's share of an L2 prefetch: the range split evenly over the grid
+// (16-byte granules), issued by one thread in pieces of at most 64 KB.
+// 32-bit arithmetic (a 64-bit division is a long subroutine).
+__device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& p) {
+  if (!p.ptr || threadIdx.x != 0) return;
+  const uint32_t nct = gridDim.x * gridDim.y * gridDim.z;
+  const uint32_t cid = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const uint32_t g16 = p.bytes >> 4, per = (g16 + nct - 1) / nct;
+  const uint32_t a = min(g16, cid * per), b = min(g16, a + per);
+  for (uint32_t o = a; o < b; o += 4096) {
+    const uint32_t n = min(4096u, b - o);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.ptr + ((uint64_t)o << 4)), "r"(n << 4)
+                 : "memory");
+  }
 }
 __device__ __forceinline__ uint4 lds_v4(uint32_t a) {
   uint4 r;

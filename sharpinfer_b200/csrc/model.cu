@@ -14,6 +14,7 @@
 //   qmv    Wdown, accumulated into x                              (:151-154)
 // then RmsNorm(x) * final_norm, lm_head -> logits, ArgMax.         (:158-159)
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -265,6 +266,38 @@ float recipe_sigma(int qt, int recipe, int64_t cols) {
   return 1.0f / (73.9f * rc);  // Q8_0: rms of a uniform int8 is ~73.9
 }
 
+// Layout choices of the decode step (all give the same results):
+//   SI_PLAN_MERGE_IN_ATTN  the last attention CTA of each kv head merges the
+//                          splits and packs the O projection's input (G >= 2)
+//                          instead of a separate merge kernel
+//   SI_PLAN_SILU_IN_DOWN   the batch-1 down-projection matvec computes
+//                          SiLU(gate) * up itself instead of a separate kernel
+//   SI_PLAN_L2_PREFETCH    each kernel pulls the weights of the kernel two
+//                          launches later into L2
+enum : unsigned { SI_PLAN_MERGE_IN_ATTN = 1, SI_PLAN_SILU_IN_DOWN = 2, SI_PLAN_L2_PREFETCH = 4 };
+constexpr unsigned SI_PLAN_DEFAULT = SI_PLAN_L2_PREFETCH;
+
+// The plan: SHARPINFER_B200_STEP_PLAN (a comma-separated subset of "merge",
+// "silu", "prefetch", or "none") when set, else SI_PLAN_DEFAULT.
+unsigned step_plan() {
+  const char* e = getenv("SHARPINFER_B200_STEP_PLAN");
+  if (!e) return SI_PLAN_DEFAULT;
+  unsigned p = 0;
+  if (strstr(e, "merge")) p |= SI_PLAN_MERGE_IN_ATTN;
+  if (strstr(e, "silu")) p |= SI_PLAN_SILU_IN_DOWN;
+  if (strstr(e, "prefetch")) p |= SI_PLAN_L2_PREFETCH;
+  return p;
+}
+
+L2Prefetch pf_of(const si_weight* w) {
+  L2Prefetch p;
+  if (w && w->bytes < (1ull << 32)) {
+    p.ptr = (const uint8_t*)w->dev;
+    p.bytes = (uint32_t)(w->bytes & ~(size_t)15);
+  }
+  return p;
+}
+
 }  // namespace
 }  // namespace si
 
@@ -295,6 +328,7 @@ struct si_model {
   uint8_t* xprep = nullptr;
   float *part_o = nullptr, *part_ml = nullptr;
   int* merge_cnt = nullptr;  // [max_batch][kv heads] CTAs of the attention kernel done (merge in the kernel)
+  unsigned plan = 0;         // SI_PLAN_* bits: how the decode step is laid out
   StepParams* dparams = nullptr;
   StepParams* hparams = nullptr;  // pinned
   int* hargmax = nullptr;         // pinned
@@ -449,7 +483,8 @@ int attn_splits(const si_model* m, int B) {
   return std::min(std::max(want, need), m->splits_max);
 }
 
-int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int B, bool pdl) {
+int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int B, bool pdl,
+                      L2Prefetch pf = L2Prefetch{}) {
   const si_model_config& c = m->cfg;
   AttnArgs a;
   a.params = m->dparams;
@@ -468,7 +503,8 @@ int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int 
   a.part_o = m->part_o;
   a.part_ml = m->part_ml;
   a.err = m->c->dev_err;
-  if (m->G >= 2) {  // the last CTA of each kv head merges and packs the O-projection input
+  a.pf = pf;
+  if (m->G >= 2 && (m->plan & SI_PLAN_MERGE_IN_ATTN)) {  // the last CTA of each kv head merges and packs
     a.merge_cnt = m->merge_cnt;
     a.xprep = m->xprep;
     a.out = out;
@@ -515,16 +551,26 @@ PrepTp tp_consumer(si_model* m, int layer, int kind) {
 int enqueue_step(si_model* m, int B) {
   const si_model_config& c = m->cfg;
   cudaStream_t s = m->c->stream;
-  const int h = c.hidden, inter = c.intermediate;
+  const int h = c.hidden, inter = c.intermediate, L = c.n_layers;
   const bool tp = m->tp > 1;
+  const bool pre = (m->plan & SI_PLAN_L2_PREFETCH) != 0;
   const QmvBuffers qb = m->c->qmv();
+  // Each kernel may prefetch into L2 the weights of the kernel two launches
+  // later: gate/up(l) -> qkv(l+1), down(l) -> Wo(l+1), attention(l) ->
+  // gate/up(l), Wo(l) -> down(l).
+  auto with_pf = [&](QmvBuffers q, const si_weight* w) {
+    if (pre && w) q.pf = pf_of(w);
+    return q;
+  };
   {
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = cfg_of(s, dim3((h + 255) / 256, B), dim3(256), 0, false, attr);
     SI_CUDA(cudaLaunchKernelEx(&cfg, k_embed, (const StepParams*)m->dparams, m->emb->qtype,
                                (const uint8_t*)m->emb->dev, m->emb->nblk, (int64_t)m->emb->rows, h, m->x));
   }
-  for (int l = 0; l < c.n_layers; l++) {
+  for (int l = 0; l < L; l++) {
+    const si_weight* qkv_next = l + 1 < L ? m->wqkv[l + 1] : nullptr;
+    const si_weight* wo_next = l + 1 < L ? m->wo[l + 1] : nullptr;
     if (tp && l > 0) {
       const PrepTp pt = tp_consumer(m, l - 1, 1);
       SI_TRY(launch_prep(s, m->x2, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
@@ -537,34 +583,38 @@ int enqueue_step(si_model* m, int B) {
                          nullptr, m->xprep, true));
     }
     if (tp || B > 1) SI_TRY(launch_qmv(s, m->wqkv[l], m->xprep, B, m->qkv, SI_EPI_STORE, qb, true));
-    SI_TRY(enqueue_attention(m, l, m->qkv, nullptr, B, true));
+    SI_TRY(enqueue_attention(m, l, m->qkv, nullptr, B, true, pre ? pf_of(m->wgu[l]) : L2Prefetch{}));
     if (tp) {
-      SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, nullptr, SI_EPI_TP, tp_producer(m, l, 0), true));
+      SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, nullptr, SI_EPI_TP, with_pf(tp_producer(m, l, 0), m->wdown[l]),
+                        true));
       const PrepTp pt = tp_consumer(m, l, 0);
       SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
                          m->x2, m->xprep, true, &pt));
     } else {
-      SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
+      SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, m->x, SI_EPI_ADD, with_pf(qb, m->wdown[l]), true));
       if (B > 1)
         SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
                            nullptr, m->xprep, true));
     }
     if (!tp && B == 1)
-      SI_TRY(launch_qmv_rms(s, m->wgu[l], m->x, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, m->gu, SI_EPI_STORE, qb,
-                            m->xprep, true));
+      SI_TRY(launch_qmv_rms(s, m->wgu[l], m->x, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, m->gu, SI_EPI_STORE,
+                            with_pf(qb, qkv_next), m->xprep, true));
     else
-      SI_TRY(launch_qmv(s, m->wgu[l], m->xprep, B, m->gu, SI_EPI_STORE, qb, true));
-    if (B == 1) {  // SiLU(gate) * up inside the down-projection matvec where the kernel allows
+      SI_TRY(launch_qmv(s, m->wgu[l], m->xprep, B, m->gu, SI_EPI_STORE, with_pf(qb, qkv_next), true));
+    if (B == 1 && (m->plan & SI_PLAN_SILU_IN_DOWN)) {  // SiLU(gate) * up inside the down-projection matvec
       if (tp)
-        SI_TRY(launch_qmv_silu(s, m->wdown[l], m->gu, m->gu + inter, nullptr, SI_EPI_TP, tp_producer(m, l, 1),
-                               m->xprep, true));
+        SI_TRY(launch_qmv_silu(s, m->wdown[l], m->gu, m->gu + inter, nullptr, SI_EPI_TP,
+                               with_pf(tp_producer(m, l, 1), wo_next), m->xprep, true));
       else
-        SI_TRY(launch_qmv_silu(s, m->wdown[l], m->gu, m->gu + inter, m->x, SI_EPI_ADD, qb, m->xprep, true));
+        SI_TRY(launch_qmv_silu(s, m->wdown[l], m->gu, m->gu + inter, m->x, SI_EPI_ADD, with_pf(qb, wo_next),
+                               m->xprep, true));
     } else {
       SI_TRY(launch_prep(s, m->gu, 2 * inter, m->gu + inter, nullptr, 0.f, SI_PREP_SILU_MUL, inter, B, nullptr,
                          m->xprep, true));
-      if (tp) SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, nullptr, SI_EPI_TP, tp_producer(m, l, 1), true));
-      else SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, m->x, SI_EPI_ADD, qb, true));
+      if (tp)
+        SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, nullptr, SI_EPI_TP, with_pf(tp_producer(m, l, 1), wo_next),
+                          true));
+      else SI_TRY(launch_qmv(s, m->wdown[l], m->xprep, B, m->x, SI_EPI_ADD, with_pf(qb, wo_next), true));
     }
   }
   if (tp) {
@@ -724,6 +774,7 @@ SI_EXPORT int si_model_create_tp(si_ctx* ctx, const si_model_config* cfg, int tp
   m->cfg = *cfg;
   m->tp = tp;
   m->rank = rank;
+  m->plan = step_plan();
   m->cfg.n_heads /= tp;
   m->cfg.n_kv_heads /= tp;
   m->cfg.intermediate /= tp;

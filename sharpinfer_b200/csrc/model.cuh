@@ -36,6 +36,7 @@ struct AttnArgs {
   int* merge_cnt = nullptr;
   uint8_t* xprep = nullptr;  // prepared-activation buffer of the O projection
   float* out = nullptr;      // optional f32 copy of the merged output [batch][nh * head_dim]
+  L2Prefetch pf;             // a later kernel's weights, prefetched into L2 at launch
 };
 
 // KV cache rows are 128 f16 (256 B).  The 16-byte chunk c (dims 8c..8c+7) of

@@ -541,6 +541,7 @@ struct QmvScratch {
   int* err;      // device error word
   int maxc;      // contributor slots per tile
   TpArgs tp;     // SI_EPI_TP: peer slots and flags
+  L2Prefetch pf; // a later kernel's weights, prefetched into L2 at launch
 };
 
 template <int QT, int B, int NW, int NS>
@@ -621,17 +622,19 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   const uint8_t* wsrc = W + ((int64_t)c0T * nblk + (int64_t)c0U * QPU) * TBB;
   int iU = c0U;                      // unit index (in its tile) of the next copy to issue
   const int pre = total < NS ? total : NS;
+  const uint64_t pol = l2_evict_first_policy();  // weights are read once per step
   if (lane == 0) {
     const uint8_t* p = wsrc;
     int u = c0U;
     for (int s = 0; s < pre; s++) {
       const uint32_t wb = (uint32_t)(min(QPU, nblk - u * QPU) * TBB);
       mbar_expect_tx(bar0 + 8 * s, wb);
-      bulk_g2s(ring_s + s * SB, p, wb, bar0 + 8 * s);
+      bulk_g2s_ef(ring_s + s * SB, p, wb, bar0 + 8 * s, pol);
       p += wb;
       if (++u == nunit) u = 0;
     }
   }
+  l2_prefetch_share(scr.pf);
   pdl_launch();  // dependents may start their independent prologue now
   pdl_wait();
   if (lane == 0) {
@@ -689,7 +692,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
         const uint32_t wb = (uint32_t)(min(QPU, nblk - iU * QPU) * TBB);
         if (lane == 0) {
           mbar_arrive_expect_tx(bar0 + 8 * s, wb + XB);
-          bulk_g2s(ring_s + s * SB, wsrc, wb, bar0 + 8 * s);
+          bulk_g2s_ef(ring_s + s * SB, wsrc, wb, bar0 + 8 * s, pol);
           bulk_g2s(ring_s + s * SB + WB, xprep + (int64_t)iU * XB, XB, bar0 + 8 * s);
         }
         wsrc += wb;
@@ -968,10 +971,12 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // activation loads delay them (the loads wait behind up to one stage per
   // warp of weight bytes instead of the whole ring).
   const int pre = npair < NS ? npair : NS;
+  const uint64_t pol = l2_evict_first_policy();  // weights are read once per step
   if (lane == 0 && pre > 0) {
     mbar_arrive_expect_tx(bar0, SB);
-    bulk_g2s(smem_u32(ring), wsrc, SB, bar0);
+    bulk_g2s_ef(smem_u32(ring), wsrc, SB, bar0, pol);
   }
+  l2_prefetch_share(scr.pf);
   pdl_launch();  // dependents may start their independent prologue now
   // pmode: prepared units in xprep, or the f32 input xf normalised here
   // with weights nw
@@ -1001,7 +1006,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
   if (lane == 0)
     for (int s = 1; s < pre; s++) {
       mbar_arrive_expect_tx(bar0 + 8 * s, SB);
-      bulk_g2s(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s);
+      bulk_g2s_ef(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s, pol);
     }
 
   // per-lane constants
@@ -1087,7 +1092,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
       if (k + NS < npair) {  // refill this stage with pair k + NS
         if (lane == 0) {
           mbar_arrive_expect_tx(bar0 + 8 * s, SB);
-          bulk_g2s(smem_u32(st), wsrc + (int64_t)(k + NS) * SB, SB, bar0 + 8 * s);
+          bulk_g2s_ef(smem_u32(st), wsrc + (int64_t)(k + NS) * SB, SB, bar0 + 8 * s, pol);
         }
         pend |= 1u << s;
       }
@@ -1427,7 +1432,7 @@ int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const 
 int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const float* nw, float eps, float* y,
                    int epi, const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
   if (w->qtype == SI_Q4_K && (epi == SI_EPI_STORE || epi == SI_EPI_ADD)) {
-    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp}, qb.split_bytes, qb.count_n};
+    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf}, qb.split_bytes, qb.count_n};
     const int r = epi == SI_EPI_ADD
                       ? launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM, x, nw, eps)
                       : launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM, x, nw, eps);
@@ -1442,7 +1447,7 @@ int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const flo
 int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const float* up, float* y, int epi,
                     const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
   if (w->qtype == SI_Q4_K) {
-    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp}, qb.split_bytes, qb.count_n};
+    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf}, qb.split_bytes, qb.count_n};
     int r = -1;
     if (epi == SI_EPI_ADD) r = launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
     else if (epi == SI_EPI_STORE) r = launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
@@ -1456,7 +1461,7 @@ int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const
 
 int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
                const QmvBuffers& qb, bool pdl) {
-  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp}, qb.split_bytes, qb.count_n};
+  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf}, qb.split_bytes, qb.count_n};
   if (epi == SI_EPI_ADD) return dispatch_qt<SI_EPI_ADD>(s, w, xprep, B, y, scr, qb.sms, pdl);
   if (epi == SI_EPI_TP) {
     if (qb.tp.tp < 1 || !qb.tp.peers || !qb.tp.epoch) SI_FAIL(SI_ERR_INVALID, "qmatvec: tensor-parallel epilogue without peers");
