@@ -392,20 +392,19 @@ __device__ __forceinline__ void bulk_g2s_ef(uint32_t dst, const void* src, uint3
       "l"(src), "r"(bytes), "r"(bar), "l"(pol)
       : "memory");
 }
-// This CTA's share of an L2 prefetch: the range split evenly over the grid
-// (16-byte granules), issued by one thread in pieces of at most 64 KB.
-// 32-bit arithmetic (a 64-bit division is a long subroutine).
+// This CTA's share of an L2 prefetch: the range split evenly over the grid,
+// one prefetch.global.L2 per 128-byte line spread over the CTA's threads.
+// Plain load-unit hints, so they never queue ahead of the CTA's own bulk
+// copies on the TMA engine.  32-bit arithmetic (a 64-bit division is a long
+// subroutine).
 __device__ __forceinline__ void l2_prefetch_share(const L2Prefetch& p) {
-  if (!p.ptr || threadIdx.x != 0) return;
+  if (!p.ptr) return;
   const uint32_t nct = gridDim.x * gridDim.y * gridDim.z;
   const uint32_t cid = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-  const uint32_t g16 = p.bytes >> 4, per = (g16 + nct - 1) / nct;
-  const uint32_t a = min(g16, cid * per), b = min(g16, a + per);
-  for (uint32_t o = a; o < b; o += 4096) {
-    const uint32_t n = min(4096u, b - o);
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.ptr + ((uint64_t)o << 4)), "r"(n << 4)
-                 : "memory");
-  }
+  const uint32_t lines = p.bytes >> 7, per = (lines + nct - 1) / nct;
+  const uint32_t a = min(lines, cid * per), b = min(lines, a + per);
+  for (uint32_t l = a + threadIdx.x; l < b; l += blockDim.x)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p.ptr + ((uint64_t)l << 7)));
 }
 __device__ __forceinline__ uint4 lds_v4(uint32_t a) {
   uint4 r;

@@ -970,12 +970,17 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // rest once the activations are in: requests queued ahead of the
   // activation loads delay them (the loads wait behind up to one stage per
   // warp of weight bytes instead of the whole ring).
+  // The whole ring is requested before the dependency wait, so HBM streams
+  // this CTA's first weights while the producer of the activations finishes
+  // and while they are prepared; the activations themselves come through
+  // ordinary loads, never queued behind these bulk copies.
   const int pre = npair < NS ? npair : NS;
   const uint64_t pol = l2_evict_first_policy();  // weights are read once per step
-  if (lane == 0 && pre > 0) {
-    mbar_arrive_expect_tx(bar0, SB);
-    bulk_g2s_ef(smem_u32(ring), wsrc, SB, bar0, pol);
-  }
+  if (lane == 0)
+    for (int s = 0; s < pre; s++) {
+      mbar_arrive_expect_tx(bar0 + 8 * s, SB);
+      bulk_g2s_ef(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s, pol);
+    }
   l2_prefetch_share(scr.pf);
   pdl_launch();  // dependents may start their independent prologue now
   // pmode: prepared units in xprep, or the f32 input xf normalised here
@@ -996,18 +1001,24 @@ __global__ void __launch_bounds__(NW * 32, 1)
     q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
                     (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
   } else {
-    if (threadIdx.x == 0) {
-      mbar_arrive_expect_tx(bar_x, (uint32_t)(nunit * XB));
-      bulk_g2s(smem_u32(xs), xprep, (uint32_t)(nunit * XB), bar_x);
+    // prepared units (nunit * XB bytes, a multiple of 16), 16 bytes per load
+    // with up to four loads in flight per thread
+    const int n16 = nunit * XB / 16;
+    for (int i0 = threadIdx.x; i0 < n16; i0 += 4 * NW * 32) {
+      uint4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int i = i0 + j * NW * 32;
+        if (i < n16) v[j] = __ldcg((const uint4*)xprep + i);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int i = i0 + j * NW * 32;
+        if (i < n16) ((uint4*)xs)[i] = v[j];
+      }
     }
-    ok = mbar_wait_bounded(bar_x, 0);
-    if (!ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
+    __syncthreads();
   }
-  if (lane == 0)
-    for (int s = 1; s < pre; s++) {
-      mbar_arrive_expect_tx(bar0 + 8 * s, SB);
-      bulk_g2s_ef(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s, pol);
-    }
 
   // per-lane constants
   const int cls = lane >> 3;                                   // MMA column class
