@@ -99,6 +99,8 @@ struct QmvBuffers {
   int sms;
   TpArgs tp;  // used by the SI_EPI_TP epilogue
   L2Prefetch pf;  // weights of a later kernel, pulled into L2 at launch
+  int self_pf;    // batch-1 matvec: own weights into L2 at launch, ring after the input
+  int q1w;        // batch-1 matvec: warps per CTA (16 or 8)
 };
 // CTAs (of nw warps) of the streaming matvec for `units` 16x256 units.
 inline int64_t qmv_warp_grid(int64_t units, int nw, int sms) {
@@ -160,7 +162,7 @@ struct si_ctx {
   si_devbuf qmv_count;                // and their counters (zero between launches)
   si::QmvBuffers qmv() const {
     return si::QmvBuffers{(float*)qmv_split.ptr, qmv_split.bytes, (int*)qmv_count.ptr,
-                          (int64_t)(qmv_count.bytes / 4), dev_err, sm_count, si::TpArgs{}, si::L2Prefetch{}};
+                          (int64_t)(qmv_count.bytes / 4), dev_err, sm_count, si::TpArgs{}, si::L2Prefetch{}, 0, 16};
   }
   // Host-pointer entry points: device staging and pinned host staging.
   si_devbuf stage[4];

@@ -274,8 +274,16 @@ float recipe_sigma(int qt, int recipe, int64_t cols) {
 //                          SiLU(gate) * up itself instead of a separate kernel
 //   SI_PLAN_L2_PREFETCH    each kernel pulls the weights of the kernel two
 //                          launches later into L2
-enum : unsigned { SI_PLAN_MERGE_IN_ATTN = 1, SI_PLAN_SILU_IN_DOWN = 2, SI_PLAN_L2_PREFETCH = 4 };
-constexpr unsigned SI_PLAN_DEFAULT = SI_PLAN_L2_PREFETCH;
+//   SI_PLAN_SELF_PREFETCH  each batch-1 matvec CTA pulls its own weights into
+//                          L2 at launch and fills its shared-memory ring once
+//                          its input is prepared
+//   SI_PLAN_Q1_8WARPS      batch-1 matvec CTAs of 8 warps instead of 16, so a
+//                          CTA of the following kernel fits beside one
+enum : unsigned {
+  SI_PLAN_MERGE_IN_ATTN = 1, SI_PLAN_SILU_IN_DOWN = 2, SI_PLAN_L2_PREFETCH = 4, SI_PLAN_SELF_PREFETCH = 8,
+  SI_PLAN_Q1_8WARPS = 16
+};
+constexpr unsigned SI_PLAN_DEFAULT = 0;
 
 // The plan: SHARPINFER_B200_STEP_PLAN (a comma-separated subset of "merge",
 // "silu", "prefetch", or "none") when set, else SI_PLAN_DEFAULT.
@@ -285,7 +293,9 @@ unsigned step_plan() {
   unsigned p = 0;
   if (strstr(e, "merge")) p |= SI_PLAN_MERGE_IN_ATTN;
   if (strstr(e, "silu")) p |= SI_PLAN_SILU_IN_DOWN;
-  if (strstr(e, "prefetch")) p |= SI_PLAN_L2_PREFETCH;
+  if (strstr(e, "prefetch") && !strstr(e, "selfprefetch")) p |= SI_PLAN_L2_PREFETCH;
+  if (strstr(e, "selfprefetch")) p |= SI_PLAN_SELF_PREFETCH;
+  if (strstr(e, "w8")) p |= SI_PLAN_Q1_8WARPS;
   return p;
 }
 
@@ -522,6 +532,8 @@ int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int 
 // and of its consumer, the RmsNorm prep that adds the partial sums.
 QmvBuffers tp_producer(si_model* m, int layer, int kind) {
   QmvBuffers qb = m->c->qmv();
+  qb.self_pf = (m->plan & SI_PLAN_SELF_PREFETCH) ? 1 : 0;
+  qb.q1w = (m->plan & SI_PLAN_Q1_8WARPS) ? 8 : 16;
   const int64_t slot = (int64_t)m->cfg.max_batch * m->cfg.hidden * 8;
   qb.tp = TpArgs{m->peers_dev, &m->dparams->epoch, m->tp, m->rank, kind, 2 * layer + kind + 1,
                  2 * m->cfg.n_layers, SI_TP_SLOTS + (int64_t)kind * m->tp * slot + (int64_t)m->rank * slot,
@@ -554,7 +566,9 @@ int enqueue_step(si_model* m, int B) {
   const int h = c.hidden, inter = c.intermediate, L = c.n_layers;
   const bool tp = m->tp > 1;
   const bool pre = (m->plan & SI_PLAN_L2_PREFETCH) != 0;
-  const QmvBuffers qb = m->c->qmv();
+  QmvBuffers qb = m->c->qmv();
+  qb.self_pf = (m->plan & SI_PLAN_SELF_PREFETCH) ? 1 : 0;
+  qb.q1w = (m->plan & SI_PLAN_Q1_8WARPS) ? 8 : 16;
   // Each kernel may prefetch into L2 the weights of the kernel two launches
   // later: gate/up(l) -> qkv(l+1), down(l) -> Wo(l+1), attention(l) ->
   // gate/up(l), Wo(l) -> down(l).

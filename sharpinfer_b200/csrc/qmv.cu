@@ -542,6 +542,9 @@ struct QmvScratch {
   int maxc;      // contributor slots per tile
   TpArgs tp;     // SI_EPI_TP: peer slots and flags
   L2Prefetch pf; // a later kernel's weights, prefetched into L2 at launch
+  int self_pf;   // k_qmv1: prefetch the CTA's own weights into L2 at launch and
+                 // fill the ring only after the input is prepared
+  int q1w;       // k_qmv1 warps per CTA (16, or 8)
 };
 
 template <int QT, int B, int NW, int NS>
@@ -891,7 +894,7 @@ __device__ __forceinline__ void q1_rms_prep(const float* __restrict__ xf, const 
 template <int NW>
 __device__ __forceinline__ void q1_silu_prep(const float* __restrict__ gate, const float* __restrict__ up, int nunit,
                                              float* stage, uint8_t* xs) {
-  constexpr int XB = Q1Cfg::XB, MAXU = Q1_SILU_MAX_UNITS / NW;
+  constexpr int XB = Q1Cfg::XB, MAXU = 4;  // units per warp (the launcher caps nunit at 4 NW)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* sv = stage + warp * 256;
   float4 g[MAXU][2], u[MAXU][2];
@@ -929,7 +932,7 @@ __device__ __forceinline__ float red4(float v) {
 __device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float(bits) - 8388608.f; }
 
 template <int EPI, int NW, int NS>
-__global__ void __launch_bounds__(NW * 32, 1)
+__global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
     k_qmv1(const uint8_t* __restrict__ W, int nunit, int64_t rows, int tiles, int tile_mode,
            int pmode, const uint8_t* __restrict__ xprep, const float* __restrict__ xf, const float* __restrict__ nw,
            float eps, float* __restrict__ y, QmvScratch scr) {
@@ -976,11 +979,24 @@ __global__ void __launch_bounds__(NW * 32, 1)
   // ordinary loads, never queued behind these bulk copies.
   const int pre = npair < NS ? npair : NS;
   const uint64_t pol = l2_evict_first_policy();  // weights are read once per step
-  if (lane == 0)
-    for (int s = 0; s < pre; s++) {
-      mbar_arrive_expect_tx(bar0 + 8 * s, SB);
-      bulk_g2s_ef(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s, pol);
-    }
+  auto issue_ring = [&]() {
+    if (lane == 0)
+      for (int s = 0; s < pre; s++) {
+        mbar_arrive_expect_tx(bar0 + 8 * s, SB);
+        bulk_g2s_ef(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s, pol);
+      }
+  };
+  if (scr.self_pf) {
+    // the warp's whole (contiguous) weight range into L2 now; the ring is
+    // filled from there once the input is ready, so the input's loads do not
+    // queue behind weight bytes entering the SM
+    if (lane == 0)
+      for (uint32_t o = 0, n = (uint32_t)npair * SB; o < n; o += 65536u)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(wsrc + o), "r"(min(65536u, n - o))
+                     : "memory");
+  } else {
+    issue_ring();
+  }
   l2_prefetch_share(scr.pf);
   pdl_launch();  // dependents may start their independent prologue now
   // pmode: prepared units in xprep, or the f32 input xf normalised here
@@ -1020,6 +1036,7 @@ __global__ void __launch_bounds__(NW * 32, 1)
     __syncthreads();
   }
 
+  if (scr.self_pf) issue_ring();
   // per-lane constants
   const int cls = lane >> 3;                                   // MMA column class
   const int xl = (lane & 7) * 16;                              // fragment slot in a group
@@ -1336,17 +1353,16 @@ int launch_reg(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
 // Batch-1 Q4_K launch; returns -1 when the shape does not suit k_qmv1 (odd
 // number of column units, too few unit pairs, or activations too large to
 // keep resident in shared memory).
-template <int EPI>
-int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y, const ScratchCap& scr, int sms,
-              bool pdl, int pmode = Q1_PREPARED, const float* xf = nullptr, const float* nw = nullptr,
-              float eps = 0.f) {
-  constexpr int NW = 16, NS = 2;
+template <int EPI, int NW>
+int launch_q1_nw(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y, const ScratchCap& scr, int sms,
+                 bool pdl, int pmode, const float* xf, const float* nw, float eps) {
+  constexpr int NS = 2;
   const int64_t nunit = w->nblk;
   const int64_t P = w->tiles * nunit / 2;
-  // the fused RmsNorm holds K <= 8192 in registers, read 16 bytes at a time
+  // the fused RmsNorm holds K <= NW * 512 in registers, read 16 bytes at a time
   if (pmode == Q1_RMSNORM && (nunit * 256 > NW * 128 * 4 || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
-  // the fused SiLU * up keeps at most 4 units per warp in registers
-  if (pmode == Q1_SILU && (nunit > Q1_SILU_MAX_UNITS || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
+  // the fused SiLU * up keeps at most 4 units per warp of 16 in registers
+  if (pmode == Q1_SILU && (nunit > Q1_SILU_MAX_UNITS * NW / 16 || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
   const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit, pmode);
   if ((nunit & 1) || P < NW || smem > 227 * 1024 || w->tiles * nunit >= (1 << 24)) return -1;
   static DeviceOnce attr_set;
@@ -1381,6 +1397,16 @@ int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y
   SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv1<EPI, NW, NS>, (const uint8_t*)w->dev, (int)nunit, w->rows, (int)tiles,
                              tile_mode, pmode, xprep, xf, nw, eps, y, q));
   return SI_OK;
+}
+
+// 16 warps per CTA (one CTA fills an SM), or 8 (half the registers and the
+// shared-memory ring, so a CTA of the next kernel can share the SM).
+template <int EPI>
+int launch_q1(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float* y, const ScratchCap& scr, int sms,
+              bool pdl, int pmode = Q1_PREPARED, const float* xf = nullptr, const float* nw = nullptr,
+              float eps = 0.f) {
+  if (scr.scr.q1w == 8) return launch_q1_nw<EPI, 8>(s, w, xprep, y, scr, sms, pdl, pmode, xf, nw, eps);
+  return launch_q1_nw<EPI, 16>(s, w, xprep, y, scr, sms, pdl, pmode, xf, nw, eps);
 }
 
 template <int QT, int EPI>
@@ -1443,7 +1469,7 @@ int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const 
 int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const float* nw, float eps, float* y,
                    int epi, const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
   if (w->qtype == SI_Q4_K && (epi == SI_EPI_STORE || epi == SI_EPI_ADD)) {
-    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf}, qb.split_bytes, qb.count_n};
+    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.self_pf, qb.q1w}, qb.split_bytes, qb.count_n};
     const int r = epi == SI_EPI_ADD
                       ? launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM, x, nw, eps)
                       : launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM, x, nw, eps);
@@ -1458,7 +1484,7 @@ int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const flo
 int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const float* up, float* y, int epi,
                     const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
   if (w->qtype == SI_Q4_K) {
-    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf}, qb.split_bytes, qb.count_n};
+    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.self_pf, qb.q1w}, qb.split_bytes, qb.count_n};
     int r = -1;
     if (epi == SI_EPI_ADD) r = launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
     else if (epi == SI_EPI_STORE) r = launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
@@ -1472,7 +1498,7 @@ int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const
 
 int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
                const QmvBuffers& qb, bool pdl) {
-  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf}, qb.split_bytes, qb.count_n};
+  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.self_pf, qb.q1w}, qb.split_bytes, qb.count_n};
   if (epi == SI_EPI_ADD) return dispatch_qt<SI_EPI_ADD>(s, w, xprep, B, y, scr, qb.sms, pdl);
   if (epi == SI_EPI_TP) {
     if (qb.tp.tp < 1 || !qb.tp.peers || !qb.tp.epoch) SI_FAIL(SI_ERR_INVALID, "qmatvec: tensor-parallel epilogue without peers");
