@@ -168,8 +168,14 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   // before the producer of q has finished.
   const int pos = a.params->pos;
   const int len = pos + 1;
-  const int chunk = (len + S - 1) / S;
-  const int t0 = s_idx * chunk, t1 = min(len, t0 + chunk);
+  // The last split holds only the newest (up to) 16 positions, the one being
+  // appended among them: the CTA that stores position pos copies its K/V only
+  // after that store, so it gets the least to copy.  The other splits share
+  // the rest evenly.
+  const int tail = S > 1 ? min(16, len) : len;
+  const int chunk = S > 1 ? (len - tail + S - 2) / (S - 1) : len;
+  const int t0 = s_idx == S - 1 ? len - tail : s_idx * chunk;
+  const int t1 = s_idx == S - 1 ? len : min(len - tail, t0 + chunk);
   const int n = max(0, t1 - t0);
   const int nsub = (n + AT_SUB - 1) / AT_SUB;
   const bool appends = t1 == len && n > 0;  // this split stores position pos

@@ -99,7 +99,7 @@ struct QmvBuffers {
   int sms;
   TpArgs tp;  // used by the SI_EPI_TP epilogue
   L2Prefetch pf;  // weights of a later kernel, pulled into L2 at launch
-  int self_pf;    // batch-1 matvec: own weights into L2 at launch, ring after the input
+  int ring_mode;  // batch-1 matvec: when its shared-memory ring is filled (0, 1, 2)
   int q1w;        // batch-1 matvec: warps per CTA (16 or 8)
 };
 // CTAs (of nw warps) of the streaming matvec for `units` 16x256 units.

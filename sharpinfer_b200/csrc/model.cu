@@ -274,6 +274,8 @@ float recipe_sigma(int qt, int recipe, int64_t cols) {
 //                          SiLU(gate) * up itself instead of a separate kernel
 //   SI_PLAN_L2_PREFETCH    each kernel pulls the weights of the kernel two
 //                          launches later into L2
+//   SI_PLAN_FULL_RING      each batch-1 matvec CTA requests its whole
+//                          shared-memory ring before waiting for its input
 //   SI_PLAN_SELF_PREFETCH  each batch-1 matvec CTA pulls its own weights into
 //                          L2 at launch and fills its shared-memory ring once
 //                          its input is prepared
@@ -281,7 +283,7 @@ float recipe_sigma(int qt, int recipe, int64_t cols) {
 //                          CTA of the following kernel fits beside one
 enum : unsigned {
   SI_PLAN_MERGE_IN_ATTN = 1, SI_PLAN_SILU_IN_DOWN = 2, SI_PLAN_L2_PREFETCH = 4, SI_PLAN_SELF_PREFETCH = 8,
-  SI_PLAN_Q1_8WARPS = 16
+  SI_PLAN_Q1_8WARPS = 16, SI_PLAN_FULL_RING = 32
 };
 constexpr unsigned SI_PLAN_DEFAULT = 0;
 
@@ -296,6 +298,7 @@ unsigned step_plan() {
   if (strstr(e, "prefetch") && !strstr(e, "selfprefetch")) p |= SI_PLAN_L2_PREFETCH;
   if (strstr(e, "selfprefetch")) p |= SI_PLAN_SELF_PREFETCH;
   if (strstr(e, "w8")) p |= SI_PLAN_Q1_8WARPS;
+  if (strstr(e, "fullring")) p |= SI_PLAN_FULL_RING;
   return p;
 }
 
@@ -471,8 +474,8 @@ int check_config(const si_model_config* c) {
   const int G = c->n_heads / c->n_kv_heads;
   if (G != 1 && G != 2 && G != 4 && G != 8) SI_FAIL(SI_ERR_UNSUPPORTED, "%d q heads per kv head", G);
   if (c->max_batch < 1 || c->max_batch > SI_MAX_BATCH) SI_FAIL(SI_ERR_INVALID, "max_batch %d outside 1..16", c->max_batch);
-  // split-KV attention: at most 511 splits of at most 1024 positions
-  if (c->max_seq > 511 * 1024) SI_FAIL(SI_ERR_UNSUPPORTED, "max_seq %d above %d", c->max_seq, 511 * 1024);
+  // split-KV attention: at most 511 splits of at most 1024 positions (the last holds 16)
+  if (c->max_seq > 510 * 1024) SI_FAIL(SI_ERR_UNSUPPORTED, "max_seq %d above %d", c->max_seq, 510 * 1024);
   for (int qt : {c->weight_qtype, c->lm_head_qtype, c->emb_qtype})
     if (qt != SI_Q4_K && qt != SI_Q6_K && qt != SI_Q8_0) SI_FAIL(SI_ERR_UNSUPPORTED, "quant type %d", qt);
   auto blk = [](int qt) { return qt == SI_Q8_0 ? 32 : 256; };
@@ -489,7 +492,7 @@ int check_config(const si_model_config* c) {
 // and at most 1024 positions per split at the longest context.
 int attn_splits(const si_model* m, int B) {
   const int want = (2 * m->c->sm_count + B * m->cfg.n_kv_heads - 1) / (B * m->cfg.n_kv_heads);
-  const int need = (m->cfg.max_seq + 1023) / 1024;
+  const int need = (m->cfg.max_seq + 1023) / 1024 + 1;  // the last split holds 16 positions
   return std::min(std::max(want, need), m->splits_max);
 }
 
@@ -509,7 +512,8 @@ int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int 
   a.rope = m->rope;
   a.scale = 1.0f / sqrtf((float)c.head_dim);  // Transformer.cs:101
   const int S = attn_splits(m, B);
-  a.chunk_max = (c.max_seq + S - 1) / S;
+  // all but the last split share the positions before the newest 16
+  a.chunk_max = S > 1 ? (c.max_seq + S - 2) / (S - 1) : c.max_seq;
   a.part_o = m->part_o;
   a.part_ml = m->part_ml;
   a.err = m->c->dev_err;
@@ -532,7 +536,7 @@ int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int 
 // and of its consumer, the RmsNorm prep that adds the partial sums.
 QmvBuffers tp_producer(si_model* m, int layer, int kind) {
   QmvBuffers qb = m->c->qmv();
-  qb.self_pf = (m->plan & SI_PLAN_SELF_PREFETCH) ? 1 : 0;
+  qb.ring_mode = (m->plan & SI_PLAN_SELF_PREFETCH) ? 2 : (m->plan & SI_PLAN_FULL_RING) ? 1 : 0;
   qb.q1w = (m->plan & SI_PLAN_Q1_8WARPS) ? 8 : 16;
   const int64_t slot = (int64_t)m->cfg.max_batch * m->cfg.hidden * 8;
   qb.tp = TpArgs{m->peers_dev, &m->dparams->epoch, m->tp, m->rank, kind, 2 * layer + kind + 1,
@@ -567,7 +571,7 @@ int enqueue_step(si_model* m, int B) {
   const bool tp = m->tp > 1;
   const bool pre = (m->plan & SI_PLAN_L2_PREFETCH) != 0;
   QmvBuffers qb = m->c->qmv();
-  qb.self_pf = (m->plan & SI_PLAN_SELF_PREFETCH) ? 1 : 0;
+  qb.ring_mode = (m->plan & SI_PLAN_SELF_PREFETCH) ? 2 : (m->plan & SI_PLAN_FULL_RING) ? 1 : 0;
   qb.q1w = (m->plan & SI_PLAN_Q1_8WARPS) ? 8 : 16;
   // Each kernel may prefetch into L2 the weights of the kernel two launches
   // later: gate/up(l) -> qkv(l+1), down(l) -> Wo(l+1), attention(l) ->
@@ -819,7 +823,8 @@ SI_EXPORT int si_model_create_tp(si_ctx* ctx, const si_model_config* cfg, int tp
   if (st != SI_OK) return fail(st);
   const int64_t h = c.hidden;
   const size_t kv_elems = (size_t)c.n_layers * B * c.n_kv_heads * c.max_seq * c.head_dim;
-  m->splits_max = std::min(511, std::max((2 * ctx->sm_count + c.n_kv_heads - 1) / c.n_kv_heads, (c.max_seq + 1023) / 1024));
+  m->splits_max = std::min(511, std::max((2 * ctx->sm_count + c.n_kv_heads - 1) / c.n_kv_heads,
+                                         (c.max_seq + 1023) / 1024 + 1));
   m->chunk_max = 1024;
   void* p;
 #define ALLOC(field, bytes)                                      \

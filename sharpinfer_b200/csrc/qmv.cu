@@ -77,6 +77,14 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
   if (mode == 3) {
     const int S = ldx, nhd = K / 128;
     const int warp = tid >> 5, lane = tid & 31;
+    // this thread's first partial outputs are requested before the statistics,
+    // so both arrive in one round trip
+    constexpr int PRE = 48;
+    const int hl0 = tid >> 7, d0 = tid & 127;
+    const float* po0 = x + ((int64_t)b * nhd + 2 * u + hl0) * S * 128 + d0;
+    float o0[PRE];
+#pragma unroll
+    for (int j = 0; j < PRE; j++) o0[j] = (k < K && j < S) ? po0[(int64_t)j * 128] : 0.f;
     if (warp < 2 && 2 * u + warp < nhd) {  // statistics of head 2u + warp
       const float2* ml = (const float2*)x2 + ((int64_t)b * nhd + 2 * u + warp) * S;
       float2 pv[(SI_ATTN_MAX_SPLITS + 32) / 32];  // all of this lane's (max, sum) pairs in one round trip
@@ -102,11 +110,15 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
     }
     __syncthreads();
     if (k < K) {
-      const int hl = tid >> 7, h = 2 * u + hl, d = tid & 127;
-      const float* po = x + ((int64_t)b * nhd + h) * S * 128 + d;
-      const float* wh = mw[hl];
+      const float* po = po0;
+      const float* wh = mw[hl0];
       float n0 = 0.f, n1 = 0.f;
-      for (int s0 = 0; s0 < S; s0 += 32) {  // 32 partial outputs in flight
+#pragma unroll
+      for (int j = 0; j < PRE; j += 2) {
+        if (j < S) n0 = fmaf(wh[j], o0[j], n0);
+        if (j + 1 < S) n1 = fmaf(wh[j + 1], o0[j + 1], n1);
+      }
+      for (int s0 = PRE; s0 < S; s0 += 32) {  // the rest, 32 partial outputs in flight
         float o[32];
 #pragma unroll
         for (int j = 0; j < 32; j++)
@@ -542,8 +554,7 @@ struct QmvScratch {
   int maxc;      // contributor slots per tile
   TpArgs tp;     // SI_EPI_TP: peer slots and flags
   L2Prefetch pf; // a later kernel's weights, prefetched into L2 at launch
-  int self_pf;   // k_qmv1: prefetch the CTA's own weights into L2 at launch and
-                 // fill the ring only after the input is prepared
+  int ring_mode; // k_qmv1: when the ring is filled (see the kernel)
   int q1w;       // k_qmv1 warps per CTA (16, or 8)
 };
 
@@ -973,29 +984,30 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   // rest once the activations are in: requests queued ahead of the
   // activation loads delay them (the loads wait behind up to one stage per
   // warp of weight bytes instead of the whole ring).
-  // The whole ring is requested before the dependency wait, so HBM streams
-  // this CTA's first weights while the producer of the activations finishes
-  // and while they are prepared; the activations themselves come through
-  // ordinary loads, never queued behind these bulk copies.
+  // When the ring is filled (scr.ring_mode):
+  //  0  one stage per warp before the dependency wait, the rest once the input
+  //     is prepared: bulk copies queued ahead of the input's own copy delay it
+  //  1  the whole ring before the dependency wait; prepared input through
+  //     ordinary loads
+  //  2  the warp's whole weight range prefetched into L2 before the wait, the
+  //     ring filled once the input is prepared (ordinary loads for it)
   const int pre = npair < NS ? npair : NS;
   const uint64_t pol = l2_evict_first_policy();  // weights are read once per step
-  auto issue_ring = [&]() {
+  const int rmode = scr.ring_mode;
+  auto issue_stages = [&](int s0, int s1) {
     if (lane == 0)
-      for (int s = 0; s < pre; s++) {
+      for (int s = s0; s < s1; s++) {
         mbar_arrive_expect_tx(bar0 + 8 * s, SB);
         bulk_g2s_ef(smem_u32(ring + s * SB), wsrc + s * SB, SB, bar0 + 8 * s, pol);
       }
   };
-  if (scr.self_pf) {
-    // the warp's whole (contiguous) weight range into L2 now; the ring is
-    // filled from there once the input is ready, so the input's loads do not
-    // queue behind weight bytes entering the SM
+  if (rmode == 2) {
     if (lane == 0)
       for (uint32_t o = 0, n = (uint32_t)npair * SB; o < n; o += 65536u)
         asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(wsrc + o), "r"(min(65536u, n - o))
                      : "memory");
   } else {
-    issue_ring();
+    issue_stages(0, rmode == 1 ? pre : min(pre, 1));
   }
   l2_prefetch_share(scr.pf);
   pdl_launch();  // dependents may start their independent prologue now
@@ -1016,6 +1028,13 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   } else if (pmode != Q1_PREPARED) {
     q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
                     (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
+  } else if (rmode == 0) {
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(bar_x, (uint32_t)(nunit * XB));
+      bulk_g2s(smem_u32(xs), xprep, (uint32_t)(nunit * XB), bar_x);
+    }
+    ok = mbar_wait_bounded(bar_x, 0);
+    if (!ok && lane == 0) atomicOr(scr.err, SI_DEVERR_WAIT_TIMEOUT);
   } else {
     // prepared units (nunit * XB bytes, a multiple of 16), 16 bytes per load
     // with up to four loads in flight per thread
@@ -1035,8 +1054,9 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
     }
     __syncthreads();
   }
+  if (rmode == 0) issue_stages(1, pre);
+  else if (rmode == 2) issue_stages(0, pre);
 
-  if (scr.self_pf) issue_ring();
   // per-lane constants
   const int cls = lane >> 3;                                   // MMA column class
   const int xl = (lane & 7) * 16;                              // fragment slot in a group
@@ -1469,7 +1489,7 @@ int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const 
 int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const float* nw, float eps, float* y,
                    int epi, const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
   if (w->qtype == SI_Q4_K && (epi == SI_EPI_STORE || epi == SI_EPI_ADD)) {
-    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.self_pf, qb.q1w}, qb.split_bytes, qb.count_n};
+    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.ring_mode, qb.q1w}, qb.split_bytes, qb.count_n};
     const int r = epi == SI_EPI_ADD
                       ? launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM, x, nw, eps)
                       : launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM, x, nw, eps);
@@ -1484,7 +1504,7 @@ int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const flo
 int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const float* up, float* y, int epi,
                     const QmvBuffers& qb, uint8_t* xprep, bool pdl) {
   if (w->qtype == SI_Q4_K) {
-    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.self_pf, qb.q1w}, qb.split_bytes, qb.count_n};
+    const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.ring_mode, qb.q1w}, qb.split_bytes, qb.count_n};
     int r = -1;
     if (epi == SI_EPI_ADD) r = launch_q1<SI_EPI_ADD>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
     else if (epi == SI_EPI_STORE) r = launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_SILU, gate, up);
@@ -1498,7 +1518,7 @@ int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const
 
 int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
                const QmvBuffers& qb, bool pdl) {
-  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.self_pf, qb.q1w}, qb.split_bytes, qb.count_n};
+  const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.ring_mode, qb.q1w}, qb.split_bytes, qb.count_n};
   if (epi == SI_EPI_ADD) return dispatch_qt<SI_EPI_ADD>(s, w, xprep, B, y, scr, qb.sms, pdl);
   if (epi == SI_EPI_TP) {
     if (qb.tp.tp < 1 || !qb.tp.peers || !qb.tp.epoch) SI_FAIL(SI_ERR_INVALID, "qmatvec: tensor-parallel epilogue without peers");
