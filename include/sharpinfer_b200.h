@@ -317,6 +317,32 @@ SI_EXPORT int si_decode_step(si_model* m, const int* tokens_host, int batch, int
 SI_EXPORT int si_decode_generate(si_model* m, const int* tokens_host, int batch, int pos0,
                                  int nsteps, int* out_tokens_host);
 
+/* Prefill: the n prompt tokens tokens_host[n] of sequence `seq` at positions
+ * pos0 .. pos0 + n - 1 through every layer at once, storing their K/V in the
+ * cache, and the greedy next token after the last one (argmax_host, may be
+ * NULL) with its logits [vocab] (logits_host, may be NULL).  Replaces the
+ * reference's prefill loop of one Transformer.Forward per prompt token
+ * (src/SharpInfer.Core/Engine/InferenceEngine.cs:82-85): one tensor-core GEMM
+ * per projection (si_qgemm's kernels, activations as f16 rows) and one causal
+ * flash attention per layer on the cache's f16 K/V.  The stored K/V are the
+ * values the decode step would store token by token.  Single-device models
+ * only (tp = 1).  Synchronous. */
+SI_EXPORT int si_model_prefill(si_model* m, int seq, const int* tokens_host, int n, int pos0, int* argmax_host,
+                               float* logits_host);
+
+/* Read cache positions pos0 .. pos0 + n - 1 of one layer and sequence as f16
+ * in the reference layout [n][kv head][dim] (KVCache.GetKey / GetValue,
+ * KVCache.cs:60-71). */
+SI_EXPORT int si_model_kv_read(si_model* m, int layer, int seq, int pos0, int n, uint16_t* k_host, uint16_t* v_host);
+
+/* Prompt-cache serialisation of positions 0 .. length - 1 of a sequence, in
+ * the byte format of KVCache.WriteRawData / ReadRawData (KVCache.cs:84-114):
+ * for each layer, K then V as f32 [length][kv heads * head_dim].  Export
+ * widens the f16 cache exactly; import rounds to f16.  out_bytes / in_bytes
+ * must be at least n_layers * 2 * length * n_kv_heads * head_dim * 4. */
+SI_EXPORT int si_model_kv_export(si_model* m, int seq, int length, void* out_host, size_t out_bytes);
+SI_EXPORT int si_model_kv_import(si_model* m, int seq, int length, const void* in_host, size_t in_bytes);
+
 /* Kernel launches of one captured decode step at this batch size (captures
  * the step if needed): the device work behind one Transformer.Forward call
  * (Transformer.cs:67-162).  For measurement. */

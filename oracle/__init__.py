@@ -41,6 +41,7 @@ _SIGS = {
     "or_model_kv_fill": (None, [_c_p, _i32, _i32, _c_p, _c_p, _i32]),
     "or_model_forward": (_i32, [_c_p, _i32, _i32, _i32, _i32, _c_p]),
     "or_round_f16": (_f32, [_f32]),
+    "or_model_kv_get": (None, [_c_p, _i32, _i32, _i32, _c_p, _c_p]),
     "or_num_threads": (_i32, []),
     "or_synth_blocks": (_i32, [_i32, _i64, _i64, ctypes.c_uint64, ctypes.c_uint64, _i32, _f32, _c_p]),
     "or_synth_f32": (None, [_i64, ctypes.c_uint64, ctypes.c_uint64, _f32, _f32, _c_p]),
@@ -208,6 +209,14 @@ class OracleModel:
         if rc:
             raise ValueError("oracle forward failed (%d)" % rc)
         return logits
+
+    def kv_get(self, seq, layer, length):
+        """Cached K, V of positions [0, length): f32 [length][kv heads][dim]."""
+        shape = (length, self.cfg.n_kv_heads, self.cfg.head_dim)
+        k = np.empty(shape, np.float32)
+        v = np.empty(shape, np.float32)
+        load().or_model_kv_get(self.handle, seq, layer, length, _p(k), _p(v))
+        return k, v
 
     def __del__(self):
         try:

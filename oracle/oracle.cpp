@@ -605,6 +605,15 @@ OR_API int or_model_forward(void* p, int seq, int token, int pos, int kv_round_f
   return 0;
 }
 
+// The cached K and V of positions [0, len) of (seq, layer) in the reference
+// layout [pos][kv head][dim] (KVCache.GetKey / GetValue, KVCache.cs:60-71).
+OR_API void or_model_kv_get(void* p, int seq, int layer, int len, float* k, float* v) {
+  OrModel* m = (OrModel*)p;
+  const size_t n = (size_t)len * m->c.n_kv_heads * m->c.head_dim;
+  memcpy(k, kv_ptr(m, m->kcache, seq, layer, 0), n * sizeof(float));
+  memcpy(v, kv_ptr(m, m->vcache, seq, layer, 0), n * sizeof(float));
+}
+
 // binary32 -> binary16 -> binary32 helper exported for tests.
 OR_API float or_round_f16(float x) { return round_f16(x); }
 

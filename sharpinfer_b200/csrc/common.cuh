@@ -245,6 +245,13 @@ int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const flo
 // y (op)= W (SiLU(gate) * up) for one row (batch 1).
 int launch_qmv_silu(cudaStream_t s, const si_weight* w, const float* gate, const float* up, float* y, int epi,
                     const QmvBuffers& qb, uint8_t* xprep, bool pdl);
+// Prefill GEMM core: y[m] (+)= rs[m] * (xf[m] . W) for f16 rows xf [M][cols]
+// scaled per row by rs[m]^-1 (a power of two); accumulate != 0 adds to y.
+int launch_qgemm_f16in(si_ctx* c, const si_weight* w, const __half* xf, const float* rs, float* y, int M,
+                       int accumulate);
+// Prefill attention on 16-bit q, k, v (bf16, or f16 when f16 is set).
+int launch_attn_prefill(si_ctx* c, const uint16_t* q, const uint16_t* k, const uint16_t* v, float* o, int batch,
+                        int heads, int kv_heads, int seq, int kv, float scale, int causal, int start_pos, bool f16);
 int launch_synth_blocks(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma,
                         int64_t blk0, int64_t nblocks, uint8_t* dst);
 int launch_synth_blocks_2d(si_ctx* c, int qt, uint64_t seed, uint64_t tag, int recipe, float sigma, int64_t grow0,

@@ -218,7 +218,8 @@ __global__ void __launch_bounds__(256) k_bf16_rows_to_f16(const uint16_t* __rest
 template <int GN>
 __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUtensorMap tmA,
                                                     const __grid_constant__ CUtensorMap tmB, float* __restrict__ Y,
-                                                    const float* __restrict__ rs, int M, int N, int K, int* err) {
+                                                    const float* __restrict__ rs, int M, int N, int K, int acc,
+                                                    int* err) {
   constexpr int B_BYTES = GemmCfg<GN>::B_BYTES;
   constexpr uint32_t IDESC = GemmCfg<GN>::IDESC;
   extern __shared__ uint8_t smem_raw[];
@@ -294,12 +295,19 @@ __global__ void __launch_bounds__(192, 1) k_gemm_tc(const __grid_constant__ CUte
       if (col0 + 32 <= N && (N & 3) == 0) {
 #pragma unroll
         for (int j = 0; j < 32; j += 4)
-          *(float4*)(yr + col0 + j) = make_float4(__uint_as_float(r[j]) * rsc, __uint_as_float(r[j + 1]) * rsc,
-                                                  __uint_as_float(r[j + 2]) * rsc, __uint_as_float(r[j + 3]) * rsc);
+        {
+          float4 v = make_float4(__uint_as_float(r[j]) * rsc, __uint_as_float(r[j + 1]) * rsc,
+                                 __uint_as_float(r[j + 2]) * rsc, __uint_as_float(r[j + 3]) * rsc);
+          if (acc) {
+            const float4 o = *(const float4*)(yr + col0 + j);
+            v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+          }
+          *(float4*)(yr + col0 + j) = v;
+        }
       } else {
 #pragma unroll
         for (int j = 0; j < 32; j++)
-          if (col0 + j < N) yr[col0 + j] = __uint_as_float(r[j]) * rsc;
+          if (col0 + j < N) yr[col0 + j] = (acc ? yr[col0 + j] : 0.f) + __uint_as_float(r[j]) * rsc;
       }
     }
   }
@@ -336,7 +344,7 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t 
 template <int GN>
 __global__ void __launch_bounds__(320, 1) k_gemm_q4k(const __grid_constant__ CUtensorMap tmA, const uint8_t* __restrict__ W,
                                                      int tiles, float* __restrict__ Y, const float* __restrict__ rs, int M,
-                                                     int N, int K, int* err) {
+                                                     int N, int K, int acc, int* err) {
   constexpr int B_BYTES = GemmCfg<GN>::B_BYTES;
   constexpr uint32_t IDESC = GemmCfg<GN>::IDESC;
   constexpr int RT = GN / 128;  // row tiles per dequantising warp
@@ -512,12 +520,19 @@ __global__ void __launch_bounds__(320, 1) k_gemm_q4k(const __grid_constant__ CUt
         if (col0 + 32 <= N && (N & 3) == 0) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
-            *(float4*)(yr + col0 + j) = make_float4(__uint_as_float(r[j]) * rsc, __uint_as_float(r[j + 1]) * rsc,
-                                                    __uint_as_float(r[j + 2]) * rsc, __uint_as_float(r[j + 3]) * rsc);
+          {
+            float4 v = make_float4(__uint_as_float(r[j]) * rsc, __uint_as_float(r[j + 1]) * rsc,
+                                   __uint_as_float(r[j + 2]) * rsc, __uint_as_float(r[j + 3]) * rsc);
+            if (acc) {
+              const float4 o = *(const float4*)(yr + col0 + j);
+              v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+            }
+            *(float4*)(yr + col0 + j) = v;
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 32; j++)
-            if (col0 + j < N) yr[col0 + j] = __uint_as_float(r[j]) * rsc;
+            if (col0 + j < N) yr[col0 + j] = (acc ? yr[col0 + j] : 0.f) + __uint_as_float(r[j]) * rsc;
         }
       }
     }
@@ -563,10 +578,24 @@ int dequant_f16(si_ctx* c, const si_weight* w, __half* dst) {
 }
 
 int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int M) {
-  const int64_t N = w->rows, K = w->cols;
+  const int64_t K = w->cols;
   if (K % GK) SI_FAIL(SI_ERR_UNSUPPORTED, "qgemm: cols %lld not a multiple of %d", (long long)K, GK);
   const size_t xbytes = ((size_t)M * K * 2 + 255) & ~(size_t)255;
   SI_TRY(ensure(c->stage[1], xbytes + (size_t)M * 4));
+  __half* xf = (__half*)c->stage[1].ptr;
+  float* rs = (float*)((uint8_t*)c->stage[1].ptr + xbytes);  // per-row 2^-e of the conversion
+  if (((uintptr_t)x & 15) != 0) SI_FAIL(SI_ERR_INVALID, "si_qgemm: x must be 16-byte aligned");
+  k_bf16_rows_to_f16<<<(unsigned)M, 256, 0, c->stream>>>(x, xf, rs, (int)K);
+  SI_CUDA(cudaGetLastError());
+  return launch_qgemm_f16in(c, w, xf, rs, y, M, 0);
+}
+
+// y[m] (+)= rs[m] * (xf[m] . W) for f16 rows xf [M][cols] (16-byte aligned)
+// already scaled by 2^e per row (rs[m] = 2^-e); accumulate != 0 adds to y.
+int launch_qgemm_f16in(si_ctx* c, const si_weight* w, const __half* xf, const float* rs, float* y, int M,
+                       int accumulate) {
+  const int64_t N = w->rows, K = w->cols;
+  if (K % GK) SI_FAIL(SI_ERR_UNSUPPORTED, "qgemm: cols %lld not a multiple of %d", (long long)K, GK);
   __half* wf = (__half*)w->f16;
   // Q4_K without a cached copy: dequantised in shared memory while the row
   // blocks of X are few (each one dequantises W again; measured on the 8B
@@ -578,11 +607,6 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
     wf = (__half*)c->stage[0].ptr;
     SI_TRY(dequant_f16(c, w, wf));
   }
-  __half* xf = (__half*)c->stage[1].ptr;
-  float* rs = (float*)((uint8_t*)c->stage[1].ptr + xbytes);  // per-row 2^-e of the conversion
-  if (((uintptr_t)x & 15) != 0) SI_FAIL(SI_ERR_INVALID, "si_qgemm: x must be 16-byte aligned");
-  k_bf16_rows_to_f16<<<(unsigned)M, 256, 0, c->stream>>>(x, xf, rs, (int)K);
-  SI_CUDA(cudaGetLastError());
   // 256-wide tiles, or 128-wide when 256 would leave SMs idle
   const int64_t tiles256 = ((N + 255) / 256) * (((int64_t)M + GM - 1) / GM);
   const int GN = tiles256 < c->sm_count ? 128 : 256;
@@ -609,10 +633,10 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
     cfg.numAttrs = 1;
     const uint8_t* wd = (const uint8_t*)w->dev;
     if (GN == 128)
-      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<128>, ta, wd, (int)w->tiles, y, (const float*)rs, M, (int)N, (int)K,
+      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<128>, ta, wd, (int)w->tiles, y, rs, M, (int)N, (int)K, accumulate,
                                  c->dev_err));
     else
-      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<256>, ta, wd, (int)w->tiles, y, (const float*)rs, M, (int)N, (int)K,
+      SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_q4k<256>, ta, wd, (int)w->tiles, y, rs, M, (int)N, (int)K, accumulate,
                                  c->dev_err));
     return SI_OK;
   }
@@ -636,9 +660,9 @@ int launch_qgemm(si_ctx* c, const si_weight* w, const uint16_t* x, float* y, int
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (GN == 128)
-    SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<128>, ta, tb, y, (const float*)rs, M, (int)N, (int)K, c->dev_err));
+    SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<128>, ta, tb, y, rs, M, (int)N, (int)K, accumulate, c->dev_err));
   else
-    SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<256>, ta, tb, y, (const float*)rs, M, (int)N, (int)K, c->dev_err));
+    SI_CUDA(cudaLaunchKernelEx(&cfg, k_gemm_tc<256>, ta, tb, y, rs, M, (int)N, (int)K, accumulate, c->dev_err));
   return SI_OK;
 }
 

@@ -28,47 +28,6 @@
 namespace si {
 namespace {
 
-// Element `col` of row r of a device-layout weight (reference rounding).
-__device__ __forceinline__ float weight_elem(int qt, const uint8_t* __restrict__ W, int64_t nblk,
-                                             int64_t r, int col) {
-  const int64_t T = r >> 4;
-  const int ri = (int)(r & 15);
-  if (qt == SI_Q4_K) {
-    const int64_t b = col >> 8;
-    const int e = col & 255, j = e >> 5;
-    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 2304);
-    const uint8_t* hdr = (const uint8_t*)(tbw + 4 * ri);
-    const float d = h2f(hdr[0] | (hdr[1] << 8)), dmin = h2f(hdr[2] | (hdr[3] << 8));
-    const uint8_t* q = hdr + 4;
-    uint32_t sc, mn;
-    if (j < 4) {
-      sc = q[j] & 63;
-      mn = q[j + 4] & 63;
-    } else {
-      sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
-      mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
-    }
-    const float d1 = __fmul_rn(d, (float)sc), m1f = __fmul_rn(dmin, (float)mn);
-    return __fsub_rn(__fmul_rn(d1, (float)dev_q4k_code(tbw, ri, e)), m1f);
-  } else if (qt == SI_Q6_K) {
-    const int64_t b = col >> 8;
-    const int e = col & 255;
-    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 3360);
-    const int8_t* scales = (const int8_t*)(tbw + 768) + 16 * ri;
-    const uint32_t dw = tbw[832 + (ri & 7)];
-    const float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
-    const float ds = __fmul_rn(d, (float)scales[e >> 4]);
-    return __fmul_rn(ds, (float)((int)dev_q6k_code(tbw, ri, e) - 32));
-  } else {
-    const int64_t b = col >> 5;
-    const int e = col & 31;
-    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 544);
-    const uint32_t dw = tbw[128 + (ri & 7)];
-    const float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
-    return __fmul_rn((float)dev_q80_code(tbw, ri, e), d);
-  }
-}
-
 // x[b] = row tokens[b] of the token embedding (Transformer.cs:76).
 __global__ void k_embed(const StepParams* __restrict__ p, int qt, const uint8_t* __restrict__ W,
                         int64_t nblk, int64_t vocab, int h, float* __restrict__ x) {
@@ -77,7 +36,7 @@ __global__ void k_embed(const StepParams* __restrict__ p, int qt, const uint8_t*
   const int b = blockIdx.y;
   const int col = blockIdx.x * blockDim.x + threadIdx.x;
   const int tok = p->tokens[b];
-  if (col < h && tok >= 0 && tok < vocab) x[(int64_t)b * h + col] = weight_elem(qt, W, nblk, tok, col);
+  if (col < h && tok >= 0 && tok < vocab) x[(int64_t)b * h + col] = dev_weight_elem(qt, W, nblk, tok, col);
 }
 
 // Greedy selection (SamplingPipeline.ArgMax, SamplingPipeline.cs:83-89):
@@ -347,6 +306,8 @@ struct si_model {
   int* hargmax = nullptr;         // pinned
   int* hist = nullptr;            // device token history of si_decode_generate
   int64_t hist_cap = 0;           // ints
+  // model-level prefill scratch (grow-only, allocated on first use)
+  si_devbuf pf_tok, pf_x, pf_xh, pf_rs, pf_qkv, pf_gu, pf_q, pf_k, pf_v, pf_o;
   std::map<int, cudaGraphExec_t> graphs;
   std::map<int, int> graph_kernels;  // kernel launches per captured step
   std::vector<void*> allocs;
@@ -971,6 +932,9 @@ SI_EXPORT int si_model_free(si_model* m) {
   si_weight_free(m->emb);
   si_weight_free(m->lm_head);
   for (void* p : m->allocs) cudaFree(p);
+  for (si_devbuf* b : {&m->pf_tok, &m->pf_x, &m->pf_xh, &m->pf_rs, &m->pf_qkv, &m->pf_gu, &m->pf_q, &m->pf_k, &m->pf_v,
+                       &m->pf_o})
+    if (b->ptr) cudaFree(b->ptr);
   if (m->hparams) cudaFreeHost(m->hparams);
   if (m->hargmax) cudaFreeHost(m->hargmax);
   if (m->hist) cudaFree(m->hist);
@@ -1193,6 +1157,148 @@ SI_EXPORT int si_decode_step_kernels(si_model* m, int batch, int* kernels) {
   cudaGraphExec_t ge;
   SI_TRY(get_graph(m, batch, &ge));
   *kernels = m->graph_kernels[batch];
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_prefill(si_model* m, int seq, const int* tokens, int n, int pos0, int* argmax_out,
+                               float* logits_out) {
+  clear_error();
+  if (!m || !tokens) SI_FAIL(SI_ERR_INVALID, "si_model_prefill: NULL argument");
+  const si_model_config& c = m->cfg;
+  if (m->tp > 1) SI_FAIL(SI_ERR_UNSUPPORTED, "si_model_prefill: tensor-parallel models prefill through si_decode_step");
+  if (seq < 0 || seq >= c.max_batch) SI_FAIL(SI_ERR_INVALID, "si_model_prefill: sequence %d outside 0..%d", seq,
+                                                c.max_batch - 1);
+  if (n < 1 || pos0 < 0 || (int64_t)pos0 + n > c.max_seq)
+    SI_FAIL(SI_ERR_INVALID, "si_model_prefill: positions %d..%d exceed max sequence length %d", pos0, pos0 + n,
+            c.max_seq);  // KVCache.cs:48-49
+  for (int i = 0; i < n; i++)
+    if (tokens[i] < 0 || tokens[i] >= c.vocab) SI_FAIL(SI_ERR_INVALID, "token id %d outside the vocabulary", tokens[i]);
+  si_ctx* ctx = m->c;
+  SI_TRY(bind_device(ctx));
+  cudaStream_t s = ctx->stream;
+  const int h = c.hidden, inter = c.intermediate, nh = c.n_heads, nkv = c.n_kv_heads, L = pos0 + n;
+  const int kmax = std::max(std::max(h, inter), nh * c.head_dim);
+  SI_TRY(ensure(m->pf_tok, (size_t)n * 4));
+  SI_TRY(ensure(m->pf_x, (size_t)n * h * 4));
+  SI_TRY(ensure(m->pf_xh, (size_t)n * kmax * 2));
+  SI_TRY(ensure(m->pf_rs, (size_t)n * 4));
+  SI_TRY(ensure(m->pf_qkv, (size_t)n * m->qkv_rows * 4));
+  SI_TRY(ensure(m->pf_gu, (size_t)n * 2 * inter * 4));
+  SI_TRY(ensure(m->pf_q, (size_t)nh * n * c.head_dim * 2));
+  SI_TRY(ensure(m->pf_k, (size_t)nkv * L * c.head_dim * 2));
+  SI_TRY(ensure(m->pf_v, (size_t)nkv * L * c.head_dim * 2));
+  SI_TRY(ensure(m->pf_o, (size_t)nh * n * c.head_dim * 4));
+  float* x = (float*)m->pf_x.ptr;
+  __half* xh = (__half*)m->pf_xh.ptr;
+  float* rs = (float*)m->pf_rs.ptr;
+  float* qkv = (float*)m->pf_qkv.ptr;
+  float* gu = (float*)m->pf_gu.ptr;
+  __half* qh = (__half*)m->pf_q.ptr;
+  __half* kd = (__half*)m->pf_k.ptr;
+  __half* vd = (__half*)m->pf_v.ptr;
+  float* o = (float*)m->pf_o.ptr;
+  SI_CUDA(cudaMemcpyAsync(m->pf_tok.ptr, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s));
+  SI_TRY(launch_embed_rows(s, (const int*)m->pf_tok.ptr, n, m->emb, h, x));
+  const int64_t per = (int64_t)nkv * c.max_seq * c.head_dim;
+  const float scale = 1.0f / sqrtf((float)c.head_dim);  // Transformer.cs:101
+  for (int l = 0; l < c.n_layers; l++) {
+    __half* kc = m->kcache + ((int64_t)l * c.max_batch + seq) * per;
+    __half* vc = m->vcache + ((int64_t)l * c.max_batch + seq) * per;
+    SI_TRY(launch_rms_rows(s, x, n, h, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, xh, rs));
+    SI_TRY(launch_qgemm_f16in(ctx, m->wqkv[l], xh, rs, qkv, n, 0));
+    SI_TRY(launch_rope_store(s, qkv, m->qkv_rows, m->rope, pos0, n, nh, nkv, kc, vc, c.max_seq, qh));
+    SI_TRY(launch_cache_dense(s, kc, c.max_seq, L, nkv, kd));
+    SI_TRY(launch_cache_dense(s, vc, c.max_seq, L, nkv, vd));
+    SI_TRY(launch_attn_prefill(ctx, (const uint16_t*)qh, (const uint16_t*)kd, (const uint16_t*)vd, o, 1, nh, nkv, n, L,
+                               scale, 1, pos0, true));
+    SI_TRY(launch_heads_rows(s, o, n, nh, xh, rs));
+    SI_TRY(launch_qgemm_f16in(ctx, m->wo[l], xh, rs, x, n, 1));
+    SI_TRY(launch_rms_rows(s, x, n, h, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, xh, rs));
+    SI_TRY(launch_qgemm_f16in(ctx, m->wgu[l], xh, rs, gu, n, 0));
+    SI_TRY(launch_silu_rows(s, gu, n, inter, xh, rs));
+    SI_TRY(launch_qgemm_f16in(ctx, m->wdown[l], xh, rs, x, n, 1));
+  }
+  // the last prompt token's logits: final RmsNorm, lm_head, greedy ArgMax (Transformer.cs:158-159)
+  SI_TRY(launch_prep(s, x + (int64_t)(n - 1) * h, h, nullptr, norm_ptr(m, -1, SI_T_FINAL_NORM), c.rms_eps,
+                     SI_PREP_RMSNORM, h, 1, nullptr, m->xprep, false));
+  SI_TRY(launch_qmv(s, m->lm_head, m->xprep, 1, m->logits, SI_EPI_STORE, ctx->qmv(), false));
+  k_argmax<<<1, 1024, 0, s>>>((const float*)m->logits, (int64_t)c.vocab, m->argmax, ArgmaxTp{});
+  SI_CUDA(cudaGetLastError());
+  SI_CUDA(cudaMemcpyAsync(m->hargmax, m->argmax, sizeof(int), cudaMemcpyDeviceToHost, s));
+  if (logits_out) SI_CUDA(cudaMemcpyAsync(logits_out, m->logits, (size_t)c.vocab * 4, cudaMemcpyDeviceToHost, s));
+  SI_CUDA(cudaStreamSynchronize(s));
+  SI_TRY(check_device_errors(ctx));
+  if (argmax_out) *argmax_out = m->hargmax[0];
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_kv_read(si_model* m, int layer, int seq, int pos0, int n, uint16_t* k, uint16_t* v) {
+  clear_error();
+  if (!m || !k || !v) SI_FAIL(SI_ERR_INVALID, "si_model_kv_read: NULL argument");
+  const si_model_config& c = m->cfg;
+  if (layer < 0 || layer >= c.n_layers || seq < 0 || seq >= c.max_batch || pos0 < 0 || n < 0 || pos0 + n > c.max_seq)
+    SI_FAIL(SI_ERR_INVALID, "si_model_kv_read: range outside the cache");
+  if (n == 0) return SI_OK;
+  si_ctx* ctx = m->c;
+  SI_TRY(bind_device(ctx));
+  const int64_t per = (int64_t)c.n_kv_heads * c.max_seq * c.head_dim;
+  const int64_t off = ((int64_t)layer * c.max_batch + seq) * per;
+  const size_t bytes = (size_t)c.n_kv_heads * (pos0 + n) * c.head_dim * 2;
+  SI_TRY(ensure(ctx->stage[3], bytes));
+  std::vector<uint16_t> dense((size_t)c.n_kv_heads * (pos0 + n) * c.head_dim);
+  for (int which = 0; which < 2; which++) {
+    SI_TRY(launch_cache_dense(ctx->stream, (which ? m->vcache : m->kcache) + off, c.max_seq, pos0 + n, c.n_kv_heads,
+                              (__half*)ctx->stage[3].ptr));
+    SI_CUDA(cudaMemcpyAsync(dense.data(), ctx->stage[3].ptr, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    SI_CUDA(cudaStreamSynchronize(ctx->stream));
+    uint16_t* out = which ? v : k;  // [n][kv head][dim], KVCache.cs:60-71
+    for (int t = 0; t < n; t++)
+      for (int kvh = 0; kvh < c.n_kv_heads; kvh++)
+        memcpy(out + ((size_t)t * c.n_kv_heads + kvh) * c.head_dim,
+               dense.data() + ((size_t)kvh * (pos0 + n) + pos0 + t) * c.head_dim, (size_t)c.head_dim * 2);
+  }
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_kv_export(si_model* m, int seq, int length, void* out, size_t out_bytes) {
+  clear_error();
+  if (!m || !out) SI_FAIL(SI_ERR_INVALID, "si_model_kv_export: NULL argument");
+  const si_model_config& c = m->cfg;
+  if (m->tp > 1) SI_FAIL(SI_ERR_UNSUPPORTED, "si_model_kv_export: export each rank's model on a single-device copy");
+  const size_t stride = (size_t)c.n_kv_heads * c.head_dim;
+  const size_t need = (size_t)c.n_layers * 2 * length * stride * 4;
+  if (length < 0 || length > c.max_seq || out_bytes < need)
+    SI_FAIL(SI_ERR_INVALID, "si_model_kv_export: %d positions need %zu bytes", length, need);
+  std::vector<uint16_t> k((size_t)length * stride), v((size_t)length * stride);
+  float* dst = (float*)out;
+  for (int l = 0; l < c.n_layers; l++) {  // KVCache.WriteRawData: per layer K then V, f32 [pos][kv head][dim]
+    SI_TRY(si_model_kv_read(m, l, seq, 0, length, k.data(), v.data()));
+    for (size_t i = 0; i < k.size(); i++) dst[i] = __half2float(__ushort_as_half(k[i]));
+    dst += k.size();
+    for (size_t i = 0; i < v.size(); i++) dst[i] = __half2float(__ushort_as_half(v[i]));
+    dst += v.size();
+  }
+  return SI_OK;
+}
+
+SI_EXPORT int si_model_kv_import(si_model* m, int seq, int length, const void* in, size_t in_bytes) {
+  clear_error();
+  if (!m || !in) SI_FAIL(SI_ERR_INVALID, "si_model_kv_import: NULL argument");
+  const si_model_config& c = m->cfg;
+  if (m->tp > 1) SI_FAIL(SI_ERR_UNSUPPORTED, "si_model_kv_import: import on a single-device model");
+  const size_t stride = (size_t)c.n_kv_heads * c.head_dim;
+  const size_t need = (size_t)c.n_layers * 2 * length * stride * 4;
+  if (length < 0 || length > c.max_seq || in_bytes < need)
+    SI_FAIL(SI_ERR_INVALID, "si_model_kv_import: %d positions need %zu bytes", length, need);
+  std::vector<uint16_t> k((size_t)length * stride), v((size_t)length * stride);
+  const float* src = (const float*)in;
+  for (int l = 0; l < c.n_layers; l++) {  // KVCache.ReadRawData, values rounded to the f16 cache
+    for (size_t i = 0; i < k.size(); i++) k[i] = __half_as_ushort(__float2half_rn(src[i]));
+    src += k.size();
+    for (size_t i = 0; i < v.size(); i++) v[i] = __half_as_ushort(__float2half_rn(src[i]));
+    src += v.size();
+    SI_TRY(si_model_kv_write(m, l, seq, 0, length, k.data(), v.data()));
+  }
   return SI_OK;
 }
 

@@ -45,6 +45,15 @@ struct AttnArgs {
 // (ldmatrix without conflicts).  Offset in halves of dim d of position p:
 __host__ __device__ __forceinline__ int kv_swz(int d, int p) { return (((d >> 3) ^ (p & 7)) << 3) | (d & 7); }
 
+// Model-level prefill kernels (prefill.cu).
+int launch_embed_rows(cudaStream_t s, const int* tokens, int n, const si_weight* emb, int h, float* x);
+int launch_rms_rows(cudaStream_t s, const float* x, int n, int h, const float* w, float eps, __half* y, float* rs);
+int launch_rope_store(cudaStream_t s, const float* qkv, int ld, const float* rope, int pos0, int n, int nh, int nkv,
+                      __half* kc, __half* vc, int max_seq, __half* qh);
+int launch_cache_dense(cudaStream_t s, const __half* cache, int max_seq, int len, int nkv, __half* out);
+int launch_heads_rows(cudaStream_t s, const float* o, int n, int nh, __half* y, float* rs);
+int launch_silu_rows(cudaStream_t s, const float* gu, int n, int inter, __half* y, float* rs);
+
 size_t attn_smem_bytes(int G, int chunk_max);
 int launch_attn(cudaStream_t s, const AttnArgs& a, int G, int splits, int batch, int nkv, bool pdl);
 

@@ -51,10 +51,35 @@ constexpr int FA_PB = FA_BQ * 128;  // P (hi or lo): [128 rows][64 keys * 2 B]
 constexpr int FA_XCH = 3 * 256 * 4;  // row maxima [2 tiles][2 halves][128] and row sums [2][128]
 constexpr int FA_SMEM = 1024 + FA_QB + FA_NST * (FA_KB + FA_VB) + 4 * FA_PB + 256 + FA_XCH;
 constexpr int FA_THREADS = 320;  // TMA warp, MMA warp, 8 softmax warps
-// kind::f16 instruction descriptors: D f32, A and B bf16, both K-major
-constexpr uint32_t FA_IDESC_S = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
-constexpr uint32_t FA_IDESC_O = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+// kind::f16 instruction descriptors: D f32, A and B bf16 (bits 7, 10) or f16
+// (format 0), both K-major
+template <bool F16>
+struct FaDesc {
+  static constexpr uint32_t AB = F16 ? 0u : ((1u << 7) | (1u << 10));
+  static constexpr uint32_t S = (1u << 4) | AB | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+  static constexpr uint32_t O = (1u << 4) | AB | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+};
 
+// One 16-bit operand type for Q, K, V and the probabilities: bf16 (the
+// public bf16 entry point) or f16 (the model's f16 KV cache).
+template <bool F16>
+__device__ __forceinline__ void split_pair(float a0, float a1, uint32_t& hi, uint32_t& lo) {
+  if (F16) {
+    const __half2 h = __floats2half2_rn(a0, a1);
+    const float2 hf = __half22float2(h);
+    const __half2 lw = __floats2half2_rn(a0 - hf.x, a1 - hf.y);
+    hi = *(const uint32_t*)&h;
+    lo = *(const uint32_t*)&lw;
+  } else {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 lw = __floats2bfloat162_rn(a0 - hf.x, a1 - hf.y);
+    hi = *(const uint32_t*)&h;
+    lo = *(const uint32_t*)&lw;
+  }
+}
+
+template <bool F16>
 __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_constant__ CUtensorMap tmQ,
                                                        const __grid_constant__ CUtensorMap tmK,
                                                        const __grid_constant__ CUtensorMap tmV, float* __restrict__ O,
@@ -127,7 +152,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
 #pragma unroll
             for (int kk = 0; kk < 4; kk++)
               umma_f16(tmem + 64 * (j & 1), sdesc_k128(sQ + c * (FA_QB / 2)) + 2 * kk,
-                       sdesc_k128(sK + st * FA_KB + c * (FA_KB / 2)) + 2 * kk, FA_IDESC_S, (c | kk) != 0);
+                       sdesc_k128(sK + st * FA_KB + c * (FA_KB / 2)) + 2 * kk, FaDesc<F16>::S, (c | kk) != 0);
         }
         umma_commit(s_full + 8 * (j & 1));
       };
@@ -141,10 +166,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
           const uint32_t ph = sP + pb * 2 * FA_PB, vt = sV + st * FA_VB, d = tmem + 128;
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
-            umma_f16(d, sdesc_k128(ph) + 2 * kk, sdesc_k128(vt) + 2 * kk, FA_IDESC_O, (j | kk) != 0);
+            umma_f16(d, sdesc_k128(ph) + 2 * kk, sdesc_k128(vt) + 2 * kk, FaDesc<F16>::O, (j | kk) != 0);
 #pragma unroll
           for (int kk = 0; kk < 4; kk++)
-            umma_f16(d, sdesc_k128(ph + FA_PB) + 2 * kk, sdesc_k128(vt) + 2 * kk, FA_IDESC_O, 1);
+            umma_f16(d, sdesc_k128(ph + FA_PB) + 2 * kk, sdesc_k128(vt) + 2 * kk, FaDesc<F16>::O, 1);
         }
         umma_commit(o_full + 8 * pb);
         umma_commit(kv_empty + 8 * st);
@@ -230,7 +255,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
       l += ps;
       // P_j goes to the buffer P_{j-2} used: wait for that product
       if (ok && j >= 2 && !mbar_wait_bounded(o_full + 8 * pb, (uint32_t)(((j - 2) / 2) & 1))) ok = false;
-      {  // P_j as bf16 hi + lo: row r, chunks of 8 keys, chunk g at (g ^ (r % 8)) * 16 in the 128-byte row
+      {  // P_j as hi + lo (bf16 or f16): row r, chunks of 8 keys, chunk g at (g ^ (r % 8)) * 16 in the 128-byte row
         const uint32_t ph = sP + pb * 2 * FA_PB + r * 128;
 #pragma unroll
         for (int gg = 0; gg < 4; gg++) {
@@ -238,12 +263,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1) k_attn_fa_tc(const __grid_const
           uint32_t hi[4], lo[4];
 #pragma unroll
           for (int e = 0; e < 4; e++) {
-            const float a0 = sv[8 * gg + 2 * e], a1 = sv[8 * gg + 2 * e + 1];
-            const __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
-            const float2 hf = __bfloat1622float2(h);
-            const __nv_bfloat162 lw = __floats2bfloat162_rn(a0 - hf.x, a1 - hf.y);
-            hi[e] = *(const uint32_t*)&h;
-            lo[e] = *(const uint32_t*)&lw;
+            split_pair<F16>(sv[8 * gg + 2 * e], sv[8 * gg + 2 * e + 1], hi[e], lo[e]);
           }
           const uint32_t off = (uint32_t)((g ^ (r & 7)) << 4);
           asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(ph + off), "r"(hi[0]), "r"(hi[1]), "r"(hi[2]),
@@ -310,15 +330,16 @@ __global__ void k_vt(const uint16_t* __restrict__ V, uint16_t* __restrict__ Vt, 
   }
 }
 
-// 3D bf16 tensor [n2][n1][n0] (n0 contiguous), box [b2 = 1][b1][64], 128-byte swizzle.
-int make_tmap3(CUtensorMap* tm, const void* ptr, int64_t n0, int64_t n1, int64_t n2, int b1) {
+// 3D 16-bit tensor [n2][n1][n0] (n0 contiguous), box [b2 = 1][b1][64], 128-byte swizzle.
+int make_tmap3(CUtensorMap* tm, const void* ptr, int64_t n0, int64_t n1, int64_t n2, int b1, bool f16) {
   auto fn = encode_fn();
   if (!fn) SI_FAIL(SI_ERR_CUDA, "si_attn_prefill: cuTensorMapEncodeTiled unavailable");
   const cuuint64_t dims[3] = {(cuuint64_t)n0, (cuuint64_t)n1, (cuuint64_t)n2};
   const cuuint64_t strides[2] = {(cuuint64_t)n0 * 2, (cuuint64_t)n0 * n1 * 2};
   const cuuint32_t box[3] = {64, (cuuint32_t)b1, 1};
   const cuuint32_t estr[3] = {1, 1, 1};
-  const CUresult r = fn(tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+  const CUresult r = fn(tm, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                        const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) SI_FAIL(SI_ERR_CUDA, "si_attn_prefill: cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -326,6 +347,45 @@ int make_tmap3(CUtensorMap* tm, const void* ptr, int64_t n0, int64_t n1, int64_t
 }
 
 }  // namespace
+
+// Prefill attention for q [batch][heads][seq][128], k, v [batch][kv_heads][kv][128]
+// (16-bit: bf16, or f16 when f16 is set) into o f32 [batch][heads][seq][128],
+// asynchronous on the context stream; the checks of si_attn_prefill apply.
+int launch_attn_prefill(si_ctx* c, const uint16_t* q, const uint16_t* k, const uint16_t* v, float* o, int batch,
+                        int heads, int kv_heads, int seq, int kv, float scale, int causal, int start_pos, bool f16) {
+  if (kv > 0) {  // tensor cores (tcgen05): V transposed into scratch, Q/K/V^T through TMA
+    const int kvp = (kv + 7) & ~7;  // 16-byte rows of V^T
+    SI_TRY(ensure(c->stage[3], (size_t)batch * kv_heads * PA_D * kvp * 2));
+    uint16_t* vt = (uint16_t*)c->stage[3].ptr;
+    k_vt<<<dim3((unsigned)((kvp + 31) / 32), PA_D / 32, (unsigned)(batch * kv_heads)), dim3(32, 8), 0, c->stream>>>(
+        v, vt, kv, kvp);
+    SI_CUDA(cudaGetLastError());
+    CUtensorMap tq, tk, tv;
+    SI_TRY(make_tmap3(&tq, q, PA_D, seq, (int64_t)batch * heads, FA_BQ, f16));
+    SI_TRY(make_tmap3(&tk, k, PA_D, kv, (int64_t)batch * kv_heads, FA_BK, f16));
+    SI_TRY(make_tmap3(&tv, vt, kvp, PA_D, (int64_t)batch * kv_heads, PA_D, f16));
+    static DeviceOnce fa_attr[2];
+    if (!fa_attr[f16].done(c->device)) {
+      if (f16) SI_CUDA(cudaFuncSetAttribute(k_attn_fa_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM));
+      else SI_CUDA(cudaFuncSetAttribute(k_attn_fa_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM));
+      fa_attr[f16].mark(c->device);
+    }
+    dim3 grid((unsigned)((seq + FA_BQ - 1) / FA_BQ), (unsigned)heads, (unsigned)batch);
+    if (f16)
+      k_attn_fa_tc<true><<<grid, FA_THREADS, FA_SMEM, c->stream>>>(tq, tk, tv, o, heads, kv_heads, seq, kv, scale,
+                                                                   causal, start_pos, c->dev_err);
+    else
+      k_attn_fa_tc<false><<<grid, FA_THREADS, FA_SMEM, c->stream>>>(tq, tk, tv, o, heads, kv_heads, seq, kv, scale,
+                                                                    causal, start_pos, c->dev_err);
+    SI_CUDA(cudaGetLastError());
+    return SI_OK;
+  }
+  // no keys: every row sees none and is 0 (FlashAttention.cs:155-163)
+  SI_CUDA(cudaMemsetAsync(o, 0, (size_t)batch * heads * seq * PA_D * 4, c->stream));
+  SI_CUDA(cudaGetLastError());
+  return SI_OK;
+}
+
 }  // namespace si
 
 using namespace si;
@@ -342,30 +402,5 @@ extern "C" SI_EXPORT int si_attn_prefill(si_ctx* c, const uint16_t* q, const uin
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15)
     SI_FAIL(SI_ERR_INVALID, "si_attn_prefill: buffers must be 16-byte aligned");
   SI_TRY(bind_device(c));
-  if (kv > 0) {  // tensor cores (tcgen05): V transposed into scratch, Q/K/V^T through TMA
-    const int kvp = (kv + 7) & ~7;  // 16-byte rows of V^T
-    SI_TRY(ensure(c->stage[3], (size_t)batch * kv_heads * PA_D * kvp * 2));
-    uint16_t* vt = (uint16_t*)c->stage[3].ptr;
-    k_vt<<<dim3((unsigned)((kvp + 31) / 32), PA_D / 32, (unsigned)(batch * kv_heads)), dim3(32, 8), 0, c->stream>>>(
-        v, vt, kv, kvp);
-    SI_CUDA(cudaGetLastError());
-    CUtensorMap tq, tk, tv;
-    SI_TRY(make_tmap3(&tq, q, PA_D, seq, (int64_t)batch * heads, FA_BQ));
-    SI_TRY(make_tmap3(&tk, k, PA_D, kv, (int64_t)batch * kv_heads, FA_BK));
-    SI_TRY(make_tmap3(&tv, vt, kvp, PA_D, (int64_t)batch * kv_heads, PA_D));
-    static uint64_t fa_attr = 0;
-    if (c->device < 64 && !(fa_attr & (1ull << c->device))) {
-      SI_CUDA(cudaFuncSetAttribute(k_attn_fa_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, FA_SMEM));
-      fa_attr |= 1ull << c->device;
-    }
-    dim3 grid((unsigned)((seq + FA_BQ - 1) / FA_BQ), (unsigned)heads, (unsigned)batch);
-    k_attn_fa_tc<<<grid, FA_THREADS, FA_SMEM, c->stream>>>(tq, tk, tv, o, heads, kv_heads, seq, kv, scale, causal,
-                                                    start_pos, c->dev_err);
-    SI_CUDA(cudaGetLastError());
-    return SI_OK;
-  }
-  // no keys: every row sees none and is 0 (FlashAttention.cs:155-163)
-  SI_CUDA(cudaMemsetAsync(o, 0, (size_t)batch * heads * seq * PA_D * 4, c->stream));
-  SI_CUDA(cudaGetLastError());
-  return SI_OK;
+  return launch_attn_prefill(c, q, k, v, o, batch, heads, kv_heads, seq, kv, scale, causal, start_pos, false);
 }

@@ -87,4 +87,45 @@ __device__ __forceinline__ void dequant_block(int qt, const uint8_t* __restrict_
   }
 }
 
+// Element `col` of row r of a device-layout weight (reference rounding).
+__device__ __forceinline__ float dev_weight_elem(int qt, const uint8_t* __restrict__ W, int64_t nblk,
+                                             int64_t r, int col) {
+  const int64_t T = r >> 4;
+  const int ri = (int)(r & 15);
+  if (qt == SI_Q4_K) {
+    const int64_t b = col >> 8;
+    const int e = col & 255, j = e >> 5;
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 2304);
+    const uint8_t* hdr = (const uint8_t*)(tbw + 4 * ri);
+    const float d = h2f(hdr[0] | (hdr[1] << 8)), dmin = h2f(hdr[2] | (hdr[3] << 8));
+    const uint8_t* q = hdr + 4;
+    uint32_t sc, mn;
+    if (j < 4) {
+      sc = q[j] & 63;
+      mn = q[j + 4] & 63;
+    } else {
+      sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+      mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+    const float d1 = __fmul_rn(d, (float)sc), m1f = __fmul_rn(dmin, (float)mn);
+    return __fsub_rn(__fmul_rn(d1, (float)dev_q4k_code(tbw, ri, e)), m1f);
+  } else if (qt == SI_Q6_K) {
+    const int64_t b = col >> 8;
+    const int e = col & 255;
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 3360);
+    const int8_t* scales = (const int8_t*)(tbw + 768) + 16 * ri;
+    const uint32_t dw = tbw[832 + (ri & 7)];
+    const float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
+    const float ds = __fmul_rn(d, (float)scales[e >> 4]);
+    return __fmul_rn(ds, (float)((int)dev_q6k_code(tbw, ri, e) - 32));
+  } else {
+    const int64_t b = col >> 5;
+    const int e = col & 31;
+    const uint32_t* tbw = (const uint32_t*)(W + (T * nblk + b) * 544);
+    const uint32_t dw = tbw[128 + (ri & 7)];
+    const float d = h2f((ri >> 3) ? (dw >> 16) : (dw & 0xFFFF));
+    return __fmul_rn((float)dev_q80_code(tbw, ri, e), d);
+  }
+}
+
 }  // namespace si

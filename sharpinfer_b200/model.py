@@ -140,6 +140,35 @@ class DecodeModel:
         N.call("si_decode_generate", self.handle, N.ptr(tok), tok.size, pos0, nsteps, N.ptr(out))
         return out
 
+    def prefill(self, tokens, pos0=0, seq=0, logits=False):
+        """The prompt tokens of sequence `seq` at positions pos0.. through every
+        layer at once (tensor-core GEMMs and causal flash attention), filling the
+        KV cache; returns the greedy next token (and its logits)."""
+        tok = np.ascontiguousarray(tokens, np.int32).ravel()
+        out = np.empty(1, np.int32)
+        lg = np.empty(self.local_vocab, np.float32) if logits else None
+        N.call("si_model_prefill", self.handle, seq, N.ptr(tok), tok.size, pos0, N.ptr(out), N.ptr(lg))
+        return (int(out[0]), lg) if logits else int(out[0])
+
+    def kv_read(self, layer, seq, pos0, n):
+        """f16 K and V of positions pos0 .. pos0 + n - 1 as [n][kv head][dim] (uint16)."""
+        shape = (n, self.cfg.n_kv_heads // self.tp, self.cfg.head_dim)
+        k = np.empty(shape, np.uint16)
+        v = np.empty(shape, np.uint16)
+        N.call("si_model_kv_read", self.handle, layer, seq, pos0, n, N.ptr(k), N.ptr(v))
+        return k, v
+
+    def kv_export(self, seq, length):
+        """The prompt-cache byte format of KVCache.WriteRawData: per layer K then V, f32."""
+        n = self.cfg.n_layers * 2 * length * self.cfg.n_kv_heads * self.cfg.head_dim
+        out = np.empty(n, np.float32)
+        N.call("si_model_kv_export", self.handle, seq, length, N.ptr(out), out.nbytes)
+        return out
+
+    def kv_import(self, seq, length, data):
+        data = np.ascontiguousarray(data, np.float32)
+        N.call("si_model_kv_import", self.handle, seq, length, N.ptr(data), data.nbytes)
+
     def step_kernels(self, batch=1):
         """Kernel launches in one captured decode step at this batch size."""
         n = ctypes.c_int()

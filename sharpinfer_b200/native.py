@@ -102,6 +102,10 @@ _SIGS = {
     "si_decode_step": (_i32, [_c_p, _c_p, _i32, _i32, _c_p, _c_p]),
     "si_decode_generate": (_i32, [_c_p, _c_p, _i32, _i32, _i32, _c_p]),
     "si_model_attention": (_i32, [_c_p, _i32, _c_p, _c_p, _i32, _i32]),
+    "si_model_prefill": (_i32, [_c_p, _i32, _c_p, _i32, _i32, _c_p, _c_p]),
+    "si_model_kv_read": (_i32, [_c_p, _i32, _i32, _i32, _i32, _c_p, _c_p]),
+    "si_model_kv_export": (_i32, [_c_p, _i32, _i32, _c_p, ctypes.c_size_t]),
+    "si_model_kv_import": (_i32, [_c_p, _i32, _i32, _c_p, ctypes.c_size_t]),
 }
 
 _lib = None

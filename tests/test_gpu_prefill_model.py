@@ -1,0 +1,112 @@
+"""Model-level prefill (si_model_prefill) against the oracle's token-by-token
+forward pass -- the reference's prefill loop, one Transformer.Forward per
+prompt token (src/SharpInfer.Core/Engine/InferenceEngine.cs:82-85,
+Layers/Transformer.cs:67-162).  The prefill runs the projections as
+tensor-core GEMMs on f16 activations and the attention as one causal flash
+attention per layer, so its sums are ordered and rounded differently from the
+reference's f32 Dot; the bars are relative L2 1e-3 for the last token's
+logits and for the stored K/V, identical greedy tokens where the top-2 margin
+is not tiny, and a decode step after the prefill that matches the oracle.
+KV export / import follows KVCache.WriteRawData / ReadRawData
+(Engine/KVCache.cs:84-114)."""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import rel_l2
+from sharpinfer_b200 import native as N
+from sharpinfer_b200.model import DecodeModel, config
+
+pytestmark = pytest.mark.gpu
+SEED = 31
+
+
+def check_against_oracle(m, om, cfg, prompt, pos0, lg_gpu, tok_gpu):
+    ref = None
+    for i, t in enumerate(prompt):
+        ref = om.forward(0, int(t), pos0 + i)
+    err = rel_l2(lg_gpu, ref)
+    assert err < 1e-3, err
+    top = np.sort(ref)[-2:]
+    if top[1] - top[0] > 1e-3 * max(1.0, abs(top[1])):
+        assert tok_gpu == oracle.argmax(ref)
+    n = pos0 + len(prompt)
+    for l in range(cfg.n_layers):
+        kg, vg = m.kv_read(l, 0, 0, n)
+        kr, vr = om.kv_get(0, l, n)
+        kg = kg.view(np.float16).astype(np.float32)
+        vg = vg.view(np.float16).astype(np.float32)
+        assert rel_l2(kg, kr) < 1e-3, (l, rel_l2(kg, kr))
+        assert rel_l2(vg, vr) < 1e-3, (l, rel_l2(vg, vr))
+    return ref
+
+
+@pytest.mark.parametrize("G", [1, 4])
+def test_prefill_matches_token_by_token_forward(ctx, G):
+    nkv = 2
+    cfg = config(2, nkv * G * 128 if G > 1 else 512, 1024, nkv * G if G > 1 else 4, nkv if G > 1 else 4, 1000, 256, 1)
+    m = DecodeModel(ctx, cfg)
+    m.synth(SEED)
+    om = oracle.synthetic_model(cfg, SEED, n_seq=1, kv_len=0)
+    rng = np.random.default_rng(G)
+    p1 = rng.integers(0, 1000, 37)
+    tok, lg = m.prefill(p1, 0, logits=True)
+    check_against_oracle(m, om, cfg, p1, 0, lg, tok)
+    # a second chunk after the first: causal offset over the cached prefix
+    p2 = rng.integers(0, 1000, 150)
+    tok, lg = m.prefill(p2, 37, logits=True)
+    check_against_oracle(m, om, cfg, p2, 37, lg, tok)
+    # decode continues from the prefilled cache
+    out, lgd = m.step([tok], 187, logits=True)
+    ref = om.forward(0, tok, 187)
+    assert rel_l2(lgd[0], ref) < 1e-3
+    m.free()
+
+
+def test_prefill_llama8b_shapes_two_layers(ctx):
+    """The Llama-3-8B shapes (hidden 4096, 32/8 heads, FFN 14336, vocab
+    128256), cut to 2 layers, 64 prompt tokens."""
+    cfg = config(2, 4096, 14336, 32, 8, 128256, 192, 1)
+    m = DecodeModel(ctx, cfg)
+    m.synth(SEED)
+    om = oracle.synthetic_model(cfg, SEED, n_seq=1, kv_len=0)
+    prompt = np.random.default_rng(8).integers(0, 128256, 64)
+    tok, lg = m.prefill(prompt, 0, logits=True)
+    check_against_oracle(m, om, cfg, prompt, 0, lg, tok)
+    m.free()
+
+
+def test_kv_export_import_round_trip(ctx):
+    cfg = config(2, 512, 1024, 4, 2, 1000, 128, 1)
+    a = DecodeModel(ctx, cfg)
+    a.synth(SEED)
+    tok = a.prefill(np.arange(40) * 7 % 1000, 0)
+    blob = a.kv_export(0, 40)
+    assert blob.size == 2 * 2 * 40 * 2 * 128
+    b = DecodeModel(ctx, cfg)
+    b.synth(SEED)
+    b.kv_import(0, 40, blob)
+    for l in range(2):
+        ka, va = a.kv_read(l, 0, 0, 40)
+        kb, vb = b.kv_read(l, 0, 0, 40)
+        assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+    oa, la = a.step([tok], 40, logits=True)
+    ob, lb = b.step([tok], 40, logits=True)
+    assert np.array_equal(la, lb) and oa[0] == ob[0]
+    with pytest.raises(N.SIError):
+        b.kv_import(0, 40, blob[:-1])
+    a.free()
+    b.free()
+
+
+def test_prefill_rejects_bad_ranges(ctx):
+    cfg = config(1, 512, 1024, 4, 2, 1000, 64, 1)
+    m = DecodeModel(ctx, cfg)
+    m.synth(1)
+    with pytest.raises(N.SIError):
+        m.prefill([1] * 10, 60)      # past max_seq
+    with pytest.raises(N.SIError):
+        m.prefill([1000], 0)         # token outside the vocabulary
+    with pytest.raises(N.SIError):
+        m.prefill([1], 0, seq=1)     # sequence outside max_batch
+    m.free()
