@@ -8,6 +8,7 @@ tensors (plumbing for memory and streams); all arithmetic runs in
 libsharpinfer_b200.so.
 """
 import ctypes
+import weakref
 
 import numpy as np
 
@@ -24,6 +25,7 @@ class QuantWeight:
 
     def __init__(self, ctx, handle, qtype, rows, cols):
         self.ctx, self.handle, self.qtype, self.rows, self.cols = ctx, handle, qtype, rows, cols
+        ctx._adopt(self)
 
     @property
     def device_bytes(self):
@@ -60,6 +62,11 @@ class B200Context:
         N.call("si_stream", self.handle, ctypes.byref(s))
         self.stream_ptr = s.value
         self._torch_stream = None
+        self._children = weakref.WeakSet()  # weights and models that live on this context
+
+    def _adopt(self, obj):
+        """Track an object whose native handle must be freed before the context."""
+        self._children.add(obj)
 
     @property
     def name(self):
@@ -92,7 +99,13 @@ class B200Context:
             cur.wait_stream(self.torch_stream)
 
     def close(self):
+        """Free the weights and models still open on this context, then the context."""
         if self.handle:
+            for obj in list(self._children):
+                try:
+                    obj.free()
+                except Exception:
+                    pass
             N.call("si_shutdown", self.handle)
             self.handle = None
 

@@ -80,6 +80,7 @@ class DecodeModel:
         h = ctypes.c_void_p()
         N.call("si_model_create_tp", ctx.handle, ctypes.byref(cfg), tp, rank, ctypes.byref(h))
         self.handle = h
+        ctx._adopt(self)
 
     @property
     def local_vocab(self):
