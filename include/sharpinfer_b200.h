@@ -275,6 +275,9 @@ SI_EXPORT int si_tp_slice(const si_model_config* cfg, int tp, int rank, int tens
                           int64_t* gb0, int64_t* nblk, int64_t* gnblk);
 SI_EXPORT int si_model_free(si_model* m);
 
+/* The whole model's configuration (all ranks together for tensor parallelism). */
+SI_EXPORT int si_model_get_config(const si_model* m, si_model_config* out);
+
 /* Upload one weight tensor as raw GGUF blocks, row-major [rows][cols] of the
  * configured type (norms: f32[hidden]).  The projection shapes are those of
  * LayerWeights (Transformer.cs:89-151). */
@@ -353,6 +356,41 @@ SI_EXPORT int si_decode_step_kernels(si_model* m, int batch, int* kernels);
  * [batch][n_heads * head_dim] (test hook for the attention kernel). */
 SI_EXPORT int si_model_attention(si_model* m, int layer, const float* qkv_dev, float* out_dev,
                                  int batch, int pos);
+
+/* ------------------------------------------------------------ GGUF files
+ * The model loader behind InferenceEngine.Load (src/SharpInfer.Core/Engine/
+ * InferenceEngine.cs:48-49), whose Models/ directory the reference does not
+ * ship.  GGUF v2 and v3; the file is memory-mapped and its quantised blocks
+ * go to the device unexpanded.  Type ids are ggml's (QuantType,
+ * Quantization.cs:6-22). */
+typedef struct si_gguf si_gguf;
+SI_EXPORT int si_gguf_open(const char* path, si_gguf** out);
+SI_EXPORT int si_gguf_close(si_gguf* g);
+/* Format version, tensor and key/value counts, file offset of the data section. */
+SI_EXPORT int si_gguf_info(const si_gguf* g, int* version, int64_t* n_tensors, int64_t* n_kv, int64_t* data_offset);
+/* Metadata: integer (any integer or bool type), number (float or integer),
+ * string (NUL-terminated, truncated to len), array item type and length. */
+SI_EXPORT int si_gguf_meta_int(const si_gguf* g, const char* key, int64_t* out);
+SI_EXPORT int si_gguf_meta_float(const si_gguf* g, const char* key, double* out);
+SI_EXPORT int si_gguf_meta_string(const si_gguf* g, const char* key, char* buf, int len);
+SI_EXPORT int si_gguf_meta_array(const si_gguf* g, const char* key, int* item_type, int64_t* count);
+/* Tensor i: name, ggml type, rows (product of the outer dimensions), cols
+ * (the innermost dimension) and bytes; its bytes in the mapped file. */
+SI_EXPORT int si_gguf_tensor_info(const si_gguf* g, int64_t i, char* name, int name_len, int* qtype, int64_t* rows,
+                                  int64_t* cols, int64_t* bytes);
+SI_EXPORT int si_gguf_find_tensor(const si_gguf* g, const char* name, int64_t* index);
+SI_EXPORT int si_gguf_tensor_data(const si_gguf* g, int64_t i, const void** data);
+/* The si_model_config of a llama/mistral-architecture file (general.
+ * architecture and its block_count, embedding_length, feed_forward_length,
+ * attention.head_count[_kv], attention.key_length, layer_norm_rms_epsilon,
+ * rope.freq_base; vocabulary from token_embd).  max_seq <= 0 takes the
+ * file's context_length.  The projections must all be one of Q4_K, Q6_K,
+ * Q8_0 (SI_ERR_UNSUPPORTED names the first that is not). */
+SI_EXPORT int si_gguf_model_config(const si_gguf* g, int max_seq, int max_batch, si_model_config* cfg);
+/* Upload every tensor of the file into a model created with its config
+ * (any tensor-parallel rank takes its own slices); a file without
+ * output.weight uses the embedding as lm_head (tied weights). */
+SI_EXPORT int si_model_load_gguf(si_model* m, const si_gguf* g);
 
 /* --------------------------------------------- f32 interface of CudaBackend
  * The functions SharpInfer's managed backend binds from `sharpinfer_cuda`

@@ -836,6 +836,13 @@ SI_EXPORT int si_model_create_tp(si_ctx* ctx, const si_model_config* cfg, int tp
   return SI_OK;
 }
 
+SI_EXPORT int si_model_get_config(const si_model* m, si_model_config* out) {
+  clear_error();
+  if (!m || !out) SI_FAIL(SI_ERR_INVALID, "si_model_get_config: NULL argument");
+  *out = m->gcfg;
+  return SI_OK;
+}
+
 SI_EXPORT int si_model_create(si_ctx* ctx, const si_model_config* cfg, si_model** out) {
   return si_model_create_tp(ctx, cfg, 1, 0, out);
 }

@@ -103,6 +103,21 @@ _SIGS = {
     "si_decode_generate": (_i32, [_c_p, _c_p, _i32, _i32, _i32, _c_p]),
     "si_model_attention": (_i32, [_c_p, _i32, _c_p, _c_p, _i32, _i32]),
     "si_model_prefill": (_i32, [_c_p, _i32, _c_p, _i32, _i32, _c_p, _c_p]),
+    "si_model_get_config": (_i32, [_c_p, ctypes.POINTER(ModelConfig)]),
+    "si_gguf_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(_c_p)]),
+    "si_gguf_close": (_i32, [_c_p]),
+    "si_gguf_info": (_i32, [_c_p, ctypes.POINTER(_i32), ctypes.POINTER(_i64), ctypes.POINTER(_i64),
+                            ctypes.POINTER(_i64)]),
+    "si_gguf_meta_int": (_i32, [_c_p, ctypes.c_char_p, ctypes.POINTER(_i64)]),
+    "si_gguf_meta_float": (_i32, [_c_p, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+    "si_gguf_meta_string": (_i32, [_c_p, ctypes.c_char_p, ctypes.c_char_p, _i32]),
+    "si_gguf_meta_array": (_i32, [_c_p, ctypes.c_char_p, ctypes.POINTER(_i32), ctypes.POINTER(_i64)]),
+    "si_gguf_tensor_info": (_i32, [_c_p, _i64, ctypes.c_char_p, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i64),
+                                   ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "si_gguf_find_tensor": (_i32, [_c_p, ctypes.c_char_p, ctypes.POINTER(_i64)]),
+    "si_gguf_tensor_data": (_i32, [_c_p, _i64, ctypes.POINTER(_c_p)]),
+    "si_gguf_model_config": (_i32, [_c_p, _i32, _i32, ctypes.POINTER(ModelConfig)]),
+    "si_model_load_gguf": (_i32, [_c_p, _c_p]),
     "si_model_kv_read": (_i32, [_c_p, _i32, _i32, _i32, _i32, _c_p, _c_p]),
     "si_model_kv_export": (_i32, [_c_p, _i32, _i32, _c_p, ctypes.c_size_t]),
     "si_model_kv_import": (_i32, [_c_p, _i32, _i32, _c_p, ctypes.c_size_t]),
