@@ -191,6 +191,8 @@ class OracleModel:
         self.handle = L.or_model_create(cfg.n_layers, cfg.hidden, cfg.intermediate, cfg.n_heads, cfg.n_kv_heads,
                                         cfg.head_dim, cfg.vocab, cfg.max_seq, cfg.rms_eps, cfg.rope_theta, n_seq,
                                         threads or nthreads())
+        if not self.handle:
+            raise ValueError("oracle: hidden size must equal heads x head_dim (Transformer.cs:50)")
         self.keep = []
 
     def set(self, layer, which, qtype, data):
@@ -220,7 +222,8 @@ class OracleModel:
 
     def __del__(self):
         try:
-            load().or_model_free(self.handle)
+            if self.handle:
+                load().or_model_free(self.handle)
         except Exception:
             pass
 

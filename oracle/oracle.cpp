@@ -487,6 +487,10 @@ struct OrModel {
 OR_API void* or_model_create(int n_layers, int hidden, int inter, int n_heads, int n_kv_heads,
                              int head_dim, int vocab, int max_seq, float eps, float theta,
                              int n_seq, int nthreads) {
+  // The reference sizes its attention output buffer by HiddenSize
+  // (Transformer.cs:50) and so needs HiddenSize == NumAttentionHeads * HeadDim;
+  // it would throw on other shapes, the restatement refuses them.
+  if (hidden != n_heads * head_dim) return nullptr;
   OrModel* m = new OrModel();
   m->c = {n_layers, hidden, inter, n_heads, n_kv_heads, head_dim, vocab, max_seq, eps, theta};
   m->n_seq = n_seq;

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 
 def test_gguf_model_decodes_like_the_synthetic_model(ctx, tmp_path):
-    cfg = config(2, 512, 1024, 8, 2, 1000, 128, 1)
+    cfg = config(2, 1024, 1024, 8, 2, 1000, 128, 1)
     path = tmp_path / "m.gguf"
     write_llama_gguf(path, cfg, 7)
     with GGUFFile(path) as f:
