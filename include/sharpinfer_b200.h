@@ -55,8 +55,12 @@ typedef enum {
 typedef enum {
   SI_F32 = 0,
   SI_F16 = 1,
+  SI_Q4_0 = 2,
   SI_Q8_0 = 8,
+  SI_Q2_K = 10,
+  SI_Q3_K = 11,
   SI_Q4_K = 12,
+  SI_Q5_K = 13,
   SI_Q6_K = 14
 } si_qtype;
 
@@ -102,7 +106,12 @@ SI_EXPORT int si_synchronize(si_ctx* ctx);
  * The bytes are what SharpInfer's loader hands to Dequantize.DequantizeTensor
  * (Quantization.cs:415-469); they are re-ordered on the device into the
  * kernel layout (same byte count) and never expanded to f32.  cols must be a
- * multiple of the block size. */
+ * multiple of the block size.
+ * Q4_0, Q2_K, Q3_K and Q5_K (cols a multiple of 256) are kept in their GGUF
+ * block layout -- GGML's, as gguf-py decodes it: Q2_K [scales][qs][d][dmin],
+ * Q3_K [hmask][qs][scales][d], Q5_K [d][dmin][scales][qh][qs] (the
+ * reference's Quantization.cs:176-356 reads these three at other offsets) --
+ * and serve si_dequant, si_qmatvec / si_qmatvec_host and si_qgemm. */
 SI_EXPORT int si_weight_upload(si_ctx* ctx, int qtype, const void* blocks_host, int64_t rows,
                                int64_t cols, si_weight** out);
 

@@ -20,6 +20,7 @@ _SIGS = {
     "or_block_size": (_i32, [_i32]),
     "or_block_bytes": (_i32, [_i32]),
     "or_dequant_tensor": (_i32, [_i32, _c_p, _i64, _c_p]),
+    "or_dequant_reference_as_written": (_i32, [_i32, _c_p, _i64, _c_p]),
     "or_dot": (_f32, [_c_p, _c_p, _i32]),
     "or_matvec_f32": (None, [_c_p, _c_p, _c_p, _i64, _i32, _i32]),
     "or_qmatvec": (_i32, [_i32, _c_p, _i64, _i32, _c_p, _c_p, _i32, _i32]),
@@ -81,6 +82,15 @@ def dequant(qtype, blocks, n):
     out = np.empty(n, dtype=np.float32)
     rc = load().or_dequant_tensor(qtype, _p(np.ascontiguousarray(blocks, np.uint8)), n, _p(out))
     if rc:
+        raise ValueError("oracle: unsupported type %d" % qtype)
+    return out
+
+
+def dequant_reference_as_written(qtype, blocks, nblocks):
+    """The reference's own Q2_K / Q3_K / Q5_K decoders exactly as written
+    (their field offsets differ from GGML's); 256 values per block."""
+    out = np.empty(nblocks * 256, dtype=np.float32)
+    if load().or_dequant_reference_as_written(qtype, _p(np.ascontiguousarray(blocks, np.uint8)), nblocks, _p(out)):
         raise ValueError("oracle: unsupported type %d" % qtype)
     return out
 

@@ -32,7 +32,10 @@
 #define OR_API extern "C" __attribute__((visibility("default")))
 
 // QuantType values (Quantization.cs:6-22).
-enum { QT_F32 = 0, QT_F16 = 1, QT_Q8_0 = 8, QT_Q4_K = 12, QT_Q6_K = 14, QT_BF16 = 30 };
+enum {
+  QT_F32 = 0, QT_F16 = 1, QT_Q4_0 = 2, QT_Q8_0 = 8, QT_Q2_K = 10, QT_Q3_K = 11, QT_Q4_K = 12, QT_Q5_K = 13,
+  QT_Q6_K = 14, QT_BF16 = 30
+};
 
 // ---------------------------------------------------------------------------
 // Quantization.cs
@@ -70,15 +73,19 @@ static inline float half_at(const uint8_t* p) {
 // BlockSize / BlockBytes (Quantization.cs:31-65), the formats on this path.
 OR_API int or_block_size(int qt) {
   switch (qt) {
-    case QT_Q8_0: return 32;
-    case QT_Q4_K: case QT_Q6_K: return 256;
+    case QT_Q4_0: case QT_Q8_0: return 32;
+    case QT_Q2_K: case QT_Q3_K: case QT_Q4_K: case QT_Q5_K: case QT_Q6_K: return 256;
     default: return 1;
   }
 }
 OR_API int or_block_bytes(int qt) {
   switch (qt) {
+    case QT_Q4_0: return 18;
     case QT_Q8_0: return 34;
+    case QT_Q2_K: return 84;
+    case QT_Q3_K: return 110;
     case QT_Q4_K: return 144;
+    case QT_Q5_K: return 176;
     case QT_Q6_K: return 210;
     case QT_F16: case QT_BF16: return 2;
     case QT_F32: return 4;
@@ -151,6 +158,154 @@ static void dequant_q6_k_block(const uint8_t* b, float* out) {
   }
 }
 
+// DequantQ4_0 (Quantization.cs:71-83): out[j] = ((q & 0xF) - 8) * d,
+// out[j + 16] = ((q >> 4) - 8) * d.
+static void dequant_q4_0_block(const uint8_t* b, float* out) {
+  float scale = half_at(b);
+  for (int j = 0; j < 16; j++) {
+    out[j] = (float)((b[2 + j] & 0x0F) - 8) * scale;
+    out[j + 16] = (float)((b[2 + j] >> 4) - 8) * scale;
+  }
+}
+
+// Q2_K, Q3_K and Q5_K in the GGML block layouts a GGUF file holds.  The
+// reference's decoders (Quantization.cs:176-197, :205-267, :322-356) read
+// these fields at other offsets -- restated as written further below -- so
+// these follow the GGML layout, with the reference's arithmetic:
+//   Q2_K [scales 16][qs 64][f16 d][f16 dmin]: element 128n + 32s + 16h + l =
+//        (d * (sc & 15)) * ((qs[32n + 16h + l] >> 2s) & 3) - dmin * (sc >> 4),
+//        sc = scales[8n + 2s + h]
+//   Q3_K [hmask 32][qs 64][scales 12][f16 d]: the reference's scale unpacking
+//        and loop (Quantization.cs:205-267) with d read from byte 108
+//   Q5_K [f16 d][f16 dmin][scales 12][qh 32][qs 128]: the reference's loop
+//        (Quantization.cs:322-356) with qh at byte 16 and qs at byte 48
+static void dequant_q2_k_ggml(const uint8_t* b, float* out) {
+  const uint8_t* scales = b;
+  const uint8_t* qs = b + 16;
+  float d = half_at(b + 80), dmin = half_at(b + 82);
+  int outIdx = 0;
+  for (int n = 0; n < 2; n++)
+    for (int s = 0; s < 4; s++)
+      for (int h = 0; h < 2; h++) {
+        const uint8_t sc = scales[8 * n + 2 * s + h];
+        float dl = d * (float)(sc & 0xF);
+        float ml = dmin * (float)(sc >> 4);
+        for (int l = 0; l < 16; l++) out[outIdx++] = dl * (float)((qs[32 * n + 16 * h + l] >> (2 * s)) & 3) - ml;
+      }
+}
+
+static void q3_k_scales(const uint8_t* raw, int* scales) {
+  for (int i = 0; i < 4; i++) {
+    scales[i] = raw[i] & 0xF;
+    scales[i + 4] = raw[i + 4] & 0xF;
+    scales[i + 8] = raw[i] >> 4;
+    scales[i + 12] = raw[i + 4] >> 4;
+  }
+  for (int i = 0; i < 4; i++) {
+    uint8_t hi = raw[8 + i];
+    scales[i] |= ((hi >> 0) & 3) << 4;
+    scales[i + 4] |= ((hi >> 2) & 3) << 4;
+    scales[i + 8] |= ((hi >> 4) & 3) << 4;
+    scales[i + 12] |= ((hi >> 6) & 3) << 4;
+  }
+  for (int i = 0; i < 16; i++) scales[i] -= 32;
+}
+
+static void q3_k_body(float dAll, const uint8_t* hmask, const uint8_t* qs, const int* scales, float* out) {
+  int outIdx = 0, qOff = 0, scIdx = 0;
+  uint8_t m = 1;
+  for (int n = 0; n < 2; n++) {
+    int shift = 0;
+    for (int j = 0; j < 4; j++) {
+      float dl = dAll * (float)scales[scIdx];
+      for (int l = 0; l < 16; l++) {
+        int lo2 = (qs[qOff + l] >> shift) & 3, hb = (hmask[l] & m) ? 0 : -4;
+        out[outIdx++] = dl * (float)(lo2 + hb);
+      }
+      float dl2 = dAll * (float)scales[scIdx + 1];
+      for (int l = 16; l < 32; l++) {
+        int lo2 = (qs[qOff + l] >> shift) & 3, hb = (hmask[l] & m) ? 0 : -4;
+        out[outIdx++] = dl2 * (float)(lo2 + hb);
+      }
+      shift += 2;
+      m = (uint8_t)(m << 1);
+      scIdx += 2;
+    }
+    qOff += 32;
+  }
+}
+
+static void dequant_q3_k_ggml(const uint8_t* b, float* out) {
+  int scales[16];
+  q3_k_scales(b + 96, scales);
+  q3_k_body(half_at(b + 108), b, b + 32, scales, out);
+}
+
+static void q5_k_body(float d, float dmin, const uint8_t* scales, const uint8_t* qs, const uint8_t* qh, float* out) {
+  int outIdx = 0, qIdx = 0, scIdx = 0;
+  uint8_t u1 = 1, u2 = 2;
+  for (int j = 0; j < 4; j++) {
+    uint8_t sc1, m1, sc2, m2;
+    get_scale_min_k4(scIdx, scales, &sc1, &m1);
+    get_scale_min_k4(scIdx + 1, scales, &sc2, &m2);
+    float d1 = d * (float)sc1, m1f = dmin * (float)m1, d2 = d * (float)sc2, m2f = dmin * (float)m2;
+    for (int l = 0; l < 32; l++) {
+      int hi1 = (qh[l] & u1) ? 16 : 0, hi2 = (qh[l] & u2) ? 16 : 0;
+      out[outIdx + l] = d1 * (float)((qs[qIdx + l] & 0xF) + hi1) - m1f;
+      out[outIdx + l + 32] = d2 * (float)((qs[qIdx + l] >> 4) + hi2) - m2f;
+    }
+    outIdx += 64;
+    qIdx += 32;
+    scIdx += 2;
+    u1 = (uint8_t)(u1 << 2);
+    u2 = (uint8_t)(u2 << 2);
+  }
+}
+
+static void dequant_q5_k_ggml(const uint8_t* b, float* out) {
+  q5_k_body(half_at(b), half_at(b + 2), b + 4, b + 48, b + 16, out);
+}
+
+// The reference's DequantQ2_K / DequantQ3_K / DequantQ5_K exactly as written
+// (Quantization.cs:176-197, :205-267, :322-356): Q2_K reads [d][dmin][16
+// scales][64 qs] and emits, for each scale j, the four 2-bit fields of
+// qs[4j .. 4j + 3] in turn; Q3_K reads d from byte 0, hmask from 2, qs from
+// 34 and the scales from 98; Q5_K reads qs from byte 16 and qh from 144.
+// Kept to show where they part from the GGML layout above.
+OR_API int or_dequant_reference_as_written(int qt, const uint8_t* data, int64_t nblocks, float* out) {
+  for (int64_t i = 0; i < nblocks; i++) {
+    float* o = out + i * 256;
+    if (qt == QT_Q2_K) {
+      const uint8_t* b = data + i * 84;
+      float d = half_at(b), dmin = half_at(b + 2);
+      const uint8_t* scales = b + 4;
+      const uint8_t* qs = b + 20;
+      int outIdx = 0;
+      for (int j = 0; j < 16; j++) {
+        float sc = d * (float)(scales[j] & 0xF), m = dmin * (float)(scales[j] >> 4);
+        for (int l = 0; l < 4; l++) {
+          uint8_t q = qs[j * 4 + l];
+          o[outIdx++] = sc * (float)(q & 3) - m;
+          o[outIdx++] = sc * (float)((q >> 2) & 3) - m;
+          o[outIdx++] = sc * (float)((q >> 4) & 3) - m;
+          o[outIdx++] = sc * (float)((q >> 6) & 3) - m;
+        }
+      }
+    } else if (qt == QT_Q3_K) {
+      const uint8_t* b = data + i * 110;
+      int scales[16];
+      q3_k_scales(b + 98, scales);
+      q3_k_body(half_at(b), b + 2, b + 34, scales, o);
+    } else if (qt == QT_Q5_K) {
+      const uint8_t* b = data + i * 176;
+      q5_k_body(half_at(b), half_at(b + 2), b + 4, b + 16, b + 144, o);
+    } else {
+      return -1;
+    }
+  }
+  return 0;
+}
+
 // DequantizeTensor (Quantization.cs:415-469), restricted to the formats of
 // this path.  Returns 0 on success, -1 for an unsupported type.
 OR_API int or_dequant_tensor(int qt, const uint8_t* data, int64_t n, float* out) {
@@ -179,6 +334,10 @@ OR_API int or_dequant_tensor(int qt, const uint8_t* data, int64_t n, float* out)
       case QT_Q8_0: dequant_q8_0_block(blk, dst); break;
       case QT_Q4_K: dequant_q4_k_block(blk, dst); break;
       case QT_Q6_K: dequant_q6_k_block(blk, dst); break;
+      case QT_Q4_0: dequant_q4_0_block(blk, dst); break;
+      case QT_Q2_K: dequant_q2_k_ggml(blk, dst); break;
+      case QT_Q3_K: dequant_q3_k_ggml(blk, dst); break;
+      case QT_Q5_K: dequant_q5_k_ggml(blk, dst); break;
       default: return -1;
     }
   }

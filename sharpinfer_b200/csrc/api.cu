@@ -56,17 +56,18 @@ int ensure_pinned(si_ctx* c, size_t bytes) {
 }
 
 static int check_qtype(int qt) {
-  if (qt != SI_Q4_K && qt != SI_Q6_K && qt != SI_Q8_0)
-    SI_FAIL(SI_ERR_UNSUPPORTED, "quant type %d is not one of Q8_0(8), Q4_K(12), Q6_K(14)", qt);
+  if (qt != SI_Q4_K && qt != SI_Q6_K && qt != SI_Q8_0 && !raw_layout(qt))
+    SI_FAIL(SI_ERR_UNSUPPORTED,
+            "quant type %d is not one of Q4_0(2), Q8_0(8), Q2_K(10), Q3_K(11), Q4_K(12), Q5_K(13), Q6_K(14)", qt);
   return SI_OK;
 }
 
 static int check_shape(int qt, int64_t rows, int64_t cols) {
   if (rows <= 0 || cols <= 0) SI_FAIL(SI_ERR_INVALID, "weight shape %lldx%lld must be positive",
                                       (long long)rows, (long long)cols);
-  if (cols % block_elems(qt))
-    SI_FAIL(SI_ERR_INVALID, "cols=%lld is not a multiple of the %d-element block", (long long)cols,
-            block_elems(qt));
+  const int unit = raw_layout(qt) ? 256 : block_elems(qt);  // raw formats: 256-element units
+  if (cols % unit)
+    SI_FAIL(SI_ERR_INVALID, "cols=%lld is not a multiple of %d", (long long)cols, unit);
   if (cols > SI_MAX_K) SI_FAIL(SI_ERR_INVALID, "cols=%lld above the supported maximum %d",
                                (long long)cols, SI_MAX_K);
   if (rows > (int64_t)1 << 31) SI_FAIL(SI_ERR_INVALID, "rows=%lld too large", (long long)rows);
@@ -82,7 +83,8 @@ static int weight_alloc(si_ctx* c, int qt, int64_t rows, int64_t cols, si_weight
   w->cols = cols;
   w->tiles = (rows + 15) / 16;
   w->nblk = cols / block_elems(qt);
-  w->bytes = (size_t)(w->tiles * w->nblk * tile_block_bytes(qt));
+  w->bytes = raw_layout(qt) ? (size_t)(rows * w->nblk * gguf_block_bytes(qt))
+                            : (size_t)(w->tiles * w->nblk * tile_block_bytes(qt));
   w->device = c->device;
   cudaError_t e = cudaMalloc(&w->dev, w->bytes);
   if (e != cudaSuccess) {
@@ -237,7 +239,16 @@ SI_EXPORT int si_weight_upload(si_ctx* c, int qt, const void* blocks, int64_t ro
       st = SI_ERR_CUDA;
       break;
     }
-    st = launch_repack(c, qt, (const uint8_t*)c->stage[0].ptr, rows, cols, r0, nr, w->dev);
+    if (raw_layout(qt)) {  // kept as GGUF blocks
+      e = cudaMemcpyAsync((uint8_t*)w->dev + r0 * rb, c->stage[0].ptr, (size_t)(nr * rb), cudaMemcpyDeviceToDevice,
+                          c->stream);
+      if (e != cudaSuccess) {
+        set_error("weight upload copy failed: %s", cudaGetErrorString(e));
+        st = SI_ERR_CUDA;
+      }
+    } else {
+      st = launch_repack(c, qt, (const uint8_t*)c->stage[0].ptr, rows, cols, r0, nr, w->dev);
+    }
     if (st == SI_OK) {
       e = cudaStreamSynchronize(c->stream);  // staging is reused by the next chunk
       if (e != cudaSuccess) {
@@ -261,6 +272,7 @@ SI_EXPORT int si_weight_synth(si_ctx* c, int qt, int64_t rows, int64_t cols, uin
   if (!c || !out) SI_FAIL(SI_ERR_INVALID, "si_weight_synth: NULL argument");
   *out = nullptr;
   SI_TRY(bind_device(c));
+  if (raw_layout(qt)) SI_FAIL(SI_ERR_UNSUPPORTED, "si_weight_synth: no generator for quant type %d", qt);
   si_weight* w = nullptr;
   SI_TRY(weight_alloc(c, qt, rows, cols, &w));
   const int64_t rb = w->nblk * gguf_block_bytes(qt);
@@ -314,6 +326,7 @@ SI_EXPORT int si_synth_blocks_host(int qt, int64_t rows, int64_t cols, uint64_t 
   clear_error();
   if (!out) SI_FAIL(SI_ERR_INVALID, "si_synth_blocks_host: out is NULL");
   SI_TRY(check_qtype(qt));
+  if (raw_layout(qt)) SI_FAIL(SI_ERR_UNSUPPORTED, "si_synth_blocks_host: no generator for quant type %d", qt);
   if (rows <= 0 || cols <= 0 || cols % block_elems(qt))
     SI_FAIL(SI_ERR_INVALID, "bad synthetic shape %lldx%lld", (long long)rows, (long long)cols);
   const uint64_t key = si_key(seed, tag);
@@ -366,6 +379,7 @@ SI_EXPORT int si_dequant(si_ctx* c, const si_weight* w, float* out) {
   if (!c || !w || !out) SI_FAIL(SI_ERR_INVALID, "si_dequant: NULL argument");
   if (w->device != c->device) SI_FAIL(SI_ERR_INVALID, "si_dequant: weight lives on device %d, context on %d", w->device, c->device);
   SI_TRY(bind_device(c));
+  if (raw_layout(w->qtype)) return launch_dequant_raw(c->stream, w, out);
   return launch_dequant(c, w, out);
 }
 
@@ -389,6 +403,9 @@ SI_EXPORT int si_qmatvec_prepared(si_ctx* c, const si_weight* w, float* y, int b
   clear_error();
   if (!c || !w || !y) SI_FAIL(SI_ERR_INVALID, "si_qmatvec_prepared: NULL argument");
   if (w->device != c->device) SI_FAIL(SI_ERR_INVALID, "si_qmatvec: weight lives on device %d, context on %d", w->device, c->device);
+  if (raw_layout(w->qtype))
+    SI_FAIL(SI_ERR_UNSUPPORTED, "si_qmatvec_prepared: quant type %d multiplies f32 activations (si_qmatvec)",
+            w->qtype);
   if (c->prep_cols != w->cols || c->prep_batch != batch)
     SI_FAIL(SI_ERR_INVALID, "si_qmatvec_prepared: prepared activations are %dx%d, weight needs %dx%lld",
             c->prep_batch, c->prep_cols, batch, (long long)w->cols);
@@ -402,6 +419,12 @@ SI_EXPORT int si_qmatvec(si_ctx* c, const si_weight* w, const float* x, float* y
   clear_error();
   if (!c || !w || !x || !y) SI_FAIL(SI_ERR_INVALID, "si_qmatvec: NULL argument");
   if (batch < 1 || batch > SI_MAX_BATCH) SI_FAIL(SI_ERR_INVALID, "si_qmatvec: batch %d outside 1..%d", batch, SI_MAX_BATCH);
+  if (raw_layout(w->qtype)) {
+    if (w->device != c->device) SI_FAIL(SI_ERR_INVALID, "si_qmatvec: weight lives on device %d, context on %d",
+                                        w->device, c->device);
+    SI_TRY(bind_device(c));
+    return launch_qmv_raw(c->stream, w, x, y, batch);
+  }
   SI_TRY(si_act_prepare(c, x, w->cols, batch));
   return si_qmatvec_prepared(c, w, y, batch, 0);
 }

@@ -198,15 +198,25 @@ inline int64_t tile_block_bytes(int qt) {
     default: return 0;
   }
 }
-inline int block_elems(int qt) { return qt == SI_Q8_0 ? 32 : 256; }
+inline int block_elems(int qt) { return (qt == SI_Q8_0 || qt == SI_Q4_0) ? 32 : 256; }
 inline int gguf_block_bytes(int qt) {
   switch (qt) {
     case SI_Q4_K: return 144;
     case SI_Q6_K: return 210;
     case SI_Q8_0: return 34;
+    case SI_Q4_0: return 18;
+    case SI_Q2_K: return 84;
+    case SI_Q3_K: return 110;
+    case SI_Q5_K: return 176;
     default: return 0;
   }
 }
+// Formats kept on the device in their GGUF block layout (rawq.cu): dequant,
+// a warp-per-row matvec on f32 activations, and the GEMM's f16 pre-pass.
+inline bool raw_layout(int qt) { return qt == SI_Q4_0 || qt == SI_Q2_K || qt == SI_Q3_K || qt == SI_Q5_K; }
+int launch_qmv_raw(cudaStream_t s, const si_weight* w, const float* x, float* y, int B);
+int launch_dequant_raw(cudaStream_t s, const si_weight* w, float* out);
+int launch_dequant_raw_f16(cudaStream_t s, const si_weight* w, __half* out);
 
 // Kernel launchers (defined in the .cu files).
 int launch_repack(si_ctx* c, int qt, const uint8_t* gguf, int64_t rows, int64_t cols,

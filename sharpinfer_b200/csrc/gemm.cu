@@ -565,6 +565,7 @@ int make_tmap(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t cols, int 
 // f16 copy of W (rows x cols) at dst on the context stream.
 int dequant_f16(si_ctx* c, const si_weight* w, __half* dst) {
   const int64_t N = w->rows;
+  if (raw_layout(w->qtype)) return launch_dequant_raw_f16(c->stream, w, dst);
   if (w->qtype == SI_Q4_K) {
     const int64_t ntb = w->tiles * w->nblk;
     k_dequant_q4k_f16<<<(unsigned)((ntb + 7) / 8), 256, 0, c->stream>>>((const uint8_t*)w->dev, N, w->nblk, ntb, dst);

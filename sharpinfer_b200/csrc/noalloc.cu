@@ -75,6 +75,11 @@ int scratch_for(int dev, DeviceScratch* out) {
 }
 
 int run(const si_weight* w, const float* x, float* y, int batch, cudaStream_t s, int dev) {
+  if (raw_layout(w->qtype)) {  // GGUF-layout formats need no scratch at all
+    SI_TRY(launch_qmv_raw(s, w, x, y, batch));
+    SI_CUDA(cudaStreamSynchronize(s));
+    return SI_OK;
+  }
   DeviceScratch sc;
   SI_TRY(scratch_for(dev, &sc));
   const int K = (int)w->cols;

@@ -13,9 +13,10 @@ HEADER = os.path.join(os.path.dirname(_HERE), "include", "sharpinfer_b200.h")
 
 SI_OK = 0
 SI_F32, SI_F16, SI_Q8_0, SI_Q4_K, SI_Q6_K = 0, 1, 8, 12, 14
+SI_Q4_0, SI_Q2_K, SI_Q3_K, SI_Q5_K = 2, 10, 11, 13
 SYNTH_PLAIN, SYNTH_MODEL = 0, 1
-BLOCK_ELEMS = {SI_Q4_K: 256, SI_Q6_K: 256, SI_Q8_0: 32}
-BLOCK_BYTES = {SI_Q4_K: 144, SI_Q6_K: 210, SI_Q8_0: 34}
+BLOCK_ELEMS = {SI_Q4_K: 256, SI_Q6_K: 256, SI_Q8_0: 32, SI_Q4_0: 32, SI_Q2_K: 256, SI_Q3_K: 256, SI_Q5_K: 256}
+BLOCK_BYTES = {SI_Q4_K: 144, SI_Q6_K: 210, SI_Q8_0: 34, SI_Q4_0: 18, SI_Q2_K: 84, SI_Q3_K: 110, SI_Q5_K: 176}
 
 _c_p = ctypes.c_void_p
 _i32 = ctypes.c_int
