@@ -1,9 +1,11 @@
 """The C-ABI library loads and exports what include/sharpinfer_b200.h declares (no GPU)."""
 import ctypes
+import os
 
 import numpy as np
 import pytest
 
+from conftest import ROOT
 from sharpinfer_b200 import native as N
 from sharpinfer_b200.backend import synth_blocks_host, synth_f16_host, synth_f32_host
 
@@ -64,3 +66,25 @@ def test_model_recipe_is_zero_mean():
 def test_host_generator_rejects_bad_shapes(qt, rows, cols):
     with pytest.raises(N.SIError):
         synth_blocks_host(qt, rows, cols, 1, 1)
+
+
+def test_csharp_binding_names_exist_in_the_library():
+    """Every function the C# backend (sharpinfer_b200/csharp/B200Backend.cs)
+    imports is declared in the header and exported, with as many parameters
+    as the header gives it; its config struct has si_model_config's fields."""
+    import re
+    src = open(os.path.join(ROOT, "sharpinfer_b200", "csharp", "B200Backend.cs")).read()
+    header = open(N.HEADER).read()
+    imports = re.findall(r"public static extern \w+\*? (\w+)\(([^)]*)\);", src)
+    assert len(imports) >= 20
+    lib = N.load()
+    for name, params in imports:
+        assert hasattr(lib, name), name
+        m = re.search(r"SI_EXPORT[^;(]*\b%s\s*\(([^)]*)\)" % name, header)
+        assert m, name
+        n_h = 0 if m.group(1).strip() in ("", "void") else m.group(1).count(",") + 1
+        n_c = 0 if not params.strip() else params.count(",") + 1
+        assert n_h == n_c, (name, n_h, n_c)
+    struct = re.search(r"public struct B200ModelConfig\s*\{(.*?)\}", src, re.S).group(1)
+    fields = sum(line.count(",") + 1 for line in struct.split(";") if line.strip().startswith("public"))
+    assert fields == len(N.ModelConfig._fields_)
