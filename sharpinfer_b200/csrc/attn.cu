@@ -241,16 +241,10 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
     float m = 0.f;
     for (int d = lane; d < HD; d += 32) m = fmaxf(m, fabsf(qs[h * HD + d]));
     m = warp_max(m);
-    int e = 0;
-    if (m > 0.f && m <= 3.0e38f) {
-      int E;
-      frexpf(m, &E);
-      e = 14 - E;
-      e = e < -100 ? -100 : (e > 100 ? 100 : e);
-    }
+    const int e = unit_exponent(m);
     if (lane == 0) {
-      qsc[h] = a.scale * ldexpf(1.0f, -e);
-      qsc[8 + h] = ldexpf(1.0f, e);
+      qsc[h] = a.scale * exp2i(-e);
+      qsc[8 + h] = exp2i(e);
     }
   }
   __syncthreads();

@@ -41,17 +41,20 @@ __device__ __forceinline__ int64_t xprep_off(int mg, int nunit, int u, int LW) {
   return (int64_t)mg * nunit * xunit_bytes(XUNIT_LANES_FULL) + (int64_t)u * xunit_bytes(LW);
 }
 
-// Power-of-two exponent e of a unit: max |v 2^e| in [2^13, 2^14).
+// Power-of-two exponent e of a unit: max |v 2^e| in [2^13, 2^14).  E is
+// read from the exponent bits (amax < 2^E for a normal amax; a subnormal one
+// gives E = -126 and e is clamped either way).
 __device__ __forceinline__ int unit_exponent(float amax) {
   int e = 0;
   if (amax > 0.f && amax <= 3.0e38f) {
-    int E;
-    frexpf(amax, &E);  // amax < 2^E
+    const int E = (int)((__float_as_uint(amax) >> 23) & 0xFFu) - 126;
     e = 14 - E;
     e = e < -100 ? -100 : (e > 100 ? 100 : e);
   }
   return e;
 }
+// 2^e for |e| <= 126, exactly, from the exponent bits.
+__device__ __forceinline__ float exp2i(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
 
 // One warp packs the 256 values sv (shared memory, 16-byte aligned) of batch
 // column cb of an MMA group with LW lanes into `unit`.
@@ -60,7 +63,7 @@ __device__ __forceinline__ void pack_unit_warp(const float* sv, uint8_t* unit, i
   for (int i = lane; i < 256; i += 32) amax = fmaxf(amax, fabsf(sv[i]));
   amax = warp_max(amax);
   const int e = unit_exponent(amax);
-  const float sc = ldexpf(1.0f, e);
+  const float sc = exp2i(e);
 #pragma unroll
   for (int r = 0; r < 2; r++) {  // fragments: 8 groups x (hi, lo) x 4 lanes
     const int task = lane + 32 * r, jj = task >> 3, part = (task >> 2) & 1, t = task & 3;
@@ -83,7 +86,7 @@ __device__ __forceinline__ void pack_unit_warp(const float* sv, uint8_t* unit, i
     *(uint32_t*)(unit + 8 * LW * 16 + (8 * cb + 4 * part + t) * 4) =
         pack2(split_part(X0 * s5, part), split_part(X1 * s5, part));
   else if (lane == 8)
-    *(float*)(unit + 132 * LW + 4 * cb) = ldexpf(1.0f, -e);
+    *(float*)(unit + 132 * LW + 4 * cb) = exp2i(-e);
 }
 
 }  // namespace si

@@ -245,7 +245,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
   amax = 0.f;
   for (int i = 0; i < 8; i++) amax = fmaxf(amax, red[i]);
   const int e = unit_exponent(amax);
-  const float s = ldexpf(1.0f, e);
+  const float s = exp2i(e);
   uint8_t* unit = xprep + xprep_off(mg, nunit, u, LW);
   if (tid < 64) {  // fragments: 8 groups x (hi, lo) x 4 lanes
     const int jj = tid >> 3, part = (tid >> 2) & 1, t = tid & 3;
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(256) k_prep(const float* __restrict__ x, int l
       const float s5 = s * 0.03125f;
       *(uint32_t*)(unit + 8 * LW * 16 + L * 4) = pack2(split_part(X0 * s5, part), split_part(X1 * s5, part));
     } else if (lane == 8) {
-      *(float*)(unit + 132 * LW + 4 * cb) = ldexpf(1.0f, -e);
+      *(float*)(unit + 132 * LW + 4 * cb) = exp2i(-e);
     }
   }
   __syncthreads();
@@ -849,15 +849,17 @@ enum { Q1_PREPARED = 0, Q1_RMSNORM = 1, Q1_SILU = 2 };
 constexpr int Q1_SILU_MAX_UNITS = 64;  // 4 units per warp of 16
 
 // Fused RmsNorm + activation preparation of a batch-1 k_qmv1 launch: every
-// CTA normalises the whole input x (K <= 8192 columns, 4 x 16-byte loads per
+// CTA reads the whole input x (K <= NW * 512 columns, 4 x 16-byte loads per
 // thread; nwv holds this thread's norm weights, read before the dependency
-// wait) and packs its prepared units into shared memory exactly as k_prep
-// mode 1 does (TensorOps.RmsNorm, TensorOps.cs:135-145: scale = 1 /
-// sqrtf(ss / n + eps), out = (x * scale) * w).  The sum of squares is taken
-// in the same order by every CTA.
+// wait) and packs x * w into its prepared units in shared memory as k_prep
+// does.  RmsNorm (TensorOps.RmsNorm, TensorOps.cs:135-145) multiplies every
+// element by one scale, 1 / sqrtf(ss / n + eps); it is returned here and
+// applied to the matvec's outputs, so packing starts without waiting for the
+// sum of squares (the same products, rounded in another order: ~1e-7).  The
+// sum of squares is taken in the same order by every CTA.
 template <int NW>
-__device__ __forceinline__ void q1_rms_prep(const float* __restrict__ xf, const float4 (&nwv)[4], float eps, int nunit,
-                                            float* red, float* stage, uint8_t* xs) {
+__device__ __forceinline__ float q1_rms_prep(const float* __restrict__ xf, const float4 (&nwv)[4], float eps,
+                                             int nunit, float* red, float* stage, uint8_t* xs) {
   constexpr int XB = Q1Cfg::XB;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = nunit * 256;
   float4 xv[4];
@@ -865,6 +867,13 @@ __device__ __forceinline__ void q1_rms_prep(const float* __restrict__ xf, const 
   for (int j = 0; j < 4; j++) {
     const int i = 4 * tid + NW * 128 * j;
     xv[j] = i < K ? __ldcg((const float4*)(xf + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int i = 4 * tid + NW * 128 * j;
+    if (i < K)
+      *(float4*)(stage + i) = make_float4(__fmul_rn(xv[j].x, nwv[j].x), __fmul_rn(xv[j].y, nwv[j].y),
+                                          __fmul_rn(xv[j].z, nwv[j].z), __fmul_rn(xv[j].w, nwv[j].w));
   }
   float ss = 0.f;
 #pragma unroll
@@ -877,23 +886,13 @@ __device__ __forceinline__ void q1_rms_prep(const float* __restrict__ xf, const 
   ss = warp_sum(ss);
   if (lane == 0) red[warp] = ss;
   __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int w = 0; w < NW; w++) tot += red[w];
-  const float scale = 1.0f / sqrtf(tot / (float)K + eps);
-#pragma unroll
-  for (int j = 0; j < 4; j++) {
-    const int i = 4 * tid + NW * 128 * j;
-    if (i < K)
-      *(float4*)(stage + i) = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), nwv[j].x),
-                                          __fmul_rn(__fmul_rn(xv[j].y, scale), nwv[j].y),
-                                          __fmul_rn(__fmul_rn(xv[j].z, scale), nwv[j].z),
-                                          __fmul_rn(__fmul_rn(xv[j].w, scale), nwv[j].w));
-  }
-  __syncthreads();
   for (int u = warp; u < nunit; u += NW)  // one warp per 256-column unit
     pack_unit_warp(stage + 256 * u, xs + u * XB, 8, 0, lane);
   __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; w++) tot += red[w];
+  return 1.0f / sqrtf(tot / (float)K + eps);
 }
 
 // Fused SiLU * up + activation preparation of a batch-1 k_qmv1 launch (the
@@ -1023,11 +1022,12 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   }
   pdl_wait();
   bool ok = true;
+  float oscale = 1.f;  // RmsNorm's scale, applied to the outputs
   if (pmode == Q1_SILU) {  // xf: gate, nw: up
     q1_silu_prep<NW>(xf, nw, nunit, (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
   } else if (pmode != Q1_PREPARED) {
-    q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
-                    (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
+    oscale = q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
+                             (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
   } else if (rmode == 0) {
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(bar_x, (uint32_t)(nunit * XB));
@@ -1152,7 +1152,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
           p0b = b8;
           has0 = true;
         } else {
-          store_tile<EPI, 1>(y, rows, cT, lane, a, b8, scr.tp);
+          store_tile<EPI, 1>(y, rows, cT, lane, a * oscale, b8 * oscale, scr.tp);
         }
         tg = tg8 = 0.f;
         cU = 0;
@@ -1200,7 +1200,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
       b8 += part[(j * 2 + slot) * 64 + 32 + lane];
     }
     if (q0 >= cb && q1 <= ce) {  // the whole tile is in this CTA
-      store_tile<EPI, 1>(y, rows, T, lane, a, b8, scr.tp);
+      store_tile<EPI, 1>(y, rows, T, lane, a * oscale, b8 * oscale, scr.tp);
       continue;
     }
     // pair p lies in CTA ((p + 1) G - 1) / P (even-share mode only)
@@ -1233,7 +1233,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
             sb += vb[j];
           }
       }
-      store_tile<EPI, 1>(y, rows, T, lane, sa, sb, scr.tp);
+      store_tile<EPI, 1>(y, rows, T, lane, sa * oscale, sb * oscale, scr.tp);
       if (lane == 0) scr.count[T] = 0;
     }
   }
