@@ -49,6 +49,7 @@ KV_LEN = 4096
 START_TOKEN = 128000
 KV_LEN_70B = 8192
 NCHECK = 16  # greedy tokens decoded first from START_TOKEN and reported (tokens_check)
+BATCH16 = 16  # sequences of the 70B batch decode
 METRIC = "decode tok/s + Q4_K matvec HBM GB/s (8B Q4_K_M 1 GPU; 70B TP at 2/4/8)"
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate/up k_qmv1 launch
 # (28672 x 4096 Q4_K, batch 1) from an ncu --set full capture of
@@ -98,14 +99,15 @@ class Cfg:
                       self.max_seq, self.max_batch)
 
 
-def token_bytes(cfg, ctx_len):
+def token_bytes(cfg, ctx_len, batch=1):
     """Algorithmic bytes one decode step reads: every weight once, the KV
-    cache up to ctx_len, the embedding row, norms and activations ignored."""
+    cache of each of the batch's sequences up to ctx_len, the embedding rows,
+    norms and activations ignored."""
     h, i, L = cfg.hidden, cfg.intermediate, cfg.n_layers
     qkv = (cfg.n_heads + 2 * cfg.n_kv_heads) * cfg.head_dim
     per_layer = q4k_bytes(qkv, h) + q4k_bytes(h, cfg.n_heads * cfg.head_dim) + q4k_bytes(2 * i, h) + q4k_bytes(h, i)
     kv = 2 * ctx_len * cfg.n_kv_heads * cfg.head_dim * 2
-    return L * (per_layer + kv) + q6k_bytes(cfg.vocab, h)
+    return L * (per_layer + batch * kv) + q6k_bytes(cfg.vocab, h)
 
 
 class ClockSampler:
@@ -164,8 +166,8 @@ def llama8b(max_seq):
     return Cfg(32, 4096, 14336, 32, 8, 128256, max_seq)
 
 
-def llama70b(max_seq):
-    return Cfg(80, 8192, 28672, 64, 8, 128256, max_seq)
+def llama70b(max_seq, max_batch=1):
+    return Cfg(80, 8192, 28672, 64, 8, 128256, max_seq, max_batch)
 
 
 def model_cfg(args):
@@ -173,7 +175,8 @@ def model_cfg(args):
     # step counts in the usual range, so every run of one model (any N, any
     # K/W up to a few hundred) builds the same cache and attention split plan.
     cap = args.ctx + 1024 * max(1, -(-positions_needed(args) // 1024))
-    c = llama70b(cap) if args.model == "70b" else llama8b(cap)
+    # the 70B model holds BATCH16 sequences: batch 1 and batch 16 run on one copy of the weights
+    c = llama70b(cap, BATCH16) if args.model == "70b" else llama8b(cap)
     if args.layers and args.layers != c.n_layers:
         c = c.cut(args.layers)
     return c
@@ -422,6 +425,31 @@ def prefill_set(ctx, torch, dev, M, reps):
                           "tflops": round(att_flops / att_ms / 1e9, 1)}}
 
 
+def decode_batch16(ctx, torch, m, cfg, pos0, steps=16):
+    """BATCH16 sequences (prefilled KV, distinct start tokens) decoded
+    together from pos0: the first 4 greedy tokens of every sequence, then
+    ms per step of a graph-replayed greedy loop timed with CUDA events."""
+    toks = [(START_TOKEN + 7919 * b) % cfg.vocab for b in range(BATCH16)]
+    chk = m.generate(toks, pos0, 4)
+    w = m.generate([int(v) for v in chk[-1]], pos0 + 4, 3)
+    s = ctx.torch_stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ctx.synchronize()
+    e0.record(s)
+    m.generate([int(v) for v in w[-1]], pos0 + 7, steps)
+    e1.record(s)
+    ctx.synchronize()
+    return e0.elapsed_time(e1) / steps, [[int(v) for v in row] for row in chk.T]
+
+
+def batch16_entry(cfg, ctx_len, ms, steps, world, tokens):
+    peak, _ = measured_peaks()
+    tb = token_bytes(cfg, ctx_len + 7 + steps // 2, BATCH16)
+    return {"batch": BATCH16, "tok_s": round(BATCH16 * 1e3 / ms, 2), "ms_per_step": round(ms, 3), "steps": steps,
+            "bytes_per_step": tb, "decode_roofline_frac": round(tb / (ms * 1e-3) / 1e9 / (peak * world), 4),
+            "tokens_check": tokens}
+
+
 def tp1_70b(ctx, torch, args):
     """The 70B model decoded on this one GPU: its first NCHECK greedy tokens
     (the tensor-parallel runs must produce the same ones) and tok/s of a
@@ -447,12 +475,14 @@ def tp1_70b(ctx, torch, args):
     e1.record(s)
     ctx.synchronize()
     ms = e0.elapsed_time(e1) / n
+    ms16, chk16 = decode_batch16(ctx, torch, m, cfg, a70.ctx)
     m.free()
     peak, _ = measured_peaks()
     tb = token_bytes(cfg, a70.ctx + NCHECK + 3 + n // 2)
     return {"workload": workload_name(a70, 1), "tok_s": round(1e3 / ms, 2), "ms_per_token": round(ms, 3),
             "steps": n, "decode_roofline_frac": round(tb / (ms * 1e-3) / 1e9 / peak, 4),
-            "tokens_check": [int(v) for v in chk[:, 0]]}
+            "tokens_check": [int(v) for v in chk[:, 0]],
+            "batch16": batch16_entry(cfg, a70.ctx, ms16, 16, 1, chk16)}
 
 
 def tp_parity_gpu(ctx, args, world, rank):
@@ -460,7 +490,7 @@ def tp_parity_gpu(ctx, args, world, rank):
     size, heads, FFN and vocabulary; ctx 8192): 4 greedy steps with logits.
     Returns (tokens, this rank's logit slices)."""
     from sharpinfer_b200.model import DecodeModel, exchange_handles
-    cfg = llama70b(KV_LEN_70B + 1024).cut(2)
+    cfg = llama70b(KV_LEN_70B + 1024, BATCH16).cut(2)
     m = DecodeModel(ctx, cfg.native(), tp=world, rank=rank)
     m.synth(SEED)
     m.kv_synth(KV_LEN_70B, SEED)
@@ -470,6 +500,11 @@ def tp_parity_gpu(ctx, args, world, rank):
         out, lg = m.step([toks[-1]], KV_LEN_70B + s, logits=True)
         toks.append(int(out[0]))
         logits.append(lg[0].copy())
+    # one batch-16 step: every sequence from its own prefilled KV
+    t16 = [(START_TOKEN + 7919 * b) % cfg.vocab for b in range(BATCH16)]
+    out16, lg16 = m.step(t16, KV_LEN_70B, logits=True)
+    logits.append(lg16.copy())
+    toks.append([t16, [int(v) for v in out16]])
     ctx.synchronize()
     return m, toks, logits
 
@@ -483,16 +518,26 @@ def tp_parity_check(toks, slices):
         a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
         return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
-    cfg = llama70b(KV_LEN_70B + 1024).cut(2)
-    om = oracle.synthetic_model(cfg, SEED, n_seq=1, kv_len=KV_LEN_70B)
+    cfg = llama70b(KV_LEN_70B + 1024, BATCH16).cut(2)
+    om = oracle.synthetic_model(cfg, SEED, n_seq=BATCH16, kv_len=KV_LEN_70B)
     worst, equal = 0.0, True
     for s in range(4):
         lg = np.concatenate([sl[s] for sl in slices])
         ref = om.forward(0, toks[s], KV_LEN_70B + s)
         worst = max(worst, rel_l2(lg, ref))
         equal = equal and (toks[s + 1] == oracle.argmax(ref))
-    return {"workload": "Llama-3-70B arch cut to 2 layers, TP over all GPUs, ctx %d, 4 greedy steps" % KV_LEN_70B,
-            "max_rel_l2": float("%.3g" % worst), "tokens_equal": bool(equal), "tokens": toks[1:], "bar": 1e-3}
+    t16, out16 = toks[5]
+    lg16 = np.concatenate([sl[4] for sl in slices], axis=1)
+    worst16, equal16 = 0.0, True
+    for b in range(BATCH16):
+        ref = om.forward(b, t16[b], KV_LEN_70B)
+        worst16 = max(worst16, rel_l2(lg16[b], ref))
+        equal16 = equal16 and (out16[b] == oracle.argmax(ref))
+    return {"workload": "Llama-3-70B arch cut to 2 layers, TP over all GPUs, ctx %d: 4 greedy steps at batch 1, "
+                        "then one step at batch %d" % (KV_LEN_70B, BATCH16),
+            "max_rel_l2": float("%.3g" % worst), "tokens_equal": bool(equal), "tokens": toks[1:5],
+            "batch16_max_rel_l2": float("%.3g" % worst16), "batch16_tokens_equal": bool(equal16),
+            "batch16_tokens": out16, "bar": 1e-3}
 
 
 def run_ours(args, world, rank, local):
@@ -549,6 +594,11 @@ def run_ours(args, world, rank, local):
         pos += 1
     e2e_ms = (time.perf_counter() - w0) * 1e3 / args.steps
     kernels_per_step = m.step_kernels(1)
+    ms16, chk16 = 0.0, None
+    if args.model == "70b" and not args.no_extras:  # the same model at batch 16 (from the prefilled KV again)
+        if world > 1:
+            dist.barrier()
+        ms16, chk16 = decode_batch16(ctx, torch, m, cfg, args.ctx)
     ctx.synchronize()
     if world > 1:
         dist.barrier()  # every rank is done with the peers' buffers before any is freed
@@ -556,10 +606,10 @@ def run_ours(args, world, rank, local):
     # the dominant kernel: this rank's fused gate/up matvec
     gu_rows, gu_cols = 2 * cfg.intermediate // world, cfg.hidden
     kern_ms, kern_bytes = matvec_roofline(ctx, torch, dev, gu_rows, gu_cols)
-    t = torch.tensor([ms, e2e_ms, kern_ms], device=dev)
+    t = torch.tensor([ms, e2e_ms, kern_ms, ms16], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, kern_ms = t.tolist()
+    ms, e2e_ms, kern_ms, ms16 = t.tolist()
 
     extra = {}
     par = None
@@ -619,6 +669,9 @@ def run_ours(args, world, rank, local):
         "clocks": clk,
         "tokens_check": [int(v) for v in chk[:, 0]],
     }
+    if chk16 is not None:
+        line["batch16"] = batch16_entry(cfg, args.ctx, ms16, 16, world, chk16)
+        line["batch16"]["workload"] = workload_name(args, world).replace("batch 1,", "batch %d," % BATCH16)
     line.update(extra)
     if par is not None:
         line["parity"] = tp_parity_check(par[0], par[1])

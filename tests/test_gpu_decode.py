@@ -149,3 +149,15 @@ def test_generate_matches_stepping(ctx):
             tok = oracle.argmax(om.forward(b, tok, 30 + s))
             assert tok == gen[s, b]
     m.free()
+
+
+def test_decode_70b_shapes_batch16_ctx8192(ctx):
+    """Llama-3-70B layer shapes (hidden 8192, 64/8 heads, FFN 28672, vocab
+    128256) cut to one layer, 16 sequences each with its own 8192-position
+    KV prefix, two greedy steps: the batch-16 path of every kernel (the
+    tensor-core Q4_K matvec, batch attention, Q6_K lm_head) against the
+    oracle per sequence."""
+    cfg = config(1, 8192, 28672, 64, 8, 128256, 8200, 16)
+    starts = [(128000 + 7919 * b) % 128256 for b in range(16)]
+    worst = run_parity(ctx, cfg, kv_len=8192, steps=2, start_tokens=starts)
+    assert worst < 2e-5, worst
