@@ -125,7 +125,7 @@ inline void qmv_scratch_need(int64_t tiles, int64_t nunit, int sms, size_t* spli
     if (maxc > worst) worst = maxc;
   }
   *split_bytes = (size_t)tiles * worst * 64 * 4;
-  const size_t tc = (size_t)sms * 2 * 2048 * 4;  // k_qmv_tc: two row-block partials per CTA
+  const size_t tc = (size_t)sms * 2 * 4096 * 4;  // k_qmv_wide: two row-block partials per CTA
   if (*split_bytes < tc) *split_bytes = tc;
   *counts = tiles;
 }
@@ -248,12 +248,13 @@ inline size_t xprep_bytes(int K, int B) {
 int launch_prep(cudaStream_t s, const float* x, int ldx, const float* x2, const float* norm_w,
                 float eps, int mode, int K, int B, float* xout, uint8_t* xprep, bool pdl,
                 const PrepTp* tpp = nullptr);
-// Batch 5..16 Q4_K matvec on the tensor cores (k_qmv_tc); -1 when the
-// weight, batch or scratch does not suit it.  Switched off by
-// SHARPINFER_B200_QMV_TC=0 (the mma.sync kernel then runs).
-int launch_qmv_tc(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
-                  const QmvBuffers& qb, bool pdl);
-bool qmv_tc_enabled();
+// Batch 5..16 Q4_K / Q6_K matvec over 256-row blocks (k_qmv_wide); -1 when
+// the weight, batch or scratch does not suit it.  Switched off by
+// SHARPINFER_B200_QMV_WIDE=0 (the one-tile-per-CTA kernel then runs); taken
+// from 7168 rows up unless SHARPINFER_B200_QMV_WIDE=2.
+int launch_qmv_wide(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
+                    const QmvBuffers& qb, bool pdl);
+bool qmv_wide_enabled();
 int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, int epi,
                const QmvBuffers& qb, bool pdl);
 // y (op)= W RmsNorm(x) nw for a single row x (batch 1); xprep is the fallback's

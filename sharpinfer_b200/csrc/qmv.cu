@@ -1521,8 +1521,8 @@ int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
   const ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.ring_mode, qb.q1w}, qb.split_bytes, qb.count_n};
   if (epi == SI_EPI_TP && (qb.tp.tp < 1 || !qb.tp.peers || !qb.tp.epoch))
     SI_FAIL(SI_ERR_INVALID, "qmatvec: tensor-parallel epilogue without peers");
-  if (B > 4 && w->qtype == SI_Q4_K && qmv_tc_enabled()) {  // tensor-core kernel for batch 5..16
-    const int r = launch_qmv_tc(s, w, xprep, B, y, epi, qb, pdl);
+  if (B > 4 && (w->qtype == SI_Q4_K || w->qtype == SI_Q6_K) && qmv_wide_enabled()) {  // batch 5..16
+    const int r = launch_qmv_wide(s, w, xprep, B, y, epi, qb, pdl);
     if (r >= 0) return r;
   }
   if (epi == SI_EPI_ADD) return dispatch_qt<SI_EPI_ADD>(s, w, xprep, B, y, scr, qb.sms, pdl);

@@ -1,11 +1,12 @@
-"""Batch 5..16 Q4_K matvec on the tensor cores (k_qmv_tc) against the
-oracle's TensorOps.MatVecMul (src/SharpInfer.Core/Tensors/TensorOps.cs:20-72)
-over the dequantised weights (Quantization.cs:273-314).
+"""Batch 5..16 Q4_K / Q6_K matvec over 256-row blocks (k_qmv_wide) against
+the oracle's TensorOps.MatVecMul (src/SharpInfer.Core/Tensors/TensorOps.cs:20-72)
+over the dequantised weights (Quantization.cs:273-314, 362-398).
 
-Shapes cover: row counts that are not a multiple of the 128-row block (the
-last block partly empty), row blocks whose units are split between CTAs
-(combined by the last CTA to arrive), the Llama-3-8B gate/up and down shapes
-and a 70B tensor-parallel vocabulary slice (16032 rows)."""
+Shapes cover: row counts that are not a multiple of the 256-row block (the
+last block partly empty, odd tile counts), row blocks whose units are split
+between CTAs (combined by the last CTA to arrive), the Llama-3-8B gate/up,
+down and lm_head shapes and a 70B tensor-parallel vocabulary slice (16032
+rows)."""
 import numpy as np
 import pytest
 
@@ -18,35 +19,44 @@ pytestmark = pytest.mark.gpu
 Q4K = N.SI_Q4_K
 
 
-def _run(ctx, rows, cols, batch, seed=77, scale=1.0):
+@pytest.fixture(autouse=True)
+def _force_wide(monkeypatch):
+    """Route every shape to k_qmv_wide (by default it takes 7168 rows and up)."""
+    monkeypatch.setenv("SHARPINFER_B200_QMV_WIDE", "2")
+QTS = [N.SI_Q4_K, N.SI_Q6_K]
+
+
+def _run(ctx, rows, cols, batch, seed=77, scale=1.0, qt=Q4K):
     import torch
-    blocks = synth_blocks_host(Q4K, rows, cols, seed, 3, N.SYNTH_PLAIN, 0.01)
+    blocks = synth_blocks_host(qt, rows, cols, seed, 3, N.SYNTH_PLAIN, 0.01)
     x = (synth_f32_host(batch * cols, seed, 100 + batch).reshape(batch, cols) * np.float32(scale)).astype(np.float32)
-    ref = oracle.qmatvec(Q4K, blocks, rows, cols, x)
-    w = ctx.upload(Q4K, blocks, rows, cols)
+    ref = oracle.qmatvec(qt, blocks, rows, cols, x)
+    w = ctx.upload(qt, blocks, rows, cols)
     y = ctx.qmatvec(w, torch.from_numpy(x).cuda())
     ctx.synchronize()
     return y.cpu().numpy(), ref, w, x
 
 
-@pytest.mark.parametrize("batch", [5, 8, 9, 12, 16])
+@pytest.mark.parametrize("qt", QTS)
+@pytest.mark.parametrize("batch", [5, 7, 8, 9, 12, 13, 16])
 @pytest.mark.parametrize("rows,cols", [(16, 256), (200, 512), (1040, 1024), (4096, 4096), (16032, 1024)])
-def test_tc_matvec_parity(ctx, rows, cols, batch):
-    y, ref, _, _ = _run(ctx, rows, cols, batch)
+def test_wide_matvec_parity(ctx, rows, cols, batch, qt):
+    y, ref, _, _ = _run(ctx, rows, cols, batch, qt=qt)
     for b in range(batch):
         assert rel_l2(y[b], ref[b]) < 2e-5, (b, rel_l2(y[b], ref[b]))
 
 
-@pytest.mark.parametrize("rows,cols", [(28672, 4096), (4096, 14336)])
-def test_tc_matvec_llama8b_shapes_batch16(ctx, rows, cols):
-    y, ref, _, _ = _run(ctx, rows, cols, 16, seed=5)
+@pytest.mark.parametrize("rows,cols,qt", [(28672, 4096, Q4K), (4096, 14336, Q4K), (128256, 4096, N.SI_Q6_K)])
+def test_wide_matvec_llama8b_shapes_batch16(ctx, rows, cols, qt):
+    y, ref, _, _ = _run(ctx, rows, cols, 16, seed=5, qt=qt)
     assert rel_l2(y, ref) < 2e-5
 
 
-def test_tc_matvec_is_deterministic(ctx):
+@pytest.mark.parametrize("qt", QTS)
+def test_wide_matvec_is_deterministic(ctx, qt):
     import torch
     rows, cols, batch = 4096, 4096, 16
-    w = ctx.synth_weight(Q4K, rows, cols, 3, 4)
+    w = ctx.synth_weight(qt, rows, cols, 3, 4)
     x = torch.from_numpy(synth_f32_host(batch * cols, 3, 5).reshape(batch, cols)).cuda()
     ys = [ctx.qmatvec(w, x).cpu().numpy() for _ in range(3)]
     ctx.synchronize()
@@ -54,12 +64,12 @@ def test_tc_matvec_is_deterministic(ctx):
 
 
 @pytest.mark.parametrize("scale", [1e-20, 3e3, 1e30])
-def test_tc_matvec_activation_range(ctx, scale):
+def test_wide_matvec_activation_range(ctx, scale):
     y, ref, _, _ = _run(ctx, 512, 1024, 11, seed=9, scale=scale)
     assert rel_l2(y, ref) < 2e-5
 
 
-def test_tc_matvec_accumulates(ctx):
+def test_wide_matvec_accumulates(ctx):
     """The residual-add epilogue: out += W x for every batch row."""
     import torch
     rows, cols, batch = 640, 2048, 13
