@@ -259,6 +259,11 @@ int launch_qmv(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, 
                const QmvBuffers& qb, bool pdl);
 // y (op)= W RmsNorm(x) nw for a single row x (batch 1); xprep is the fallback's
 // prepared-activation buffer.
+// Tensor parallel, batch 1: y = W RmsNorm(xres + the ranks' partial sums) nw,
+// the new residual written to xout, in one batch-1 Q4_K kernel; -1 when that
+// kernel does not apply (then k_prep's SI_PREP_RMSNORM_TP and a matvec).
+int launch_qmv_rms_tp(cudaStream_t s, const si_weight* w, const float* xres, float* xout, const float* nw, float eps,
+                      float* y, const QmvBuffers& qb, const PrepTp& pt, bool pdl);
 int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const float* nw, float eps, float* y,
                    int epi, const QmvBuffers& qb, uint8_t* xprep, bool pdl);
 // y (op)= W (SiLU(gate) * up) for one row (batch 1).

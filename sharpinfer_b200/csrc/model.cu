@@ -240,14 +240,18 @@ float recipe_sigma(int qt, int recipe, int64_t cols) {
 //                          its input is prepared
 //   SI_PLAN_Q1_8WARPS      batch-1 matvec CTAs of 8 warps instead of 16, so a
 //                          CTA of the following kernel fits beside one
+//   SI_PLAN_TP_PREP_APART  tensor parallel, batch 1: the residual + partial
+//                          sums and RmsNorm in a k_prep launch of their own
+//                          instead of inside the qkv / gate-up matvec
 enum : unsigned {
   SI_PLAN_MERGE_IN_ATTN = 1, SI_PLAN_SILU_IN_DOWN = 2, SI_PLAN_L2_PREFETCH = 4, SI_PLAN_SELF_PREFETCH = 8,
-  SI_PLAN_Q1_8WARPS = 16, SI_PLAN_FULL_RING = 32
+  SI_PLAN_Q1_8WARPS = 16, SI_PLAN_FULL_RING = 32, SI_PLAN_TP_PREP_APART = 64
 };
 constexpr unsigned SI_PLAN_DEFAULT = 0;
 
 // The plan: SHARPINFER_B200_STEP_PLAN (a comma-separated subset of "merge",
-// "silu", "prefetch", or "none") when set, else SI_PLAN_DEFAULT.
+// "silu", "prefetch", "selfprefetch", "w8", "fullring", "tpapart", or
+// "none") when set, else SI_PLAN_DEFAULT.
 unsigned step_plan() {
   const char* e = getenv("SHARPINFER_B200_STEP_PLAN");
   if (!e) return SI_PLAN_DEFAULT;
@@ -258,6 +262,7 @@ unsigned step_plan() {
   if (strstr(e, "selfprefetch")) p |= SI_PLAN_SELF_PREFETCH;
   if (strstr(e, "w8")) p |= SI_PLAN_Q1_8WARPS;
   if (strstr(e, "fullring")) p |= SI_PLAN_FULL_RING;
+  if (strstr(e, "tpapart")) p |= SI_PLAN_TP_PREP_APART;
   return p;
 }
 
@@ -534,6 +539,7 @@ int enqueue_step(si_model* m, int B) {
   QmvBuffers qb = m->c->qmv();
   qb.ring_mode = (m->plan & SI_PLAN_SELF_PREFETCH) ? 2 : (m->plan & SI_PLAN_FULL_RING) ? 1 : 0;
   qb.q1w = (m->plan & SI_PLAN_Q1_8WARPS) ? 8 : 16;
+  const bool tp_fused = !(m->plan & SI_PLAN_TP_PREP_APART);
   // Each kernel may prefetch into L2 the weights of the kernel two launches
   // later: gate/up(l) -> qkv(l+1), down(l) -> Wo(l+1), attention(l) ->
   // gate/up(l), Wo(l) -> down(l).
@@ -550,10 +556,17 @@ int enqueue_step(si_model* m, int B) {
   for (int l = 0; l < L; l++) {
     const si_weight* qkv_next = l + 1 < L ? m->wqkv[l + 1] : nullptr;
     const si_weight* wo_next = l + 1 < L ? m->wo[l + 1] : nullptr;
+    bool qkv_done = false, gu_done = false;  // matvecs that took their RmsNorm in
     if (tp && l > 0) {
       const PrepTp pt = tp_consumer(m, l - 1, 1);
-      SI_TRY(launch_prep(s, m->x2, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
-                         m->x, m->xprep, true, &pt));
+      const int r = B == 1 && tp_fused ? launch_qmv_rms_tp(s, m->wqkv[l], m->x2, m->x, norm_ptr(m, l, SI_T_ATTN_NORM),
+                                                          c.rms_eps, m->qkv, qb, pt, true)
+                                       : -1;
+      if (r > 0) return r;
+      qkv_done = r == 0;
+      if (!qkv_done)
+        SI_TRY(launch_prep(s, m->x2, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
+                           m->x, m->xprep, true, &pt));
     } else if (!tp && B == 1) {  // RmsNorm inside the matvec where the kernel allows
       SI_TRY(launch_qmv_rms(s, m->wqkv[l], m->x, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, m->qkv, SI_EPI_STORE, qb,
                             m->xprep, true));
@@ -561,14 +574,20 @@ int enqueue_step(si_model* m, int B) {
       SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_ATTN_NORM), c.rms_eps, SI_PREP_RMSNORM, h, B,
                          nullptr, m->xprep, true));
     }
-    if (tp || B > 1) SI_TRY(launch_qmv(s, m->wqkv[l], m->xprep, B, m->qkv, SI_EPI_STORE, qb, true));
+    if ((tp || B > 1) && !qkv_done) SI_TRY(launch_qmv(s, m->wqkv[l], m->xprep, B, m->qkv, SI_EPI_STORE, qb, true));
     SI_TRY(enqueue_attention(m, l, m->qkv, nullptr, B, true, pre ? pf_of(m->wgu[l]) : L2Prefetch{}));
     if (tp) {
       SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, nullptr, SI_EPI_TP, with_pf(tp_producer(m, l, 0), m->wdown[l]),
                         true));
       const PrepTp pt = tp_consumer(m, l, 0);
-      SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
-                         m->x2, m->xprep, true, &pt));
+      const int r = B == 1 && tp_fused ? launch_qmv_rms_tp(s, m->wgu[l], m->x, m->x2, norm_ptr(m, l, SI_T_FFN_NORM),
+                                                          c.rms_eps, m->gu, with_pf(qb, qkv_next), pt, true)
+                                       : -1;
+      if (r > 0) return r;
+      gu_done = r == 0;
+      if (!gu_done)
+        SI_TRY(launch_prep(s, m->x, h, nullptr, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, SI_PREP_RMSNORM_TP, h, B,
+                           m->x2, m->xprep, true, &pt));
     } else {
       SI_TRY(launch_qmv(s, m->wo[l], m->xprep, B, m->x, SI_EPI_ADD, with_pf(qb, m->wdown[l]), true));
       if (B > 1)
@@ -578,7 +597,7 @@ int enqueue_step(si_model* m, int B) {
     if (!tp && B == 1)
       SI_TRY(launch_qmv_rms(s, m->wgu[l], m->x, norm_ptr(m, l, SI_T_FFN_NORM), c.rms_eps, m->gu, SI_EPI_STORE,
                             with_pf(qb, qkv_next), m->xprep, true));
-    else
+    else if (!gu_done)
       SI_TRY(launch_qmv(s, m->wgu[l], m->xprep, B, m->gu, SI_EPI_STORE, with_pf(qb, qkv_next), true));
     if (B == 1 && (m->plan & SI_PLAN_SILU_IN_DOWN)) {  // SiLU(gate) * up inside the down-projection matvec
       if (tp)

@@ -556,6 +556,8 @@ struct QmvScratch {
   L2Prefetch pf; // a later kernel's weights, prefetched into L2 at launch
   int ring_mode; // k_qmv1: when the ring is filled (see the kernel)
   int q1w;       // k_qmv1 warps per CTA (16, or 8)
+  PrepTp ptp;    // k_qmv1 Q1_RMSNORM_TP: the partial sums to add to the residual
+  float* xout;   // ... and where CTA 0 writes the new residual
 };
 
 template <int QT, int B, int NW, int NS>
@@ -837,7 +839,7 @@ struct Q1Cfg {
   __host__ __device__ static size_t part_off(int NW, int NS, int nunit) { return red_off(NW, NS, nunit) + 256; }
   static size_t smem(int NW, int NS, int nunit, int pmode) {
     const size_t part = (size_t)NW * 2 * 64 * 4;
-    const size_t stage = pmode == 1 ? (size_t)nunit * 256 * 4 : pmode == 2 ? (size_t)NW * 256 * 4 : 0;
+    const size_t stage = (pmode == 1 || pmode == 3) ? (size_t)nunit * 256 * 4 : pmode == 2 ? (size_t)NW * 256 * 4 : 0;
     return part_off(NW, NS, nunit) + (part > stage ? part : stage);
   }
 };
@@ -845,7 +847,9 @@ struct Q1Cfg {
 // Input preparation of a k_qmv1 launch: 0 = prepared units copied from
 // xprep, 1 = RmsNorm of x (q1_rms_prep).
 // 2 = SiLU(gate) * up of two f32 inputs (q1_silu_prep).
-enum { Q1_PREPARED = 0, Q1_RMSNORM = 1, Q1_SILU = 2 };
+// 3 = RmsNorm of the residual plus every rank's tensor-parallel partial sums
+// (SI_PREP_RMSNORM_TP's arithmetic); CTA 0 also writes the new residual.
+enum { Q1_PREPARED = 0, Q1_RMSNORM = 1, Q1_SILU = 2, Q1_RMSNORM_TP = 3 };
 constexpr int Q1_SILU_MAX_UNITS = 64;  // 4 units per warp of 16
 
 // Fused RmsNorm + activation preparation of a batch-1 k_qmv1 launch: every
@@ -857,9 +861,10 @@ constexpr int Q1_SILU_MAX_UNITS = 64;  // 4 units per warp of 16
 // applied to the matvec's outputs, so packing starts without waiting for the
 // sum of squares (the same products, rounded in another order: ~1e-7).  The
 // sum of squares is taken in the same order by every CTA.
-template <int NW>
+template <int NW, bool TPSUM>
 __device__ __forceinline__ float q1_rms_prep(const float* __restrict__ xf, const float4 (&nwv)[4], float eps,
-                                             int nunit, float* red, float* stage, uint8_t* xs) {
+                                             int nunit, float* red, float* stage, uint8_t* xs,
+                                             const PrepTp& tpp, float* __restrict__ xout) {
   constexpr int XB = Q1Cfg::XB;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, K = nunit * 256;
   float4 xv[4];
@@ -867,6 +872,40 @@ __device__ __forceinline__ float q1_rms_prep(const float* __restrict__ xf, const
   for (int j = 0; j < 4; j++) {
     const int i = 4 * tid + NW * 128 * j;
     xv[j] = i < K ? __ldcg((const float4*)(xf + i)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if constexpr (TPSUM) {
+    // residual + the ranks' partial sums in rank order, as SI_PREP_RMSNORM_TP
+    // adds them; each word awaited through its tag, four ranks' words of
+    // four elements in flight at a time
+    const unsigned want = *tpp.epoch * (unsigned)tpp.nlayers2 + (unsigned)tpp.flag_add;
+    const uint8_t* slot0 = tpp.comm + tpp.slots_off;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int i = 4 * tid + NW * 128 * j;
+      if (i >= K) continue;
+      float a[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
+      for (int r0 = 0; r0 < tpp.tp; r0 += 4) {
+        uint2 w[4][4];
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+          for (int e = 0; e < 4; e++)
+            w[r][e] = r0 + r < tpp.tp ? ld_tagged((const uint2*)(slot0 + (int64_t)(r0 + r) * tpp.src_stride) + i + e)
+                                      : make_uint2(0u, want);
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+          if (r0 + r >= tpp.tp) break;
+          const uint2* sl = (const uint2*)(slot0 + (int64_t)(r0 + r) * tpp.src_stride);
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            const uint32_t bits = (int)(w[r][e].y - want) >= 0 ? w[r][e].x : wait_tagged(sl + i + e, want, tpp.err);
+            a[e] = __fadd_rn(a[e], __uint_as_float(bits));
+          }
+        }
+      }
+      xv[j] = make_float4(a[0], a[1], a[2], a[3]);
+      if (blockIdx.x == 0) *(float4*)(xout + i) = xv[j];
+    }
   }
 #pragma unroll
   for (int j = 0; j < 4; j++) {
@@ -941,7 +980,7 @@ __device__ __forceinline__ float red4(float v) {
 // exact small integer -> f32: 2^23 + v as bits, minus 2^23
 __device__ __forceinline__ float magic_f(uint32_t bits) { return __uint_as_float(bits) - 8388608.f; }
 
-template <int EPI, int NW, int NS>
+template <int EPI, int NW, int NS, bool TPSUM>
 __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
     k_qmv1(const uint8_t* __restrict__ W, int nunit, int64_t rows, int tiles, int tile_mode,
            int pmode, const uint8_t* __restrict__ xprep, const float* __restrict__ xf, const float* __restrict__ nw,
@@ -1013,7 +1052,7 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   // pmode: prepared units in xprep, or the f32 input xf normalised here
   // with weights nw
   float4 nwv[4];
-  if (pmode == Q1_RMSNORM) {
+  if (pmode == Q1_RMSNORM || pmode == Q1_RMSNORM_TP) {
 #pragma unroll
     for (int j = 0; j < 4; j++) {  // norm weights: not written by any kernel of the step
       const int i = 4 * (int)threadIdx.x + NW * 128 * j;
@@ -1026,8 +1065,13 @@ __global__ void __launch_bounds__(NW * 32, NW <= 8 ? 2 : 1)
   if (pmode == Q1_SILU) {  // xf: gate, nw: up
     q1_silu_prep<NW>(xf, nw, nunit, (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
   } else if (pmode != Q1_PREPARED) {
-    oscale = q1_rms_prep<NW>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
-                             (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs);
+    if constexpr (TPSUM)
+      oscale = q1_rms_prep<NW, true>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
+                                     (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs, scr.ptp, scr.xout);
+    else
+      oscale = q1_rms_prep<NW, false>(xf, nwv, eps, nunit, (float*)(smem + Q1Cfg::red_off(NW, NS, nunit)),
+                                      (float*)(smem + Q1Cfg::part_off(NW, NS, nunit)), (uint8_t*)xs, scr.ptp,
+                                      scr.xout);
   } else if (rmode == 0) {
     if (threadIdx.x == 0) {
       mbar_arrive_expect_tx(bar_x, (uint32_t)(nunit * XB));
@@ -1380,17 +1424,21 @@ int launch_q1_nw(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float
   const int64_t nunit = w->nblk;
   const int64_t P = w->tiles * nunit / 2;
   // the fused RmsNorm holds K <= NW * 512 in registers, read 16 bytes at a time
-  if (pmode == Q1_RMSNORM && (nunit * 256 > NW * 128 * 4 || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
+  if ((pmode == Q1_RMSNORM || pmode == Q1_RMSNORM_TP) &&
+      (nunit * 256 > NW * 128 * 4 || (((uintptr_t)xf | (uintptr_t)nw) & 15)))
+    return -1;
   // the fused SiLU * up keeps at most 4 units per warp of 16 in registers
   if (pmode == Q1_SILU && (nunit > Q1_SILU_MAX_UNITS * NW / 16 || (((uintptr_t)xf | (uintptr_t)nw) & 15))) return -1;
   const size_t smem = Q1Cfg::smem(NW, NS, (int)nunit, pmode);
   if ((nunit & 1) || P < NW || smem > 227 * 1024 || w->tiles * nunit >= (1 << 24)) return -1;
-  static DeviceOnce attr_set;
+  static DeviceOnce attr_set, attr_set_tp;
   int dev = 0;
   SI_CUDA(cudaGetDevice(&dev));
-  if (!attr_set.done(dev)) {
-    SI_CUDA(cudaFuncSetAttribute(k_qmv1<EPI, NW, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    attr_set.mark(dev);
+  DeviceOnce& once = pmode == Q1_RMSNORM_TP ? attr_set_tp : attr_set;
+  if (!once.done(dev)) {
+    SI_CUDA(cudaFuncSetAttribute(pmode == Q1_RMSNORM_TP ? k_qmv1<EPI, NW, NS, true> : k_qmv1<EPI, NW, NS, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    once.mark(dev);
   }
   // Tile mode gives every CTA whole row tiles: no partial sums cross CTAs,
   // at the price of up to one tile of imbalance.  Even-share mode balances
@@ -1414,7 +1462,8 @@ int launch_q1_nw(cudaStream_t s, const si_weight* w, const uint8_t* xprep, float
   }
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(s, dim3((unsigned)grid), dim3(NW * 32), smem, pdl, attr);
-  SI_CUDA(cudaLaunchKernelEx(&cfg, k_qmv1<EPI, NW, NS>, (const uint8_t*)w->dev, (int)nunit, w->rows, (int)tiles,
+  SI_CUDA(cudaLaunchKernelEx(&cfg, pmode == Q1_RMSNORM_TP ? k_qmv1<EPI, NW, NS, true> : k_qmv1<EPI, NW, NS, false>,
+                             (const uint8_t*)w->dev, (int)nunit, w->rows, (int)tiles,
                              tile_mode, pmode, xprep, xf, nw, eps, y, q));
   return SI_OK;
 }
@@ -1497,6 +1546,19 @@ int launch_qmv_rms(cudaStream_t s, const si_weight* w, const float* x, const flo
   }
   SI_TRY(launch_prep(s, x, (int)w->cols, nullptr, nw, eps, SI_PREP_RMSNORM, (int)w->cols, 1, nullptr, xprep, pdl));
   return launch_qmv(s, w, xprep, 1, y, epi, qb, pdl);
+}
+
+// y = W RmsNorm(xres + sum over ranks of the partial sums) nw for one row
+// (tensor parallel, batch 1), with the new residual written to xout: inside
+// the batch-1 Q4_K kernel where it applies (returns -1 otherwise).
+int launch_qmv_rms_tp(cudaStream_t s, const si_weight* w, const float* xres, float* xout, const float* nw, float eps,
+                      float* y, const QmvBuffers& qb, const PrepTp& pt, bool pdl) {
+  if (w->qtype != SI_Q4_K || !pt.comm || !pt.epoch || pt.tp < 1 || pt.tp > SI_TP_MAX || ((uintptr_t)xout & 15))
+    return -1;
+  ScratchCap scr{QmvScratch{qb.split, qb.count, qb.err, 0, qb.tp, qb.pf, qb.ring_mode, qb.q1w}, qb.split_bytes, qb.count_n};
+  scr.scr.ptp = pt;
+  scr.scr.xout = xout;
+  return launch_q1<SI_EPI_STORE>(s, w, nullptr, y, scr, qb.sms, pdl, Q1_RMSNORM_TP, xres, nw, eps);
 }
 
 // y (op)= W (SiLU(gate) * up) for one row (batch 1): the batch-1 Q4_K kernel
