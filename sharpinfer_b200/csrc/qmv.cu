@@ -875,36 +875,54 @@ __device__ __forceinline__ float q1_rms_prep(const float* __restrict__ xf, const
   }
   if constexpr (TPSUM) {
     // residual + the ranks' partial sums in rank order, as SI_PREP_RMSNORM_TP
-    // adds them; each word awaited through its tag, four ranks' words of
-    // four elements in flight at a time
+    // adds them; each word awaited through its tag.  The words of all 16
+    // elements of two ranks are requested together (one round trip per two
+    // ranks: these system-scope loads are slow).
     const unsigned want = *tpp.epoch * (unsigned)tpp.nlayers2 + (unsigned)tpp.flag_add;
     const uint8_t* slot0 = tpp.comm + tpp.slots_off;
+    float a[4][4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-      const int i = 4 * tid + NW * 128 * j;
-      if (i >= K) continue;
-      float a[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w};
-      for (int r0 = 0; r0 < tpp.tp; r0 += 4) {
-        uint2 w[4][4];
+      a[j][0] = xv[j].x;
+      a[j][1] = xv[j].y;
+      a[j][2] = xv[j].z;
+      a[j][3] = xv[j].w;
+    }
+    for (int r0 = 0; r0 < tpp.tp; r0 += 2) {
+      uint2 w[2][4][4];
 #pragma unroll
-        for (int r = 0; r < 4; r++)
+      for (int r = 0; r < 2; r++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int i = 4 * tid + NW * 128 * j;
 #pragma unroll
           for (int e = 0; e < 4; e++)
-            w[r][e] = r0 + r < tpp.tp ? ld_tagged((const uint2*)(slot0 + (int64_t)(r0 + r) * tpp.src_stride) + i + e)
-                                      : make_uint2(0u, want);
+            w[r][j][e] = r0 + r < tpp.tp && i < K
+                             ? ld_tagged((const uint2*)(slot0 + (int64_t)(r0 + r) * tpp.src_stride) + i + e)
+                             : make_uint2(0u, want);
+        }
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
-          if (r0 + r >= tpp.tp) break;
-          const uint2* sl = (const uint2*)(slot0 + (int64_t)(r0 + r) * tpp.src_stride);
+      for (int r = 0; r < 2; r++) {
+        if (r0 + r >= tpp.tp) break;
+        const uint2* sl = (const uint2*)(slot0 + (int64_t)(r0 + r) * tpp.src_stride);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int i = 4 * tid + NW * 128 * j;
+          if (i >= K) continue;
 #pragma unroll
           for (int e = 0; e < 4; e++) {
-            const uint32_t bits = (int)(w[r][e].y - want) >= 0 ? w[r][e].x : wait_tagged(sl + i + e, want, tpp.err);
-            a[e] = __fadd_rn(a[e], __uint_as_float(bits));
+            const uint32_t bits =
+                (int)(w[r][j][e].y - want) >= 0 ? w[r][j][e].x : wait_tagged(sl + i + e, want, tpp.err);
+            a[j][e] = __fadd_rn(a[j][e], __uint_as_float(bits));
           }
         }
       }
-      xv[j] = make_float4(a[0], a[1], a[2], a[3]);
-      if (blockIdx.x == 0) *(float4*)(xout + i) = xv[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int i = 4 * tid + NW * 128 * j;
+      xv[j] = make_float4(a[j][0], a[j][1], a[j][2], a[j][3]);
+      if (blockIdx.x == 0 && i < K) *(float4*)(xout + i) = xv[j];
     }
   }
 #pragma unroll
