@@ -110,7 +110,7 @@ inline int64_t qmv_warp_grid(int64_t units, int nw, int sms) {
 // Scratch a streaming matvec over `tiles` row tiles of `nunit` units needs:
 // split floats and counter ints (an upper bound over the ring layouts).
 inline void qmv_scratch_need(int64_t tiles, int64_t nunit, int sms, size_t* split_bytes,
-                             int64_t* counts) {
+                             int64_t* counts, bool wide = true) {
   int64_t worst = 0;
   for (const int nw : {8, 16}) {  // k_qmv_warp: units split over grid x nw warps
     const int64_t units = tiles * nunit, grid = qmv_warp_grid(units, nw, sms);
@@ -125,8 +125,10 @@ inline void qmv_scratch_need(int64_t tiles, int64_t nunit, int sms, size_t* spli
     if (maxc > worst) worst = maxc;
   }
   *split_bytes = (size_t)tiles * worst * 64 * 4;
-  const size_t tc = (size_t)sms * 2 * 4096 * 4;  // k_qmv_wide: two row-block partials per CTA
-  if (*split_bytes < tc) *split_bytes = tc;
+  // k_qmv_wide: two row-block partials per CTA (a caller without room for
+  // them passes wide = false; k_qmv_wide then declines and another kernel runs)
+  const size_t tc = (size_t)sms * 2 * 4096 * 4;
+  if (wide && *split_bytes < tc) *split_bytes = tc;
   *counts = tiles;
 }
 }  // namespace si

@@ -87,7 +87,7 @@ int run(const si_weight* w, const float* x, float* y, int batch, cudaStream_t s,
   const int64_t nunit = w->qtype == SI_Q8_0 ? (w->nblk + 7) / 8 : w->nblk;
   size_t split_need;
   int64_t counts;
-  qmv_scratch_need(w->tiles, nunit, sc.sms, &split_need, &counts);
+  qmv_scratch_need(w->tiles, nunit, sc.sms, &split_need, &counts, false);
   if (split_off + split_need > kNoAllocScratchBytes || counts > (int64_t)kCountInts)
     SI_FAIL(SI_ERR_UNSUPPORTED, "si_qmatvec_noalloc: %lldx%lld at batch %d needs %zu bytes of scratch, %zu available",
             (long long)w->rows, (long long)w->cols, batch, split_off + split_need, kNoAllocScratchBytes);
