@@ -852,6 +852,15 @@ struct Q1Cfg {
 enum { Q1_PREPARED = 0, Q1_RMSNORM = 1, Q1_SILU = 2, Q1_RMSNORM_TP = 3 };
 constexpr int Q1_SILU_MAX_UNITS = 64;  // 4 units per warp of 16
 
+// ld_tagged without a compiler memory barrier, so the residual's loads and
+// these can be in flight together (the words are only read, and each is
+// single-copy atomic).
+__device__ __forceinline__ uint2 ld_tagged_free(const void* p) {
+  uint64_t w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p));
+  return make_uint2((uint32_t)w, (uint32_t)(w >> 32));
+}
+
 // Fused RmsNorm + activation preparation of a batch-1 k_qmv1 launch: every
 // CTA reads the whole input x (K <= NW * 512 columns, 4 x 16-byte loads per
 // thread; nwv holds this thread's norm weights, read before the dependency
@@ -898,7 +907,7 @@ __device__ __forceinline__ float q1_rms_prep(const float* __restrict__ xf, const
 #pragma unroll
           for (int e = 0; e < 4; e++)
             w[r][j][e] = r0 + r < tpp.tp && i < K
-                             ? ld_tagged((const uint2*)(slot0 + (int64_t)(r0 + r) * tpp.src_stride) + i + e)
+                             ? ld_tagged_free((const uint2*)(slot0 + (int64_t)(r0 + r) * tpp.src_stride) + i + e)
                              : make_uint2(0u, want);
         }
 #pragma unroll
