@@ -455,11 +455,15 @@ int check_config(const si_model_config* c) {
 }
 
 // Splits of the attention kernel for batch B: enough CTAs for two per SM,
-// and at most 1024 positions per split at the longest context.
+// and at most 1024 positions per split at the longest context -- 256 where
+// the split count allows it, so that a CTA's scores fit beside a second CTA
+// in shared memory (at batch 16 a 1024-position split leaves one 4-warp CTA
+// per SM and the KV stream at a third of HBM bandwidth).
 int attn_splits(const si_model* m, int B) {
   const int want = (2 * m->c->sm_count + B * m->cfg.n_kv_heads - 1) / (B * m->cfg.n_kv_heads);
   const int need = (m->cfg.max_seq + 1023) / 1024 + 1;  // the last split holds 16 positions
-  return std::min(std::max(want, need), m->splits_max);
+  const int fit = (m->cfg.max_seq + 255) / 256 + 1;
+  return std::min(std::max(std::max(want, need), std::min(fit, m->splits_max)), m->splits_max);
 }
 
 int enqueue_attention(si_model* m, int layer, const float* qkv, float* out, int B, bool pdl,

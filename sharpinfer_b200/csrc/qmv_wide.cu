@@ -497,11 +497,11 @@ int launch_wide_k(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int 
 template <int QT, int EPI>
 int launch_wide_q(cudaStream_t s, const si_weight* w, const uint8_t* xprep, int B, float* y, const WdScratch& scr,
                   int sms, bool pdl) {
-  static const int tsel = [] {  // tiles per compute warp: 0 = by batch size
+  static const int tsel = [] {  // tiles per compute warp: SHARPINFER_B200_QMV_WIDE_T=2 selects two
     const char* e = getenv("SHARPINFER_B200_QMV_WIDE_T");
     return e ? atoi(e) : 0;
   }();
-  const bool t2 = tsel ? tsel == 2 : B > 8;
+  const bool t2 = tsel == 2;  // one tile per warp measured faster at every batch
   if (B <= 8)
     return t2 ? launch_wide_k<QT, EPI, 2, 2>(s, w, xprep, B, y, scr, sms, pdl)
               : launch_wide_k<QT, EPI, 2, 1>(s, w, xprep, B, y, scr, sms, pdl);
