@@ -36,7 +36,7 @@ namespace {
 constexpr int HD = 128;
 constexpr int AT_WARPS = 4;
 constexpr int AT_SUB = 64;                 // positions per ring stage (4 blocks of 16)
-constexpr int AT_NS = 4;                   // ring stages
+constexpr int AT_NS = 4;                   // ring stages (2 at batch >= 4: a third CTA fits per SM)
 constexpr int AT_STAGE = AT_SUB * HD * 2;  // 16 KB
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& a0, uint32_t& a1, uint32_t& a2, uint32_t& a3) {
@@ -60,15 +60,15 @@ __device__ __forceinline__ uint32_t split2(float v0, float v1, int part) {
 }
 
 struct AttnSmem {
-  int G, cp;  // heads per kv head, positions per split rounded up to 64
-  __host__ __device__ size_t qs() const { return (size_t)AT_NS * AT_STAGE; }           // f32 [G][128]
+  int G, cp, ns;  // heads per kv head, positions per split rounded up to 64, ring stages
+  __host__ __device__ size_t qs() const { return (size_t)ns * AT_STAGE; }              // f32 [G][128]
   __host__ __device__ size_t qsc() const { return qs() + (size_t)G * HD * 4; }          // f32 [16]
   __host__ __device__ size_t sc() const { return qsc() + 64; }                          // f32 [G][cp]
   __host__ __device__ size_t pp() const { return sc() + (size_t)G * cp * 4; }           // f16 [2][G][cp]
   __host__ __device__ size_t ored() const { return pp() + (size_t)2 * G * cp * 2; }     // f32 [W][G][128]
   __host__ __device__ size_t stat() const { return ored() + (size_t)AT_WARPS * G * HD * 4; }  // f32 [G][2] + 2
   __host__ __device__ size_t bars() const { return (stat() + (2 * G + 2) * 4 + 7) & ~(size_t)7; }
-  __host__ __device__ size_t total() const { return bars() + AT_NS * 8; }
+  __host__ __device__ size_t total() const { return bars() + (size_t)ns * 8; }
 };
 
 // The last CTA of (sequence b, kv head kvh) to finish merges the S splits of
@@ -89,7 +89,7 @@ __device__ __forceinline__ void attn_merge_last(const AttnArgs& a, uint8_t* smem
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  static_assert(8 * SI_ATTN_MAX_SPLITS * 4 <= 16384 && 16640 + 8 * HD * 4 <= AT_NS * AT_STAGE, "merge scratch");
+  static_assert(8 * SI_ATTN_MAX_SPLITS * 4 <= 16384 && 16640 + 8 * HD * 4 <= 2 * AT_STAGE, "merge scratch");
   float* wts = (float*)smem;                        // [G][S] merge weights
   float* inv = (float*)(smem + 16384);              // [G] 1 / sum_s w_s l_s
   float* sv = (float*)(smem + 16640);               // [G][128] merged values (16-byte aligned)
@@ -144,14 +144,14 @@ __device__ __forceinline__ void attn_merge_last(const AttnArgs& a, uint8_t* smem
   if (tid == 0) *cnt = 0;
 }
 
-template <int G>
+template <int G, int NS>
 __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   constexpr int NT = (2 * G + 7) / 8;  // n-tiles of 8 (head, hi/lo) columns
   extern __shared__ __align__(128) uint8_t smem[];
   const int s_idx = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int S = gridDim.x, nkv = gridDim.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
-  const AttnSmem L{G, (a.chunk_max + 63) & ~63};
+  const AttnSmem L{G, (a.chunk_max + 63) & ~63, NS};
   const int cp = L.cp;
   uint8_t* ring = smem;
   float* qs = (float*)(smem + L.qs());
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   __half* kc = a.kcache + cache_off;
   __half* vc = a.vcache + cache_off;
   if (tid == 0) {
-    for (int i = 0; i < AT_NS; i++) mbar_init(bar0 + 8 * i, 1);
+    for (int i = 0; i < NS; i++) mbar_init(bar0 + 8 * i, 1);
     mbar_fence_init();
   }
   __syncthreads();
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   const int items = 2 * nsub;
   const uint64_t pol = l2_evict_first_policy();  // the cache is read once per step
   auto issue = [&](int it) {
-    const int st = it % AT_NS;
+    const int st = it % NS;
     const int sub = it < nsub ? it : it - nsub;
     const __half* base = it < nsub ? kc : vc;
     const int p0 = t0 + sub * AT_SUB;
@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
     bulk_g2s_ef(smem_u32(ring + st * AT_STAGE), base + (int64_t)p0 * HD, bytes, bar0 + 8 * st, pol);
   };
   if (tid == 0 && !appends)
-    for (int it = 0; it < min(items, AT_NS); it++) issue(it);
+    for (int it = 0; it < min(items, NS); it++) issue(it);
   l2_prefetch_share(a.pf);
   pdl_wait();
   const float* qkv = a.qkv + (int64_t)b * a.qkv_ld;
@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   }
   __syncthreads();
   if (tid == 0 && appends)
-    for (int it = 0; it < min(items, AT_NS); it++) issue(it);
+    for (int it = 0; it < min(items, NS); it++) issue(it);
 
   // per-head power-of-two scale of q: max |q 2^e| in [2^13, 2^14)
   for (int h = warp; h < G; h += AT_WARPS) {
@@ -269,16 +269,16 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
   bool ok = true;
   // After a wait gives up (agreed by the whole CTA at the stage's barrier)
   // nothing more is issued; thread 0 waits once, bounded, on each item still
-  // in flight -- items it .. it + AT_NS - 1 -- and the CTA skips the rest.
+  // in flight -- items it .. it + NS - 1 -- and the CTA skips the rest.
   auto drain = [&](int it) {
     if (tid == 0)
-      for (int j = it; j < min(items, it + AT_NS); j++) mbar_wait_bounded(bar0 + 8 * (j % AT_NS), (uint32_t)((j / AT_NS) & 1));
+      for (int j = it; j < min(items, it + NS); j++) mbar_wait_bounded(bar0 + 8 * (j % NS), (uint32_t)((j / NS) & 1));
   };
   const int p0 = 16 * warp;  // this warp's block in every stage
   // ---- pass 1: scores ----
   for (int it = 0; it < nsub; it++) {
-    const int st = it % AT_NS;
-    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / AT_NS) & 1)))) ok = false;
+    const int st = it % NS;
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / NS) & 1)))) ok = false;
     const int rb = it * AT_SUB;
     const int np = min(AT_SUB, n - rb);
     if (ok && p0 < np) {
@@ -310,7 +310,7 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
       drain(it);
       break;
     }
-    if (tid == 0 && it + AT_NS < items) issue(it + AT_NS);
+    if (tid == 0 && it + NS < items) issue(it + NS);
   }
   // ---- softmax statistics per head (TensorOps.Softmax: max, exp, sum) ----
   for (int h = warp; h < G && ok; h += AT_WARPS) {
@@ -344,8 +344,8 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
 #pragma unroll
     for (int mt = 0; mt < 8; mt++) o[nt][mt][0] = o[nt][mt][1] = o[nt][mt][2] = o[nt][mt][3] = 0.f;
   for (int it = nsub; it < items && ok; it++) {
-    const int st = it % AT_NS;
-    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / AT_NS) & 1)))) ok = false;
+    const int st = it % NS;
+    if (!__all_sync(0xFFFFFFFFu, mbar_wait_bounded(bar0 + 8 * st, (uint32_t)((it / NS) & 1)))) ok = false;
     const int rb = (it - nsub) * AT_SUB;
     const int np = min(AT_SUB, n - rb);
     uint8_t* vst = ring + st * AT_STAGE;
@@ -383,9 +383,9 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
       drain(it);
       break;
     }
-    if (tid == 0 && it + AT_NS < items) {
+    if (tid == 0 && it + NS < items) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // zeroed rows before the refill
-      issue(it + AT_NS);
+      issue(it + NS);
     }
   }
   // reduce the warps' partial outputs
@@ -419,13 +419,14 @@ __global__ void __launch_bounds__(AT_WARPS * 32) k_attn_decode(AttnArgs a) {
 
 }  // namespace
 
-size_t attn_smem_bytes(int G, int chunk_max) {
-  const AttnSmem L{G, (chunk_max + 63) & ~63};
+size_t attn_smem_bytes(int G, int chunk_max, int ns) {
+  const AttnSmem L{G, (chunk_max + 63) & ~63, ns};
   return L.total();
 }
 
 int launch_attn(cudaStream_t s, const AttnArgs& a, int G, int splits, int batch, int nkv, bool pdl) {
-  const size_t smem = attn_smem_bytes(G, a.chunk_max);
+  const int ns = batch >= 4 ? 2 : AT_NS;
+  const size_t smem = attn_smem_bytes(G, a.chunk_max, ns);
   if (smem > 227 * 1024) SI_FAIL(SI_ERR_UNSUPPORTED, "attention: %zu bytes of shared memory needed", smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(splits, nkv, batch);
@@ -440,9 +441,15 @@ int launch_attn(cudaStream_t s, const AttnArgs& a, int G, int splits, int batch,
   switch (G) {
 #define SI_ATTN_CASE(GG)                                                                      \
   case GG:                                                                                    \
-    SI_CUDA(cudaFuncSetAttribute(k_attn_decode<GG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                 (int)smem));                                                 \
-    SI_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<GG>, a));                                  \
+    if (ns == 2) {                                                                            \
+      SI_CUDA(cudaFuncSetAttribute(k_attn_decode<GG, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   (int)smem));                                               \
+      SI_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<GG, 2>, a));                             \
+    } else {                                                                                  \
+      SI_CUDA(cudaFuncSetAttribute(k_attn_decode<GG, AT_NS>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                   (int)smem));                                               \
+      SI_CUDA(cudaLaunchKernelEx(&cfg, k_attn_decode<GG, AT_NS>, a));                         \
+    }                                                                                         \
     return SI_OK;
     SI_ATTN_CASE(1)
     SI_ATTN_CASE(2)

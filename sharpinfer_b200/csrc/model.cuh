@@ -54,7 +54,7 @@ int launch_cache_dense(cudaStream_t s, const __half* cache, int max_seq, int len
 int launch_heads_rows(cudaStream_t s, const float* o, int n, int nh, __half* y, float* rs);
 int launch_silu_rows(cudaStream_t s, const float* gu, int n, int inter, __half* y, float* rs);
 
-size_t attn_smem_bytes(int G, int chunk_max);
+size_t attn_smem_bytes(int G, int chunk_max, int ns);
 int launch_attn(cudaStream_t s, const AttnArgs& a, int G, int splits, int batch, int nkv, bool pdl);
 
 }  // namespace si
